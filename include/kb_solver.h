@@ -1,0 +1,168 @@
+/*
+ * kb_solver.h -- C ABI of the kernel-bench B200 solver kernels (libkb_solver.so, sm_100a).
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream handle (cudaStream_t
+ * passed as void*), enqueues its work on that stream and returns an int status:
+ *   KB_OK (0), KB_ERR_ARG (1: invalid size/argument), KB_ERR_LAUNCH (2: CUDA launch failure),
+ *   KB_ERR_SIZE (3: S above KB_MAX_S or an unsupported shape).
+ * Nothing here allocates device memory; callers own every buffer.  Conventions:
+ *   - float tensors are fp32, row-major, contiguous; a "[C,S]" array has row stride S;
+ *   - node_* / leaf_state arrays are int32; row/split index arrays are int64;
+ *   - boolean masks are uint8 (0/1);
+ *   - jumps: [K,S] int32 pointer-doubling table, jumps[r*S+s] = 2^r-th ancestor of s or -1,
+ *     K = ceil(log2(max_ancestor_depth)) (kb_build_jumps builds it);
+ *   - compact levels: internal species nodes grouped by depth, deepest level first
+ *     (lv_ptr int64 [n_levels+1], lv_par/lv_c1/lv_c2 int32).
+ * References are to the reference project (SisyphusMountain/kernel-bench), file:line.
+ */
+#ifndef KB_SOLVER_H
+#define KB_SOLVER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KB_MAX_S 8192
+
+/* Version of this ABI (bumped on any signature change). */
+int kb_abi_version(void);
+
+/* Build the pointer-doubling ancestor table from node_parent on the device.
+ * No reference counterpart (the reference caches an equivalent table on the host,
+ * kbench/core/kernels/wave_step.py:35-55 _get_jumps). */
+int kb_build_jumps(const int* node_parent, int S, int K, int* jumps, void* stream);
+
+/* ---- E-step (kbench/core/kernels/e_step.py) ------------------------------------------- */
+
+/* Replaces e_fixed_point_triton (e_step.py:438-501): iterate E <- F(E) on the device until
+ * max|dE| < tol or max_iter iterations, then one more application for E_s1/E_s2/Ebar.
+ * E_tmp is a [G,S] ping-pong buffer; *iters_out (device int) receives the iteration count. */
+int kb_e_fixed_point(const float* E0, float* E_out, float* E_tmp, float* E_s1, float* E_s2, float* Ebar,
+                     const float* log_pS, const float* log_pD, const float* log_pL, const float* max_coupling,
+                     const float* col_log_probs, const int* node_parent, const int* node_child1,
+                     const int* node_child2, const int* jumps, int K, int S, int G, int max_iter, double tol,
+                     int use_col_weights, int* iters_out, void* stream);
+
+/* Replaces _launch_e_step_forward_2d (e_step.py:244-287): one E application per item row;
+ * max_diff_out [G] may be NULL. */
+int kb_e_step_forward(const float* E, float* E_new, float* E_s1, float* E_s2, float* Ebar, float* max_diff_out,
+                      const float* log_pS, const float* log_pD, const float* log_pL, const float* max_coupling,
+                      const float* col_log_probs, const int* node_parent, const int* node_child1,
+                      const int* node_child2, const int* jumps, int K, int S, int G, int use_col_weights,
+                      void* stream);
+
+/* Replaces _TritonEStep2D.backward (e_step.py:325-409; kernels :102-241): VJP of one E
+ * application. g_* may be NULL (zero cotangent). grad_col [S] is overwritten (sum over rows). */
+int kb_e_step_vjp(const float* E, const float* E_new, const float* E_s1, const float* E_s2, const float* Ebar,
+                  const float* log_pS, const float* log_pD, const float* log_pL, const float* col_log_probs,
+                  const int* node_parent, const int* node_child1, const int* node_child2, const int* jumps, int K,
+                  const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1, const int* lv_c2,
+                  const float* g_new, const float* g_s1, const float* g_s2, const float* g_ebar, float* grad_E,
+                  float* grad_pS, float* grad_pD, float* grad_pL, float* grad_mc, float* grad_col, int S, int G,
+                  int use_col_weights, void* stream);
+
+/* ---- split reduction (kbench/core/kernels/dts_fused.py) ------------------------------- */
+
+/* Replaces compute_dts_forward (dts_fused.py:171-231). out [W,S] must be pre-filled with -inf
+ * (rows of inactive or split-less parents are not written). log_pD/log_pS are [rows,S] with row
+ * stride param_row_stride (0: one shared row), row = item_idx[item_offset + parent].
+ * out_row (may be NULL) remaps a parent's output row. */
+int kb_dts_forward(const float* Pi, const float* Pibar, const long long* sl, const long long* sr,
+                   const int* node_child1, const int* node_child2, const float* log_pD, const float* log_pS,
+                   long long param_row_stride, const long long* item_idx, long long item_offset,
+                   const float* log_split_probs, const long long* eq1_reduce_idx, int n_eq1,
+                   const long long* ge2_ptr, const long long* ge2_parent_ids, int n_ge2,
+                   const unsigned char* active_rows, float* out, const long long* out_row, int S, void* stream);
+
+/* ---- forward wave (kbench/core/kernels/wave_step.py) ---------------------------------- */
+
+/* Replaces compute_wave_step (wave_step.py:1128-1268): one Jacobi sweep of rows [ws, ws+W).
+ * Reads pi_in rows [pi_ws, pi_ws+W), writes pi_out_rows[0..W); with store_final also writes the
+ * final Pibar rows pibar[ws..ws+W) and pibar_row_max. residual [C] and dts [W,S] may be NULL.
+ * Aliasing of pi_in/pi_out/pibar rows as done by kbench/core/inference/forward.py is allowed. */
+int kb_wave_step(const float* pi_in, long long pi_ws, float* pi_out_rows, float* pibar, float* pibar_row_max,
+                 float* residual, const float* dts, const float* mc, const float* dl, const float* ebar,
+                 const float* e, const float* sl1, const float* sl2, long long const_row_stride,
+                 const float* col_log_probs, int use_col_weights, const int* node_child1, const int* node_child2,
+                 const int* jumps, int K, const int* leaf_state, const float* leaf_logp, const long long* item_idx,
+                 int use_leaf, int store_final, int ws, int W, int S, void* stream);
+
+/* Replaces compute_leaf_initial_wave_step (wave_step.py:1078-1126). */
+int kb_leaf_initial(float* pi_out_rows, const float* mc, const float* dl, const float* ebar, const float* e,
+                    const float* sl1, const float* sl2, long long const_row_stride, const float* col_log_probs,
+                    int use_col_weights, const int* node_child1, const int* node_child2,
+                    const int* node_subtree_start, const int* node_subtree_end, const int* leaf_state,
+                    const float* leaf_logp, const long long* item_idx, int ws, int W, int S, void* stream);
+
+/* Fused wave sweep: all pi_iters iterations of each listed row in one launch (leaf rows are
+ * seeded as compute_leaf_initial_wave_step does; other rows start from their dts row).  Writes
+ * the final Pi, Pibar rows and pibar_row_max -- the buffer state kbench/core/inference/
+ * forward.py:60-115 leaves after the wave.  dts is [n_rows,S] aligned with rows. */
+int kb_wave_sweep(const int* rows, int n_rows, const float* dts, float* pi, float* pibar, float* pibar_row_max,
+                  float* residual, const float* mc, const float* dl, const float* ebar, const float* e,
+                  const float* sl1, const float* sl2, long long const_row_stride, const float* col_log_probs,
+                  int use_col_weights, const int* node_child1, const int* node_child2,
+                  const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
+                  const int* leaf_state, const float* leaf_logp, const long long* item_idx, int pi_iters, int S,
+                  void* stream);
+
+/* ---- backward (kbench/core/kernels/wave_backward.py) ---------------------------------- */
+
+/* Replaces active_mask_from_rhs_absmax_fused (wave_backward.py:247-280). */
+int kb_active_mask(const float* rhs, long long row_stride, int W, int S, float threshold, int strict_gt,
+                   unsigned char* out, void* stream);
+
+/* Replaces wave_backward_uniform_fused (wave_backward.py:1737-1867, Neumann solver):
+ * per active row, v = sum_{n<=neumann_terms} (J^T)^n rhs and the parameter buckets aw0..aw4,
+ * aw345 ([W,S] each; zero on inactive rows; v_k rows of inactive rows untouched).
+ * const_mode: 0 shared [S] constants, 1 row-expanded [W,S], 2 item rows [G,S] via item_idx.
+ * leaf_mode: 0 [S], 1 [G], 2 [G,S], 3 scalar. grad_col (may be NULL) is accumulated. */
+int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
+                    const float* rhs, long long rhs_row_stride, const unsigned char* active, const float* dl,
+                    const float* ebar, const float* e, const float* sl1, const float* sl2, int const_mode,
+                    const float* col_log_probs, int use_col_weights, const int* node_child1,
+                    const int* node_child2, const int* node_parent, const int* jumps, int K,
+                    const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1, const int* lv_c2,
+                    int use_leaf_index, const int* leaf_state, const float* leaf_logp, int leaf_mode,
+                    const float* leaf_term, const long long* item_idx, int neumann_terms, float* grad_col,
+                    float* v_k, float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4, int ws,
+                    int W, int S, void* stream);
+
+/* Replaces dts_cross_backward_accum_fused (wave_backward.py:2319-2535): per split, the Pi
+ * cotangents of both children (including the merged speciation terms) are added into
+ * accumulated_rhs; the staged Pibar u_d rows / sums / side flags (output_ud) or grad_Pibar_l/r
+ * rows are written; parameter cotangents are accumulated (accum_param/accum_mt) or written per
+ * split.  Parameter/gradient addressing: value at base + item*row_stride + s*elem_stride. */
+int kb_dts_adjoint(const float* Pi, const float* Pibar, const float* v_k, const unsigned char* active,
+                   const long long* sl, const long long* sr, const long long* reduce_idx, const float* wlsp,
+                   const float* log_pD, long long pD_row_stride, int pD_elem_stride, const float* log_pS,
+                   long long pS_row_stride, int pS_elem_stride, const long long* item_idx, const int* node_child1,
+                   const int* node_child2, float* accumulated_rhs, int output_ud, float* pibar_ud, float* pibar_A,
+                   unsigned char* side_active, float side_threshold, int side_threshold_enabled,
+                   int skip_inactive_zero, float* grad_Pibar_l, float* grad_Pibar_r, int accum_param,
+                   float* grad_log_pD, float* grad_log_pS, long long gp_row_stride, int gp_elem_stride,
+                   float* param_pD, float* param_pS, int accum_mt, float* grad_mt, long long gmt_row_stride,
+                   int gmt_elem_stride, const float* mt, long long mt_row_stride, int mt_elem_stride,
+                   const float* pibar_row_max, int ws, int N, int S, void* stream);
+
+/* Replaces _pibar_ud_side_active_kernel (wave_backward.py:2536-2567). */
+int kb_side_active(const float* pibar_ud, int rows, int S, float threshold, int threshold_enabled,
+                   unsigned char* out, void* stream);
+
+/* Replaces uniform_cross_pibar_vjp_tree_from_ud_fused (wave_backward.py:2748-2896): per active
+ * split side, in-place subtree sums of pibar_ud, then p'(A - subtree) into the child's adjoint
+ * row and grad_col (may be NULL). */
+int kb_pibar_vjp_tree(const float* Pi, const float* col_log_probs, int use_col_weights, float* pibar_ud,
+                      const float* pibar_A, const unsigned char* side_active, const long long* sl,
+                      const long long* sr, const long long* reduce_idx, const unsigned char* active,
+                      const float* pibar_row_max, const long long* lv_ptr, int n_levels, const int* lv_par,
+                      const int* lv_c1, const int* lv_c2, float* accumulated_rhs, float* grad_col, int N, int S,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KB_SOLVER_H */

@@ -1,0 +1,123 @@
+"""E-step wrappers (reference: ``kbench/core/kernels/e_step.py``).
+
+The names ``e_fixed_point_triton``, ``e_step_triton_autograd`` and ``_TritonEStep2D`` are the
+reference's (kept so callers bind unchanged); the work runs in the sm_100a kernels of
+``csrc/kb_estep.cu`` -- there is no Triton here.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib, tree
+from ._common import f32, i32, require_cuda_f32, rows_of
+
+
+def _as_item_state(t, S, G):
+    return rows_of(t, G, S)
+
+
+def _launch_e_step_forward_2d(E, log_pS_mat, log_pD_mat, log_pL_mat, max_coupling_mat, col_log_probs,
+                              node_parent, node_child1, node_child2, max_ancestor_depth, *,
+                              max_diff_out=None, out=None, use_col_weights=True):
+    """One E application per item row (reference ``e_step.py:244-287``)."""
+    require_cuda_f32("_launch_e_step_forward_2d", E)
+    G, S = int(E.shape[0]), int(E.shape[1])
+    E = f32(E)
+    E_new, E_s1, E_s2, Ebar = (torch.empty_like(E) for _ in range(4)) if out is None else out
+    tt = tree.tables(node_parent, node_child1, node_child2, max_ancestor_depth)
+    pS, pD, pL, mc = (rows_of(t, G, S) for t in (log_pS_mat, log_pD_mat, log_pL_mat, max_coupling_mat))
+    col = f32(col_log_probs.reshape(-1))
+    _lib.call("kb_e_step_forward", E.data_ptr(), E_new.data_ptr(), E_s1.data_ptr(), E_s2.data_ptr(),
+              Ebar.data_ptr(), _lib.ptr(max_diff_out), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(),
+              mc.data_ptr(), col.data_ptr(), tt.parent.data_ptr(), tt.child1.data_ptr(),
+              tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K, S, G, int(bool(use_col_weights)),
+              _lib.stream_handle(E.device))
+    return E_new, E_s1, E_s2, Ebar
+
+
+class _TritonEStep2D(torch.autograd.Function):
+    """Differentiable E application (reference ``e_step.py:290-409``); backward = one fused VJP
+    kernel (``kb_e_step_vjp``)."""
+
+    @staticmethod
+    def forward(E, log_pS_mat, log_pD_mat, log_pL_mat, max_coupling_mat, col_log_probs, node_parent,
+                node_child1, node_child2, max_ancestor_depth, use_col_weights):
+        return _launch_e_step_forward_2d(E, log_pS_mat, log_pD_mat, log_pL_mat, max_coupling_mat,
+                                         col_log_probs, node_parent, node_child1, node_child2,
+                                         int(max_ancestor_depth), use_col_weights=bool(use_col_weights))
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.save_for_backward(inputs[0], *output, *inputs[1:4], inputs[5], *inputs[6:9])
+        ctx.max_ancestor_depth = int(inputs[9])
+        ctx.use_col_weights = bool(inputs[10])
+
+    @staticmethod
+    def backward(ctx, grad_E_new, grad_E_s1_out, grad_E_s2_out, grad_Ebar_out):
+        (E, E_new, E_s1, E_s2, Ebar, log_pS_mat, log_pD_mat, log_pL_mat, col_log_probs, node_parent,
+         node_child1, node_child2) = ctx.saved_tensors
+        G, S = int(E.shape[0]), int(E.shape[1])
+        tt = tree.tables(node_parent, node_child1, node_child2, ctx.max_ancestor_depth)
+        gs = [None if g is None else f32(g) for g in (grad_E_new, grad_E_s1_out, grad_E_s2_out, grad_Ebar_out)]
+        grad_E, grad_pS, grad_pD, grad_pL, grad_mc = (torch.empty_like(E) for _ in range(5))
+        grad_col = torch.empty_like(col_log_probs)
+        pS, pD, pL = (rows_of(t, G, S) for t in (log_pS_mat, log_pD_mat, log_pL_mat))
+        _lib.call("kb_e_step_vjp", E.data_ptr(), E_new.data_ptr(), E_s1.data_ptr(), E_s2.data_ptr(),
+                  Ebar.data_ptr(), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(),
+                  f32(col_log_probs).data_ptr(), tt.parent.data_ptr(), tt.child1.data_ptr(),
+                  tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K, tt.lv_ptr.data_ptr(), tt.n_levels,
+                  tt.lv_par.data_ptr(), tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(),
+                  *[_lib.ptr(g) for g in gs], grad_E.data_ptr(), grad_pS.data_ptr(), grad_pD.data_ptr(),
+                  grad_pL.data_ptr(), grad_mc.data_ptr(), grad_col.data_ptr(), S, G,
+                  int(ctx.use_col_weights), _lib.stream_handle(E.device))
+        return (grad_E, grad_pS, grad_pD, grad_pL, grad_mc, grad_col, None, None, None, None, None)
+
+
+def e_step_triton_autograd(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
+                           node_child2, max_ancestor_depth, use_col_weights=True):
+    """Reference ``e_step.py:412-435``."""
+    E_arg = E.contiguous()
+    G, S = int(E_arg.shape[0]), int(E_arg.shape[1])
+    return _TritonEStep2D.apply(
+        E_arg, *(_as_item_state_ad(p, S, G) for p in (log_pS, log_pD, log_pL, max_coupling)),
+        col_log_probs.contiguous(), node_parent, node_child1, node_child2, int(max_ancestor_depth),
+        bool(use_col_weights))
+
+
+def _as_item_state_ad(t, S, G):
+    """Differentiable [G,S] view of a parameter (autograd flows back through reshape/expand)."""
+    if t.ndim == 2 and tuple(t.shape) == (G, S):
+        return t.contiguous()
+    if t.numel() == S:
+        return t.reshape(1, S).expand(G, S).contiguous()
+    if t.numel() == G:
+        return t.reshape(G, 1).expand(G, S).contiguous()
+    return t.reshape(1, 1).expand(G, S).contiguous()
+
+
+def e_fixed_point_triton(E0, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
+                         node_child2, max_ancestor_depth, *, max_iter=2000, tol=1e-8, use_col_weights=True):
+    """E fixed point (reference ``e_step.py:438-501``), iterated in one persistent CTA on the
+    device (no per-iteration host synchronisation).  Returns (E, E_s1, E_s2, Ebar)."""
+    max_iter = int(max_iter)
+    tol = float(tol)
+    if max_iter < 1:
+        raise ValueError("max_iter must be at least 1")
+    if tol <= 0.0:
+        raise ValueError("tol must be positive")
+    require_cuda_f32("e_fixed_point_triton", E0)
+    E0 = f32(E0)
+    G, S = int(E0.shape[0]), int(E0.shape[1])
+    tt = tree.tables(node_parent, node_child1, node_child2, max_ancestor_depth)
+    pS, pD, pL, mc = (rows_of(t, G, S) for t in (log_pS, log_pD, log_pL, max_coupling))
+    col = f32(col_log_probs.reshape(-1))
+    E_out, E_tmp, E_s1, E_s2, Ebar = (torch.empty_like(E0) for _ in range(5))
+    iters = torch.zeros((1,), dtype=torch.int32, device=E0.device)
+    _lib.call("kb_e_fixed_point", E0.data_ptr(), E_out.data_ptr(), E_tmp.data_ptr(), E_s1.data_ptr(),
+              E_s2.data_ptr(), Ebar.data_ptr(), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(), mc.data_ptr(),
+              col.data_ptr(), tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
+              tt.jumps.data_ptr(), tt.K, S, G, max_iter, tol, int(bool(use_col_weights)), iters.data_ptr(),
+              _lib.stream_handle(E0.device))
+    e_fixed_point_triton.last_iters = iters
+    return E_out, E_s1, E_s2, Ebar

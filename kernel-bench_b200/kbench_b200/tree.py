@@ -1,0 +1,116 @@
+"""Device-side species-tree tables shared by the kernels.
+
+``tables(node_parent, ...)`` returns (and caches, keyed by the ``node_parent`` storage like the
+reference's own host caches, ``kbench/core/kernels/wave_step.py:35-55``) the pointer-doubling
+ancestor table used for the ancestor-or-self path sums and int32/int64 copies of the compact
+level arrays used for bottom-up subtree sums.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+@dataclass
+class TreeTables:
+    S: int
+    K: int
+    jumps: torch.Tensor          # [max(K,1), S] int32
+    parent: torch.Tensor         # [S] int32
+    child1: torch.Tensor         # [S] int32
+    child2: torch.Tensor         # [S] int32
+    lv_ptr: torch.Tensor | None  # [L+1] int64
+    lv_par: torch.Tensor | None
+    lv_c1: torch.Tensor | None
+    lv_c2: torch.Tensor | None
+    n_levels: int
+
+
+_CACHE: dict = {}
+
+
+def rounds_for_depth(max_ancestor_depth: int) -> int:
+    """Doubling rounds so that 2^K >= the longest root path (nodes, counting self)."""
+    d = max(1, int(max_ancestor_depth))
+    return 0 if d <= 1 else int(math.ceil(math.log2(d)))
+
+
+def _i32(t, device):
+    return t.to(device=device, dtype=torch.int32).contiguous()
+
+
+def tables(node_parent, node_child1, node_child2, max_ancestor_depth, *, compact_level_ptr=None,
+           compact_level_parents=None, compact_level_child1=None, compact_level_child2=None) -> TreeTables:
+    device = node_parent.device
+    S = int(node_parent.numel())
+    key = (node_parent.data_ptr(), node_child1.data_ptr(), S, int(max_ancestor_depth),
+           None if compact_level_ptr is None else compact_level_ptr.data_ptr(), device.index)
+    hit = _CACHE.get(key)
+    if hit is not None:
+        return hit
+    parent = _i32(node_parent, device)
+    c1 = _i32(node_child1, device)
+    c2 = _i32(node_child2, device)
+    K = rounds_for_depth(max_ancestor_depth)
+    jumps = torch.empty((max(K, 1), S), dtype=torch.int32, device=device)
+    if K:
+        _lib.call("kb_build_jumps", parent.data_ptr(), S, K, jumps.data_ptr(), _lib.stream_handle(device))
+    if compact_level_ptr is None:
+        compact_level_ptr, compact_level_parents, compact_level_child1, compact_level_child2 = \
+            derive_levels(node_parent, node_child1, node_child2)
+    if compact_level_ptr is not None:
+        lv_ptr = compact_level_ptr.to(device=device, dtype=torch.int64).contiguous()
+        lv_par = _i32(compact_level_parents, device)
+        lv_c1 = _i32(compact_level_child1, device)
+        lv_c2 = _i32(compact_level_child2, device)
+        n_levels = int(lv_ptr.numel()) - 1
+    else:
+        lv_ptr = lv_par = lv_c1 = lv_c2 = None
+        n_levels = 0
+    tt = TreeTables(S, K, jumps, parent, c1, c2, lv_ptr, lv_par, lv_c1, lv_c2, n_levels)
+    # keep the source tensors alive with the entry so their addresses are not reused
+    _CACHE[key] = tt
+    tt._keep = (node_parent, node_child1, node_child2, compact_level_ptr)  # type: ignore[attr-defined]
+    return tt
+
+
+def derive_levels(node_parent, node_child1, node_child2):
+    """Compact levels (internal nodes grouped by depth, deepest level first) from the parent
+    and child arrays, for callers that did not pass the precomputed ones."""
+    par = node_parent.detach().to("cpu", torch.int64)
+    c1 = node_child1.detach().to("cpu", torch.int64)
+    c2 = node_child2.detach().to("cpu", torch.int64)
+    S = int(par.numel())
+    depth = [0] * S
+    # depth by walking up (trees here are shallow); memoised
+    for s in range(S):
+        d, cur = 0, int(par[s])
+        while 0 <= cur < S:
+            d += 1
+            cur = int(par[cur])
+        depth[s] = d
+    internal = [s for s in range(S) if 0 <= int(c1[s]) < S]
+    levels = sorted({depth[s] for s in internal}, reverse=True)
+    ptr, lp, l1, l2 = [0], [], [], []
+    for d in levels:
+        nodes = [s for s in internal if depth[s] == d]
+        lp += nodes
+        l1 += [int(c1[s]) for s in nodes]
+        l2 += [int(c2[s]) for s in nodes]
+        ptr.append(len(lp))
+    dev = node_parent.device
+    return (torch.tensor(ptr, dtype=torch.int64, device=dev), torch.tensor(lp, dtype=torch.int32, device=dev),
+            torch.tensor(l1, dtype=torch.int32, device=dev), torch.tensor(l2, dtype=torch.int32, device=dev))
+
+
+def from_helpers(sh: dict) -> TreeTables:
+    return tables(sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]),
+                  compact_level_ptr=sh.get("compact_level_ptr"),
+                  compact_level_parents=sh.get("compact_level_parents"),
+                  compact_level_child1=sh.get("compact_level_child1"),
+                  compact_level_child2=sh.get("compact_level_child2"))

@@ -1,0 +1,51 @@
+"""Shared helpers for the tests (loading golden fixtures, tolerance checks)."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+# Tolerances stated by the benchmark: loss to rel 1e-5; gradients and intermediates to
+# rel 1e-4 / abs 1e-6, applied per element as |got - ref| <= atol + rtol * |ref|, with
+# matching -inf patterns.
+LOSS_RTOL = 1e-5
+RTOL = 1e-4
+ATOL = 1e-6
+
+
+def golden_names():
+    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+
+
+def load_golden(name):
+    from kbench_b200.problem_io import unflatten_case
+    return unflatten_case(np.load(GOLDEN / f"{name}.npz"))
+
+
+def oracle_static(captured):
+    st = dict(captured["static"])
+    st["solver_options"] = captured["meta"]["solver_options"]
+    return st
+
+
+def assert_close(name, got, ref, rtol=RTOL, atol=ATOL):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64).reshape(got.shape)
+    ninf_g, ninf_r = np.isneginf(got), np.isneginf(ref)
+    assert np.array_equal(ninf_g, ninf_r), f"{name}: -inf pattern differs ({int((ninf_g != ninf_r).sum())} elems)"
+    assert not np.isnan(got).any(), f"{name}: NaN in result"
+    fin = ~ninf_r
+    d = np.abs(got[fin] - ref[fin])
+    tol = atol + rtol * np.abs(ref[fin])
+    bad = d > tol
+    if bad.any():
+        i = int(np.argmax(d / tol))
+        raise AssertionError(f"{name}: {int(bad.sum())} elements out of tolerance; worst |d|={d[i]:.3e} "
+                             f"ref={ref[fin][i]:.6e} (tol {tol[i]:.3e})")
+
+
+def assert_loss(got, ref, rtol=LOSS_RTOL):
+    assert abs(float(got) - float(ref)) <= rtol * abs(float(ref)), f"loss {got} vs {ref}"
