@@ -161,6 +161,58 @@ int kb_pibar_vjp_tree(const float* Pi, const float* col_log_probs, int use_col_w
                       const int* lv_c1, const int* lv_c2, float* accumulated_rhs, float* grad_col, int N, int S,
                       void* stream);
 
+/* ---- fused level engine (no reference counterpart: B200 schedule of the same math) ------- */
+
+/* Linear-space per-column constants of the wave update for [G,S] item rows (n = G*S):
+ * linA = 2^dl + 2^ebar, linB = 2^(mc+e), linC1 = 2^sl1, linC2 = 2^sl2. */
+int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const float* e, const float* sl1,
+                  const float* sl2, int n, float* linA, float* linB, float* linC1, float* linC2, void* stream);
+
+/* Forward of one dependency level (replaces, for the rows listed, compute_dts_forward +
+ * compute_leaf_initial_wave_step + pi_iters x compute_wave_step of kbench/core/inference/
+ * forward.py:60-115): per row (one CTA) the split reduction over its splits
+ * [split_ptr[b], split_ptr[b+1]) of (sl, sr, lsp) -- or the leaf seed for split-less leaf rows --
+ * then all pi_iters iterations on chip; writes the final pi, pibar rows, pibar_row_max, the split
+ * reduction (dts_save, may be NULL) and the last-iteration residual (may be NULL).
+ * fallback_count (device int, may be NULL) counts rows recomputed in log space. */
+int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
+                     const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src, float* pi,
+                     float* pibar, float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
+                     const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
+                     const float* sl2, const float* leaf_logp, const float* linA, const float* linB,
+                     const float* linC1, const float* linC2, const float* log_pD, const float* log_pS,
+                     long long param_row_stride, long long const_row_stride, const float* col_log_probs,
+                     int use_col_weights, const int* node_parent, const int* node_child1, const int* node_child2,
+                     const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
+                     const long long* item_idx, const int* leaf_state, int pi_iters, int S, void* stream);
+
+/* Backward of one dependency level (replaces, for the rows listed, active_mask_from_rhs_absmax_
+ * fused + compute_dts_forward + wave_backward_uniform_fused + dts_cross_backward_accum_fused +
+ * uniform_cross_pibar_vjp_tree_from_ud_fused as driven by kbench/api/_implicit_grad.py:
+ * 190-353): per active row the Neumann adjoint, its parameter and column cotangents into
+ * grad_acc ([10,S] fp64: aw0..aw5 sums, split pD/pS/mt sums, column gradient), and every split's
+ * child cotangents added into accumulated_rhs. dts_saved may be NULL (recomputed); v_out [C,S]
+ * (may be NULL) receives the solved adjoint row of every active row. */
+int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
+                      const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
+                      const float* pibar_row_max, const float* dts_saved, float* accumulated_rhs, float* v_out,
+                      double* grad_acc,
+                      float threshold, int strict_gt, float side_threshold, int side_threshold_enabled,
+                      int neumann_terms, const float* mc, const float* dl, const float* ebar, const float* e,
+                      const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
+                      const float* log_pS, long long param_row_stride, long long const_row_stride,
+                      const float* col_log_probs, int use_col_weights, const int* node_parent,
+                      const int* node_child1, const int* node_child2, const int* node_pre, const int* node_pre_end,
+                      const int* jumps, int K, const long long* item_idx, const int* leaf_state, int S,
+                      void* stream);
+
+/* Gradient accumulators of kb_level_backward -> the eight fp32 [S] cotangent vectors of the
+ * backward glue (grad_log_pD, grad_log_pS, grad_mt, grad_E, grad_Ebar, grad_E_s1, grad_E_s2,
+ * grad_col_log_probs). */
+int kb_finalize_grads(const double* grad_acc, int S, float* grad_log_pD, float* grad_log_pS, float* grad_mt,
+                      float* grad_E, float* grad_Ebar, float* grad_E_s1, float* grad_E_s2, float* grad_col,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,11 +1,227 @@
-"""Placeholder until the fused engine lands: delegates to the reference-structured driver."""
+"""The fused B200 engine (default driver of ``runtime.run_forward`` / ``run_backward``).
 
-from . import glue
+Schedule.  The reference processes rows in "waves" of equal clade size, smallest first, and calls
+``pi_iters`` wave-step launches per wave plus a split-reduction launch (``kbench/core/inference/
+forward.py:60-115``).  A row only depends on the final Pi/Pibar of its split children, so any
+topological banding gives bit-identical per-row arithmetic.  The engine re-bands the rows into
+dependency levels (level 0: leaf rows; otherwise 1 + the deepest child level) once per problem:
+at the large config that is 186 levels instead of 1,666 size-waves, and each level is ONE launch
+(``kb_level_forward``) that does the split reduction and all iterations of every row of the level.
+The backward runs the levels in reverse with one launch each (``kb_level_backward``).
+
+The engine supports the layouts of every benchmark config (one shared item row: ``statewise`` and
+not ``itemwise``); anything else is routed to the reference-structured driver of ``glue.py``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib, glue, tree
+from .kernels._common import f32, i32, i64
 
 
-def forward(static, theta, col_weights):
-    return glue.solve_e_pi(static, theta, col_weights)
+@dataclass
+class LevelPlan:
+    n_levels: int
+    level_ptr: list            # row offsets of each level in ``rows`` (host ints)
+    rows: torch.Tensor         # int32 [C] rows in level order
+    split_ptr: torch.Tensor    # int64 [C+1] CSR of each listed row's splits
+    sl: torch.Tensor           # int64 [N]
+    sr: torch.Tensor
+    lsp: torch.Tensor          # f32 [N]
+    level_of: np.ndarray       # level of every row (host)
+    children_per_level: list   # distinct child rows referenced per level (for the traffic model)
+    n_splits: int
 
 
-def backward(static, theta, col_weights, saved):
-    return glue.implicit_grad(static, theta, col_weights, saved)
+def build_plan(static) -> LevelPlan:
+    """Dependency levels and the per-row split CSR, from the reference wave layout."""
+    cached = getattr(static, "_plan", None)
+    if cached is not None:
+        return cached
+    wl = static.wave_layout
+    dev = wl["leaf_state_index"].device
+    C = int(wl["leaf_state_index"].numel())
+    level = np.zeros(C, dtype=np.int64)
+    par, sls, srs, lsps = [], [], [], []
+    for meta in wl["wave_metas"]:
+        if "sl" not in meta:
+            continue
+        ws = int(meta["start"])
+        sl = meta["sl"].detach().cpu().numpy().astype(np.int64)
+        sr = meta["sr"].detach().cpu().numpy().astype(np.int64)
+        p = ws + meta["reduce_idx"].detach().cpu().numpy().astype(np.int64)
+        n = sl.shape[0]
+        lp = meta.get("log_split_probs")
+        lp = np.zeros(n, np.float32) if lp is None else lp.detach().cpu().numpy().reshape(n).astype(np.float32)
+        np.maximum.at(level, p, np.maximum(level[sl], level[sr]) + 1)
+        par.append(p); sls.append(sl); srs.append(sr); lsps.append(lp)
+    if par:
+        par = np.concatenate(par); sls = np.concatenate(sls); srs = np.concatenate(srs)
+        lsps = np.concatenate(lsps)
+    else:
+        par = sls = srs = np.zeros(0, np.int64)
+        lsps = np.zeros(0, np.float32)
+    order_rows = np.lexsort((np.arange(C), level))
+    pos = np.empty(C, dtype=np.int64)
+    pos[order_rows] = np.arange(C)
+    order_splits = np.lexsort((np.arange(par.shape[0]), pos[par]))
+    counts = np.bincount(pos[par], minlength=C) if par.shape[0] else np.zeros(C, np.int64)
+    split_ptr = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    n_levels = int(level.max()) + 1 if C else 0
+    level_ptr = [0] + np.cumsum(np.bincount(level, minlength=n_levels)).tolist()
+    children = []
+    sp_sorted = par[order_splits]
+    lv_of_split = level[sp_sorted]
+    s_l, s_r = sls[order_splits], srs[order_splits]
+    for L in range(n_levels):
+        m = lv_of_split == L
+        children.append(int(np.unique(np.concatenate([s_l[m], s_r[m]])).shape[0]) if m.any() else 0)
+    plan = LevelPlan(
+        n_levels=n_levels, level_ptr=level_ptr,
+        rows=torch.from_numpy(order_rows.astype(np.int32)).to(dev),
+        split_ptr=torch.from_numpy(split_ptr).to(dev),
+        sl=torch.from_numpy(s_l.astype(np.int64)).to(dev),
+        sr=torch.from_numpy(s_r.astype(np.int64)).to(dev),
+        lsp=torch.from_numpy(lsps[order_splits].astype(np.float32)).to(dev),
+        level_of=level, children_per_level=children, n_splits=int(par.shape[0]),
+    )
+    static._plan = plan
+    return plan
+
+
+def supported(static) -> bool:
+    return bool(static.statewise) and not bool(static.itemwise)
+
+
+class _Topo:
+    """Device arrays of the species tree the engine kernels take."""
+
+    def __init__(self, sh):
+        self.tt = tree.from_helpers(sh)
+        self.pre = i32(sh["node_subtree_start"])
+        self.pre_end = i32(sh["node_subtree_end"])
+
+
+def _topo(static):
+    t = getattr(static, "_topo", None)
+    if t is None:
+        t = _Topo(static.state_helpers)
+        static._topo = t
+    return t
+
+
+def forward(static, theta, col_weights, *, pi_residual_out=None, timing=None):
+    """theta -> the 13 forward intermediates (same order as ``glue.solve_e_pi``) and the saved
+    split reductions ``dts_wave`` [C,S] for the backward."""
+    if not supported(static):
+        return glue.solve_e_pi(static, theta, col_weights, pi_residual_out=pi_residual_out), {}
+    so = static.solver_options
+    so.validate()
+    plan = build_plan(static)
+    topo = _topo(static)
+    tt = topo.tt
+    sh, wl = static.state_helpers, static.wave_layout
+    S = int(sh["S"])
+    pS, pD, pL, mc, clp, ucw = glue.solve_parameters(static, theta, col_weights)
+    E, E_s1, E_s2, Ebar = glue.solve_e(static, pS, pD, pL, mc, clp, ucw, theta)
+    k = glue.wave_constants(E, Ebar, E_s1, E_s2, pS, pD, mc, S)
+    dev = E.device
+    G = int(E.shape[0])
+    st = _lib.stream_handle(dev)
+    lin = torch.empty((4, G, S), device=dev, dtype=torch.float32)
+    _lib.call("kb_lin_consts", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(), k["e"].data_ptr(),
+              k["sl1"].data_ptr(), k["sl2"].data_ptr(), G * S, lin[0].data_ptr(), lin[1].data_ptr(),
+              lin[2].data_ptr(), lin[3].data_ptr(), st)
+    C = int(wl["leaf_state_index"].numel())
+    pi = torch.empty((C, S), device=dev, dtype=torch.float32)
+    pibar = torch.empty((C, S), device=dev, dtype=torch.float32)
+    row_max = torch.empty((C,), device=dev, dtype=torch.float32)
+    dts = torch.empty((C, S), device=dev, dtype=torch.float32)
+    leaf_state = i32(wl["leaf_state_index"])
+    item_idx = i64(static.rate_item_idx)
+    pDp, pSp = f32(k["pD_param"]), f32(k["pS_param"])
+    prs = 0 if int(pDp.shape[0]) == 1 else S
+    crs = 0 if G == 1 else S
+    fallback = torch.zeros((1,), device=dev, dtype=torch.int32)
+    static._fallback_rows = fallback
+    rows_ptr = plan.rows.data_ptr()
+    sp_ptr = plan.split_ptr.data_ptr()
+    for L in range(plan.n_levels):
+        a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
+        if b == a:
+            continue
+        _lib.call("kb_level_forward", rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
+                  plan.sr.data_ptr(), plan.lsp.data_ptr(), pi.data_ptr(), pibar.data_ptr(), pi.data_ptr(),
+                  pibar.data_ptr(), row_max.data_ptr(), dts.data_ptr(), _lib.ptr(pi_residual_out),
+                  fallback.data_ptr(), k["mc"].data_ptr(), k["dl"].data_ptr(), k["ebar"].data_ptr(),
+                  k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(),
+                  lin[0].data_ptr(), lin[1].data_ptr(), lin[2].data_ptr(), lin[3].data_ptr(), pDp.data_ptr(),
+                  pSp.data_ptr(), prs, crs, f32(clp).data_ptr(), int(ucw), tt.parent.data_ptr(),
+                  tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
+                  tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), int(so.pi_iters), S, st)
+    roots = pi[wl["root_row_ids"]]
+    out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
+    return out, {"dts_wave": dts}
+
+
+@torch.no_grad()
+def backward(static, theta, col_weights, saved, *, v_out=None):
+    """(forward intermediates) -> (grad_theta, grad_col); uses ``saved["dts_wave"]`` when the
+    forward was run by this engine, otherwise recomputes the split reductions."""
+    if not supported(static):
+        return glue.implicit_grad(static, theta, col_weights, saved)
+    so = static.solver_options
+    if so.self_loop_solver != "neumann":
+        return glue.implicit_grad(static, theta, col_weights, saved)
+    plan = build_plan(static)
+    topo = _topo(static)
+    tt = topo.tt
+    sh, wl = static.state_helpers, static.wave_layout
+    Pi, Pibar, row_max = f32(saved["pi_wave"]), f32(saved["pibar_wave"]), f32(saved["pibar_row_max"])
+    C, S = int(Pi.shape[0]), int(Pi.shape[1])
+    dev = Pi.device
+    st = _lib.stream_handle(dev)
+    E = saved["E"]
+    ucw = not glue.col_weights_are_uniform(col_weights)
+    k = glue.wave_constants(E, saved["Ebar"], saved["E_s1"], saved["E_s2"], saved["log_pS"], saved["log_pD"],
+                            saved["max_coupling"], S)
+    G = int(E.shape[0])
+    acc = torch.zeros((C, S), device=dev, dtype=torch.float32)
+    roots = wl["root_row_ids"]
+    acc.index_copy_(0, roots, glue.root_rhs(Pi, roots))
+    gacc = torch.zeros((10, S), device=dev, dtype=torch.float64)
+    dts = saved.get("dts_wave")
+    leaf_state = i32(wl["leaf_state_index"])
+    item_idx = i64(static.rate_item_idx)
+    pDp, pSp = f32(k["pD_param"]), f32(k["pS_param"])
+    prs = 0 if int(pDp.shape[0]) == 1 else S
+    crs = 0 if G == 1 else S
+    thr = float(so.adjoint_pruning_threshold)
+    side_thr = float(so.pibar_side_threshold)
+    rows_ptr = plan.rows.data_ptr()
+    sp_ptr = plan.split_ptr.data_ptr()
+    clp = f32(saved["col_log_probs"])
+    for L in reversed(range(plan.n_levels)):
+        a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
+        if b == a:
+            continue
+        _lib.call("kb_level_backward", rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
+                  plan.sr.data_ptr(), plan.lsp.data_ptr(), Pi.data_ptr(), Pibar.data_ptr(), row_max.data_ptr(),
+                  _lib.ptr(dts), acc.data_ptr(), _lib.ptr(v_out), gacc.data_ptr(), thr, int(not so.use_adjoint_pruning), side_thr,
+                  int(side_thr > 0.0), int(so.neumann_terms), k["mc"].data_ptr(), k["dl"].data_ptr(),
+                  k["ebar"].data_ptr(), k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(),
+                  k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
+                  tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(),
+                  topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(),
+                  S, st)
+    static._last_acc = acc
+    static._last_gacc = gacc
+    g = glue.GradAccumulators(E, S, dev)
+    _lib.call("kb_finalize_grads", gacc.data_ptr(), S, g.pD.data_ptr(), g.pS.data_ptr(), g.mt.data_ptr(),
+              g.E.data_ptr(), g.Ebar.data_ptr(), g.E_s1.data_ptr(), g.E_s2.data_ptr(), g.col.data_ptr(), st)
+    return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)

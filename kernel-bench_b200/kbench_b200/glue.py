@@ -241,8 +241,16 @@ def root_rhs(Pi, root_ids):
 
 
 @torch.no_grad()
-def implicit_grad(static, theta, col_weights, saved):
-    """Reference ``_implicit_grad.py:98-370`` followed by :func:`e_adjoint_and_theta_vjp`."""
+def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumulation=False):
+    """Reference ``_implicit_grad.py:98-370`` followed by :func:`e_adjoint_and_theta_vjp`.
+
+    ``exact_accumulation=False`` reproduces the reference's accumulation exactly: every wave's
+    parameter cotangents are added into fp32 running sums (the split kernels add per element
+    with atomics).  At large problems those running sums reach ~1e3 while most single-split
+    contributions are many orders of magnitude smaller, so fp32 swamping loses ~1e-3 of the
+    split sums.  ``exact_accumulation=True`` runs the same kernels but starts each wave's fp32
+    partial sums from zero and adds them into fp64 totals (the accuracy the fused engine gets
+    from its fp64 accumulators)."""
     so = static.solver_options
     wl, sh = static.wave_layout, static.state_helpers
     Pi, Pibar = saved["pi_wave"], saved["pibar_wave"]
@@ -254,10 +262,22 @@ def implicit_grad(static, theta, col_weights, saved):
                        saved["max_coupling"], S)
     acc = torch.zeros((C, S), device=dev, dtype=torch.float32)
     g = GradAccumulators(E, S, dev)
+    if exact_accumulation:
+        g_total = {n: torch.zeros((S,), device=dev, dtype=torch.float64)
+                   for n in ("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2", "col")}
     roots = wl["root_row_ids"]
     acc.index_copy_(0, roots, root_rhs(Pi, roots))
     item_idx = static.rate_item_idx
     leaf_state = wl["leaf_state_index"].to(device=dev, dtype=torch.int32).contiguous()
+    chunk = 64 if exact_accumulation else None
+
+    def flush():
+        for n in ("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2"):
+            g_total[n] += getattr(g, n)[0].double()
+            getattr(g, n).zero_()
+        g_total["col"] += g.col.double()
+        g.col.zero_()
+
     for meta in reversed(wl["wave_metas"]):
         ws, W = int(meta["start"]), int(meta["W"])
         rhs_k = acc[ws:ws + W]
@@ -265,45 +285,75 @@ def implicit_grad(static, theta, col_weights, saved):
                                                    use_pruning=bool(so.use_adjoint_pruning)).contiguous()
         has_splits = "sl" in meta
         dts_r = _dts(meta, Pi, Pibar, sh, k, item_idx, active) if has_splits else None
-        v_k, aw0, aw1, aw2, aw345, aw3, aw4 = wave_backward_uniform_fused(
-            Pi, Pibar, ws, W, S, dts_r, rhs_k, k["mc"], k["dl"], k["ebar"], k["e"], k["sl1"], k["sl2"],
-            saved["col_log_probs"], sh["node_child1"], sh["node_child2"], None, neumann_terms=so.neumann_terms,
-            leaf_state_idx=leaf_state, leaf_logp=k["leaf"], has_leaf_term=not has_splits, active_mask=active,
-            node_parent=sh["node_parent"], max_ancestor_depth=int(sh["max_ancestor_depth"]),
-            pibar_row_max=saved["pibar_row_max"], item_idx=item_idx, item_indexed_consts=True,
-            compact_level_ptr=sh["compact_level_ptr"], compact_level_parents=sh["compact_level_parents"],
-            compact_level_child1=sh["compact_level_child1"], compact_level_child2=sh["compact_level_child2"],
-            grad_col_log_probs=g.col, use_col_weights=ucw, self_loop_solver=so.self_loop_solver)
-        g.pD[0] += aw0.sum(dim=0)
-        g.pS[0] += aw345.sum(dim=0)
-        g.E[0] += (aw0 + aw2).sum(dim=0)
-        g.Ebar[0] += aw1.sum(dim=0)
-        g.E_s1[0] += aw4.sum(dim=0)
-        g.E_s2[0] += aw3.sum(dim=0)
-        g.mt[0] += aw2.sum(dim=0)
-        if has_splits:
-            ud, A, side, _, _ = dts_cross_backward_accum_fused(
-                Pi, Pibar, v_k, ws, meta["sl"], meta["sr"], meta["reduce_idx"], meta["log_split_probs"],
-                k["pD_param"], k["pS_param"], sh["node_child1"], sh["node_child2"], acc, S, active_mask=active,
-                merge_s_term=True, grad_log_pD=g.pD, grad_log_pS=g.pS, grad_mt=g.mt, accum_param_reductions=True,
-                accum_mt_reduction=True, output_pibar_ud=True, output_pibar_side_active=True,
-                pibar_side_threshold=so.pibar_side_threshold, mt_squeezed=k["mc"],
-                pibar_row_max=saved["pibar_row_max"], skip_inactive_pibar_output_zero=True, item_idx=item_idx)
-            uniform_cross_pibar_vjp_tree_from_ud_fused(
-                Pi, saved["col_log_probs"], ud, A, meta["sl"], meta["sr"], acc, S, active_mask=active,
-                reduce_idx=meta["reduce_idx"], pibar_row_max=saved["pibar_row_max"], skip_zero_sides=True,
-                side_active=side, compact_level_ptr=sh["compact_level_ptr"],
+        v_k = torch.empty((W, S), device=dev, dtype=torch.float32)
+        row_blocks = [(0, W)] if chunk is None else [(a, min(a + chunk, W)) for a in range(0, W, chunk)]
+        for a, b in row_blocks:
+            out = wave_backward_uniform_fused(
+                Pi, Pibar, ws + a, b - a, S, None if dts_r is None else dts_r[a:b], rhs_k[a:b], k["mc"], k["dl"],
+                k["ebar"], k["e"], k["sl1"], k["sl2"], saved["col_log_probs"], sh["node_child1"], sh["node_child2"],
+                None, neumann_terms=so.neumann_terms, leaf_state_idx=leaf_state, leaf_logp=k["leaf"],
+                has_leaf_term=not has_splits, active_mask=active[a:b], node_parent=sh["node_parent"],
+                max_ancestor_depth=int(sh["max_ancestor_depth"]), pibar_row_max=saved["pibar_row_max"],
+                item_idx=item_idx, item_indexed_consts=True, compact_level_ptr=sh["compact_level_ptr"],
                 compact_level_parents=sh["compact_level_parents"], compact_level_child1=sh["compact_level_child1"],
                 compact_level_child2=sh["compact_level_child2"], grad_col_log_probs=g.col, use_col_weights=ucw,
-                side_active_threshold=so.pibar_side_threshold)
+                self_loop_solver=so.self_loop_solver)
+            vb, aw0, aw1, aw2, aw345, aw3, aw4 = out
+            v_k[a:b] = vb
+            dbg = getattr(static, "_debug_sums", None)
+            if dbg is not None:
+                for name, t in (("aw0", aw0), ("aw1", aw1), ("aw2", aw2), ("aw3", aw3), ("aw4", aw4), ("aw345", aw345)):
+                    dbg[name] = dbg.get(name, 0) + t.double().sum(dim=0)
+            g.pD[0] += aw0.sum(dim=0)
+            g.pS[0] += aw345.sum(dim=0)
+            g.E[0] += (aw0 + aw2).sum(dim=0)
+            g.Ebar[0] += aw1.sum(dim=0)
+            g.E_s1[0] += aw4.sum(dim=0)
+            g.E_s2[0] += aw3.sum(dim=0)
+            g.mt[0] += aw2.sum(dim=0)
+            if exact_accumulation:
+                flush()
+        if v_out is not None:
+            v_out[ws:ws + W][active] = v_k[active]
+        if has_splits:
+            n_split = int(meta["sl"].numel())
+            split_blocks = [(0, n_split)] if chunk is None else [(a, min(a + chunk, n_split))
+                                                                   for a in range(0, n_split, chunk)]
+            for a, b in split_blocks:
+                sl_c, sr_c, red_c = meta["sl"][a:b], meta["sr"][a:b], meta["reduce_idx"][a:b]
+                ud, A, side, _, _ = dts_cross_backward_accum_fused(
+                    Pi, Pibar, v_k, ws, sl_c, sr_c, red_c, meta["log_split_probs"][a:b], k["pD_param"],
+                    k["pS_param"], sh["node_child1"], sh["node_child2"], acc, S, active_mask=active,
+                    merge_s_term=True, grad_log_pD=g.pD, grad_log_pS=g.pS, grad_mt=g.mt,
+                    accum_param_reductions=True, accum_mt_reduction=True, output_pibar_ud=True,
+                    output_pibar_side_active=True, pibar_side_threshold=so.pibar_side_threshold,
+                    mt_squeezed=k["mc"], pibar_row_max=saved["pibar_row_max"],
+                    skip_inactive_pibar_output_zero=True, item_idx=item_idx)
+                uniform_cross_pibar_vjp_tree_from_ud_fused(
+                    Pi, saved["col_log_probs"], ud, A, sl_c, sr_c, acc, S, active_mask=active, reduce_idx=red_c,
+                    pibar_row_max=saved["pibar_row_max"], skip_zero_sides=True, side_active=side,
+                    compact_level_ptr=sh["compact_level_ptr"], compact_level_parents=sh["compact_level_parents"],
+                    compact_level_child1=sh["compact_level_child1"],
+                    compact_level_child2=sh["compact_level_child2"], grad_col_log_probs=g.col, use_col_weights=ucw,
+                    side_active_threshold=so.pibar_side_threshold)
+                if exact_accumulation:
+                    flush()
+    if exact_accumulation:
+        for n in ("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2"):
+            getattr(g, n)[0] = g_total[n].float()
+        g.col.copy_(g_total["col"].float())
+    static._last_acc = acc
     return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
 
 
 def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col_weights):
-    """Reference ``_implicit_grad.py:373-475``: solve ``(I - J_E^T) w = q`` with BiCGSTAB, one E-step
+    """The accumulated cotangents are kept on ``static._last_grad_acc`` for inspection.
+
+    Reference ``_implicit_grad.py:373-475``: solve ``(I - J_E^T) w = q`` with BiCGSTAB, one E-step
     VJP kernel per matvec, then the theta / column-weight VJP through the parameter extraction."""
     so = static.solver_options
     sh = static.state_helpers
+    static._last_grad_acc = g
     topo = (sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]))
     E_star = saved["E"]
     E_req = E_star.detach().requires_grad_(True)

@@ -64,17 +64,23 @@ def make_static(captured: dict, device, *, engine: str = "fused") -> SimpleNames
 
 
 def run_forward(static, theta, col_weights):
-    """theta -> (loss, dict of forward intermediates)."""
+    """theta -> (loss, dict of forward intermediates).
+
+    The fused engine also returns ``saved["dts_wave"]`` (the per-row split reductions), which its
+    backward reuses instead of recomputing them; every other key is the reference's."""
+    from .glue import nll_from_root_rows
+    extras = {}
     with torch.no_grad():
         if getattr(static, "engine", "fused") == "fused":
             from . import engine
-            out = engine.forward(static, theta, col_weights)
+            out, extras = engine.forward(static, theta, col_weights)
         else:
             from . import glue
             out = glue.solve_e_pi(static, theta, col_weights)
-        from .glue import nll_from_root_rows
         loss = nll_from_root_rows(out[4], out[0])
-    return loss, dict(zip(FORWARD_SAVED_NAMES, out))
+    saved = dict(zip(FORWARD_SAVED_NAMES, out))
+    saved.update(extras)
+    return loss, saved
 
 
 def run_backward(static, theta, col_weights, saved: dict):
