@@ -27,6 +27,12 @@ _CTYPES = {
 
 _lib = None
 
+# Launch accounting: every kb_* call that enqueues device work increments LAUNCHES[name]
+# (kb_abi_version and argument-only failures excluded).  Read by bench.py to report how many
+# of this library's kernels ran inside a timed region.
+LAUNCHES: dict = {}
+_NO_LAUNCH = {"kb_abi_version"}
+
 
 def parse_header(text: str | None = None) -> dict[str, list]:
     """Return ``{name: [ctypes arg types]}`` for every ``int kb_*(...)`` declaration."""
@@ -73,6 +79,8 @@ def call(name: str, *args) -> None:
     """Call ``kb_<name>`` and map a non-zero status to the reference's exception types."""
     status = getattr(lib(), name)(*args)
     if status == KB_OK:
+        if name not in _NO_LAUNCH:
+            LAUNCHES[name] = LAUNCHES.get(name, 0) + 1
         return
     if status in (KB_ERR_ARG, KB_ERR_SIZE):
         raise ValueError(f"{name}: invalid argument or unsupported size (status {status})")

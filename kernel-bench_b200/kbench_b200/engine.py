@@ -115,7 +115,43 @@ def _topo(static):
     return t
 
 
-def forward(static, theta, col_weights, *, pi_residual_out=None, timing=None):
+class LevelTimer:
+    """Optional per-level CUDA-event timing of the engine's level kernels (set
+    ``static._level_timer = LevelTimer()``); events are recorded on the launching stream."""
+
+    def __init__(self):
+        self.events = {"kb_level_forward": [], "kb_level_backward": []}
+
+    def wrap(self, name, level, fn):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        self.events[name].append((level, a, b))
+
+    def totals(self):
+        """{kernel: (total_ms, n_launches, per-level list of (level, ms))} after a sync."""
+        out = {}
+        for name, evs in self.events.items():
+            per = [(lv, a.elapsed_time(b)) for lv, a, b in evs]
+            out[name] = (sum(t for _, t in per), len(per), per)
+        return out
+
+    def reset(self):
+        for v in self.events.values():
+            v.clear()
+
+
+def _launch(static, name, level, *args):
+    timer = getattr(static, "_level_timer", None)
+    if timer is None:
+        _lib.call(name, *args)
+    else:
+        timer.wrap(name, level, lambda: _lib.call(name, *args))
+
+
+def forward(static, theta, col_weights, *, pi_residual_out=None):
     """theta -> the 13 forward intermediates (same order as ``glue.solve_e_pi``) and the saved
     split reductions ``dts_wave`` [C,S] for the backward."""
     if not supported(static):
@@ -155,7 +191,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, timing=None):
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
             continue
-        _lib.call("kb_level_forward", rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
+        _launch(static, "kb_level_forward", L, rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
                   plan.sr.data_ptr(), plan.lsp.data_ptr(), pi.data_ptr(), pibar.data_ptr(), pi.data_ptr(),
                   pibar.data_ptr(), row_max.data_ptr(), dts.data_ptr(), _lib.ptr(pi_residual_out),
                   fallback.data_ptr(), k["mc"].data_ptr(), k["dl"].data_ptr(), k["ebar"].data_ptr(),
@@ -210,7 +246,7 @@ def backward(static, theta, col_weights, saved, *, v_out=None):
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
             continue
-        _lib.call("kb_level_backward", rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
+        _launch(static, "kb_level_backward", L, rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
                   plan.sr.data_ptr(), plan.lsp.data_ptr(), Pi.data_ptr(), Pibar.data_ptr(), row_max.data_ptr(),
                   _lib.ptr(dts), acc.data_ptr(), _lib.ptr(v_out), gacc.data_ptr(), thr, int(not so.use_adjoint_pruning), side_thr,
                   int(side_thr > 0.0), int(so.neumann_terms), k["mc"].data_ptr(), k["dl"].data_ptr(),
