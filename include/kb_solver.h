@@ -174,7 +174,9 @@ int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const flo
  * [split_ptr[b], split_ptr[b+1]) of (sl, sr, lsp) -- or the leaf seed for split-less leaf rows --
  * then all pi_iters iterations on chip; writes the final pi, pibar rows, pibar_row_max, the split
  * reduction (dts_save, may be NULL) and the last-iteration residual (may be NULL).
- * fallback_count (device int, may be NULL) counts rows recomputed in log space. */
+ * fallback_count (device int, may be NULL) counts rows recomputed in log space.  packed: [4,S] uint32
+ * per-column tables (children, Euler-tour enter/exit, preorder start/end, parent | first-child
+ * flag; two 16-bit fields each, 0xFFFF = none) -- see kbench_b200/tree.py pack_columns(). */
 int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                      const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src, float* pi,
                      float* pibar, float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
@@ -184,34 +186,33 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
                      long long param_row_stride, long long const_row_stride, const float* col_log_probs,
                      int use_col_weights, const int* node_parent, const int* node_child1, const int* node_child2,
                      const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
-                     const long long* item_idx, const int* leaf_state, int pi_iters, int S, void* stream);
+                     const long long* item_idx, const int* leaf_state, const unsigned* packed, int pi_iters, int S,
+                     void* stream);
 
 /* Backward of one dependency level (replaces, for the rows listed, active_mask_from_rhs_absmax_
  * fused + compute_dts_forward + wave_backward_uniform_fused + dts_cross_backward_accum_fused +
  * uniform_cross_pibar_vjp_tree_from_ud_fused as driven by kbench/api/_implicit_grad.py:
- * 190-353): per active row the Neumann adjoint, its parameter and column cotangents into
- * grad_acc ([10,S] fp64: aw0..aw5 sums, split pD/pS/mt sums, column gradient), and every split's
- * child cotangents added into accumulated_rhs. dts_saved may be NULL (recomputed); v_out [C,S]
- * (may be NULL) receives the solved adjoint row of every active row. */
+ * 190-353).  Persistent: min(n_rows, n_slots) CTAs, CTA b takes rows b, b+grid, ...  Per active
+ * row: the Neumann adjoint, its parameter and column cotangents (summed in shared memory per CTA
+ * and added to that CTA's fp64 slot of grad_slots [n_slots, 8, NTV] at the end; slots persist
+ * across levels and are reduced in a fixed order by kb_reduce_grad_slots), and every split's child
+ * cotangents added into accumulated_rhs.  dts_saved may be NULL (recomputed); v_out [C,S] (may be
+ * NULL) receives the solved adjoint row of every active row.  packed_padded: [4,NTV] tables of
+ * pack_columns(..., ntv) with NTV = threads x columns-per-thread (kbench_b200/tree.py). */
 int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                       const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
                       const float* pibar_row_max, const float* dts_saved, float* accumulated_rhs, float* v_out,
-                      double* grad_acc,
-                      float threshold, int strict_gt, float side_threshold, int side_threshold_enabled,
-                      int neumann_terms, const float* mc, const float* dl, const float* ebar, const float* e,
-                      const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
-                      const float* log_pS, long long param_row_stride, long long const_row_stride,
-                      const float* col_log_probs, int use_col_weights, const int* node_parent,
-                      const int* node_child1, const int* node_child2, const int* node_pre, const int* node_pre_end,
-                      const int* jumps, int K, const long long* item_idx, const int* leaf_state, int S,
-                      void* stream);
+                      double* grad_slots, int n_slots, float threshold, int strict_gt, float side_threshold,
+                      int side_threshold_enabled, int neumann_terms, const float* mc, const float* dl,
+                      const float* ebar, const float* e, const float* sl1, const float* sl2,
+                      const float* leaf_logp, const float* log_pD, const float* log_pS,
+                      long long param_row_stride, long long const_row_stride, const float* col_log_probs,
+                      int use_col_weights, const long long* item_idx, const int* leaf_state,
+                      const unsigned* packed_padded, int S, void* stream);
 
-/* Gradient accumulators of kb_level_backward -> the eight fp32 [S] cotangent vectors of the
- * backward glue (grad_log_pD, grad_log_pS, grad_mt, grad_E, grad_Ebar, grad_E_s1, grad_E_s2,
- * grad_col_log_probs). */
-int kb_finalize_grads(const double* grad_acc, int S, float* grad_log_pD, float* grad_log_pS, float* grad_mt,
-                      float* grad_E, float* grad_Ebar, float* grad_E_s1, float* grad_E_s2, float* grad_col,
-                      void* stream);
+/* Fixed-order sum of kb_level_backward's fp64 slots -> out8 [8,S] fp32: the cotangents of
+ * log_pD, log_pS, max_coupling, E, Ebar, E_s1, E_s2 and col_log_probs (in that order). */
+int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S, float* out8, void* stream);
 
 #ifdef __cplusplus
 }

@@ -213,3 +213,86 @@ __device__ __forceinline__ float block_exclusive_scan(float* a, int n, float* tm
 }
 
 }  // namespace kb
+
+namespace kb {
+
+// Exclusive prefix sums in place over buf[0 .. blockDim.x*CH) (the caller zero-pads the tail);
+// thread t owns the contiguous chunk [t*CH, (t+1)*CH).  Returns the total.  tmp >= 32 floats.
+// Syncs on exit (the caller syncs before, after writing buf).
+template <int CH>
+__device__ __forceinline__ float block_exclusive_scan_ch(float* buf, float* tmp) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, wid = tid >> 5, nw = (blockDim.x + 31) >> 5;
+  float v[CH];
+  float* base = buf + tid * CH;
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(base + j);
+      v[j] = q.x; v[j + 1] = q.y; v[j + 2] = q.z; v[j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) v[j] = base[j];
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) local += v[j];
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) tmp[wid] = incl;
+  __syncthreads();
+  float wbase = 0.f, total;
+  {
+    float t = lane < nw ? tmp[lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    // t = inclusive prefix of warp totals at warp index `lane`
+    const float prev = __shfl_up_sync(0xffffffffu, t, 1);
+    wbase = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : prev, wid);
+    total = __shfl_sync(0xffffffffu, t, nw - 1);
+  }
+  float run = wbase + incl - local;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const float x = v[j];
+    v[j] = run;
+    run += x;
+  }
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4)
+      *reinterpret_cast<float4*>(base + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) base[j] = v[j];
+  }
+  __syncthreads();
+  return total;
+}
+
+// Block max / min-of-positives / sum in one reduction; tmp >= 96 floats.  Two barriers.
+__device__ __forceinline__ void block_max_minpos_sum(float& mx, float& mn, float& sm, float* tmp) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  mx = warp_max(mx);
+  mn = -warp_max(-mn);
+  sm = warp_sum(sm);
+  __syncthreads();
+  if (lane == 0) { tmp[wid] = mx; tmp[32 + wid] = mn; tmp[64 + wid] = sm; }
+  __syncthreads();
+  const float a1 = lane < nw ? tmp[lane] : 0.f;
+  const float a2 = lane < nw ? tmp[32 + lane] : 3.0e38f;
+  const float a3 = lane < nw ? tmp[64 + lane] : 0.f;
+  mx = warp_max(a1);
+  mn = -warp_max(-a2);
+  sm = warp_sum(a3);
+}
+
+}  // namespace kb

@@ -64,6 +64,7 @@ struct LevelConsts {
   int K;
   const long long* item_idx;
   const int* leaf_state;
+  const unsigned* packed;  // [4,S]: children, Euler tour, preorder, parent (16-bit pairs)
   int S;
 };
 
@@ -213,15 +214,97 @@ struct FwdArgs {
   int pi_iters;
 };
 
+__device__ __forceinline__ unsigned lo16(unsigned v) { return v & 0xFFFFu; }
+__device__ __forceinline__ unsigned hi16(unsigned v) { return v >> 16; }
+
+// dts of one row from its splits (online LSE across splits) into x[] (log values); the two
+// child Pi rows are staged in Pl / Pr (shared) for the speciation gathers.
 template <int VPT>
-__global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
+__device__ __forceinline__ void dts_row2(const LevelConsts& c, const float* __restrict__ Pi,
+                                         const float* __restrict__ Pibar, const SplitCSR& sp, long long i0,
+                                         long long i1, size_t pb, const unsigned* cc, float* Pl, float* Pr,
+                                         float* x) {
+  const int S = c.S;
+  float m[VPT], acc[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) { m[k] = neg_inf(); acc[k] = 0.f; }
+  for (long long i = i0; i < i1; ++i) {
+    const long long l = sp.sl[i], r = sp.sr[i];
+    const float* pil = Pi + (size_t)l * S;
+    const float* pir = Pi + (size_t)r * S;
+    const float* pbl = Pibar + (size_t)l * S;
+    const float* pbr = Pibar + (size_t)r * S;
+    __syncthreads();
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
+      Pl[s] = pil[s];
+      Pr[s] = pir[s];
+    }
+    __syncthreads();
+    const float lsp = sp.lsp[i];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * blockDim.x;
+      if (s < S) {
+        const float ld = c.log_pD[pb + s];
+        const float ls = c.log_pS[pb + s];
+        const unsigned a = lo16(cc[k]), b = hi16(cc[k]);
+        const float pl = Pl[s], pr = Pr[s];
+        const float v0 = lsp + ld + pl + pr;
+        const float v1 = lsp + pl + pbr[s];
+        const float v2 = lsp + pr + pbl[s];
+        const float v3 = lsp + ls + (a < (unsigned)S ? Pl[a] : neg_inf()) + (b < (unsigned)S ? Pr[b] : neg_inf());
+        const float v4 = lsp + ls + (a < (unsigned)S ? Pr[a] : neg_inf()) + (b < (unsigned)S ? Pl[b] : neg_inf());
+        const float sm_ = fmaxf(fmaxf(fmaxf(v0, v1), fmaxf(v2, v3)), v4);
+        const float sms = safe_max(sm_);
+        const float ssum = ex2(v0 - sms) + ex2(v1 - sms) + ex2(v2 - sms) + ex2(v3 - sms) + ex2(v4 - sms);
+        if (i == i0) {
+          m[k] = sm_;
+          acc[k] = ssum;
+        } else {
+          const float nm = fmaxf(m[k], sm_);
+          const float nms = safe_max(nm);
+          acc[k] = (is_neg_inf(m[k]) ? 0.f : acc[k] * ex2(m[k] - nms)) + ssum * ex2(sms - nms);
+          m[k] = nm;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) x[k] = lg2(acc[k]) + m[k];
+}
+
+// Ancestor-or-self path sums of the values pv[] through one scan of the Euler tour in T2
+// (padded to blockDim.x * 2 * VPT floats, tail zero).  Returns path[] for the own columns.
+template <int VPT>
+__device__ __forceinline__ void tour_pathsums(float* T2, float* tmp, const unsigned* tr, const float* pv, int S,
+                                              float* path) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int s = threadIdx.x + k * blockDim.x;
+    if (s < S) {
+      T2[lo16(tr[k])] = pv[k];
+      T2[hi16(tr[k])] = -pv[k];
+    }
+  }
+  __syncthreads();
+  block_exclusive_scan_ch<2 * VPT>(T2, tmp);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int s = threadIdx.x + k * blockDim.x;
+    path[k] = s < S ? T2[lo16(tr[k])] + pv[k] : 0.f;
+  }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
   extern __shared__ float sm[];
   const LevelConsts& c = a.c;
   const int S = c.S;
-  float* P = sm;
-  float* X = sm + S;
-  float* Y = sm + 2 * S;
-  float* red = sm + 3 * S;
+  const int NT = blockDim.x;
+  const int TN = NT * 2 * VPT;  // padded tour length >= 2S
+  float* T2 = sm;
+  float* P = sm + TN;
+  float* red = P + NT * VPT;  // 128 floats
   const int b = blockIdx.x;
   const long long row = a.sp.rows[b];
   const long long item = c.item_idx[row];
@@ -233,20 +316,39 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
   const int leaf = is_leaf ? leaf_raw : -1;
   const float leafv = is_leaf ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
 
+  // per-column topology and linear constants, loaded once
+  unsigned cc[VPT], tr[VPT];
+  float kA[VPT], kB[VPT], kC1[VPT], kC2[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int s = threadIdx.x + k * NT;
+    cc[k] = 0xFFFFFFFFu;
+    tr[k] = 0u;
+    kA[k] = kB[k] = kC1[k] = kC2[k] = 0.f;
+    if (s < S) {
+      cc[k] = c.packed[s];
+      tr[k] = c.packed[S + s];
+      kA[k] = c.linA[cb + s];
+      kB[k] = c.linB[cb + s];
+      kC1[k] = c.linC1[cb + s];
+      kC2[k] = c.linC2[cb + s];
+    }
+  }
+
   // ---- initial row (log values) ----
   float x[VPT];
   if (is_leaf) {
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
+      const int s = threadIdx.x + k * NT;
       x[k] = s < S ? leaf_seed(c, cb, item, leaf, s) : neg_inf();
     }
   } else {
-    dts_row<VPT>(c, a.Pi_src, a.Pibar_src, a.sp, i0, i1, pb, X, Y, x);
+    dts_row2<VPT>(c, a.Pi_src, a.Pibar_src, a.sp, i0, i1, pb, cc, T2, T2 + S, x);
     if (a.dts_save) {
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * blockDim.x;
+        const int s = threadIdx.x + k * NT;
         if (s < S) a.dts_save[(size_t)row * S + s] = x[k];
       }
     }
@@ -255,39 +357,41 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
 #pragma unroll
   for (int k = 0; k < VPT; ++k) m0 = fmaxf(m0, x[k]);
   const float Rd = safe_max(block_max(m0, red));  // scale of the initial row (and of the dts term)
+  // zero the whole tour buffer (the padded tail must stay zero for the scans)
+  for (int i = threadIdx.x; i < TN; i += NT) T2[i] = 0.f;
 
   // ---- linear-space iterations ----
-  float pv[VPT], td[VPT];
+  float pv[VPT], td[VPT], zl[VPT];
   float psum = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
+    const int s = threadIdx.x + k * NT;
     pv[k] = s < S ? ex2(x[k] - Rd) : 0.f;
     td[k] = is_leaf ? 0.f : pv[k];
-    if (s < S) { P[s] = pv[k]; X[s] = pv[k]; }
+    if (s < S) P[s] = pv[k];
     psum += pv[k];
   }
   float sumP = block_sum(psum, red);
   float R = Rd;
   bool fallback = false;
-  float zl[VPT];  // last iteration's unnormalised values (relative to Rlast)
   float Rlast = R;
   for (int it = 1; it < a.pi_iters; ++it) {
-    const float* anc = pathsums(X, Y, c);
+    float path[VPT];
+    tour_pathsums<VPT>(T2, red, tr, pv, S, path);
     const float fd = ex2(Rd - R);
     const float lf = is_leaf ? ex2(leafv - R) : 0.f;
     float zmax = 0.f, zmin = 3.0e38f, zsum = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
+      const int s = threadIdx.x + k * NT;
       float z = 0.f;
       if (s < S) {
-        const float D = sumP - anc[s];
-        z = pv[k] * __ldg(c.linA + cb + s);
-        if (D > 0.f) z = fmaf(D, __ldg(c.linB + cb + s), z);
-        const int ca = c.c1[s], cbb = c.c2[s];
-        if ((unsigned)ca < (unsigned)S) z = fmaf(P[ca], __ldg(c.linC1 + cb + s), z);
-        if ((unsigned)cbb < (unsigned)S) z = fmaf(P[cbb], __ldg(c.linC2 + cb + s), z);
+        const float D = sumP - path[k];
+        z = pv[k] * kA[k];
+        if (D > 0.f) z = fmaf(D, kB[k], z);
+        const unsigned ca = lo16(cc[k]), cbb = hi16(cc[k]);
+        if (ca < (unsigned)S) z = fmaf(P[ca], kC1[k], z);
+        if (cbb < (unsigned)S) z = fmaf(P[cbb], kC2[k], z);
         if (s == leaf) z += lf;
         z = fmaf(td[k], fd, z);
         zmax = fmaxf(zmax, z);
@@ -296,24 +400,8 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
       }
       zl[k] = z;
     }
-    // one combined reduction: max, min-positive, sum
-    {
-      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-      const int nw = (blockDim.x + 31) >> 5;
-      zmax = warp_max(zmax);
-      zmin = -warp_max(-zmin);
-      zsum = warp_sum(zsum);
-      __syncthreads();
-      if (lane == 0) { red[wid] = zmax; red[32 + wid] = zmin; red[64 + wid] = zsum; }
-      __syncthreads();
-      float a1 = lane < nw ? red[lane] : 0.f;
-      float a2 = lane < nw ? red[32 + lane] : 3.0e38f;
-      float a3 = lane < nw ? red[64 + lane] : 0.f;
-      zmax = warp_max(a1);
-      zmin = -warp_max(-a2);
-      zsum = warp_sum(a3);
-    }
-    if (zmax > 0.f && zmin < zmax * 7.8886091e-31f) {  // 2^-100
+    block_max_minpos_sum(zmax, zmin, zsum, red);
+    if (zmax > 0.f && zmin < zmax * 7.8886091e-31f) {  // 2^-100: fp32 linear values unsafe
       fallback = true;
       break;
     }
@@ -321,15 +409,13 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
     if (it == a.pi_iters - 1) break;  // keep zl (relative to Rlast) for the final write
     const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
     R = zmax > 0.f ? R + lg2(zmax) : R;
-    __syncthreads();
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
+      const int s = threadIdx.x + k * NT;
       pv[k] = zl[k] * inv;
-      if (s < S) { P[s] = pv[k]; X[s] = pv[k]; }
+      if (s < S) P[s] = pv[k];
     }
     sumP = zsum * inv;
-    __syncthreads();
   }
 
   float pf[VPT];  // final Pi (log values)
@@ -338,7 +424,7 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
       float d = 0.f;
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * blockDim.x;
+        const int s = threadIdx.x + k * NT;
         if (s < S && zl[k] > 0.f && pv[k] > 0.f) d = fmaxf(d, fabsf(lg2(zl[k]) - lg2(pv[k])));
       }
       d = block_max(d, red);
@@ -349,10 +435,12 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
   } else {
     // log-space recomputation of the whole row from its initial values (rare)
     if (threadIdx.x == 0 && a.fallback_count) atomicAdd(a.fallback_count, 1);
+    float* X = T2;
+    float* Y = T2 + S;
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
+      const int s = threadIdx.x + k * NT;
       if (s < S) P[s] = x[k];
     }
     __syncthreads();
@@ -363,7 +451,7 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
         float d = 0.f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
-          const int s = threadIdx.x + k * blockDim.x;
+          const int s = threadIdx.x + k * NT;
           if (s < S && !is_neg_inf(nv[k]) && !is_neg_inf(P[s])) d = fmaxf(d, fabsf(nv[k] - P[s]));
         }
         d = block_max(d, red);
@@ -372,24 +460,26 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
       __syncthreads();
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * blockDim.x;
+        const int s = threadIdx.x + k * NT;
         if (s < S) P[s] = nv[k];
       }
       __syncthreads();
     }
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
+      const int s = threadIdx.x + k * NT;
       pf[k] = s < S ? P[s] : neg_inf();
     }
+    __syncthreads();
+    for (int i = threadIdx.x; i < TN; i += NT) T2[i] = 0.f;
   }
 
-  // ---- final Pi, row max, Pibar (as the reference computes them from the final log row) ----
+  // ---- final Pi, row max, Pibar (from the final log row, as the reference computes them) ----
   float* prow = a.pi + (size_t)row * S;
   float mx = neg_inf();
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
+    const int s = threadIdx.x + k * NT;
     if (s < S) {
       prow[s] = pf[k];
       float w = pf[k];
@@ -399,27 +489,28 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
   }
   const float row_max = block_max(mx, red);
   const float rms = safe_max(row_max);
+  float pe[VPT];
   float sum = 0.f;
-  __syncthreads();
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
+    const int s = threadIdx.x + k * NT;
+    pe[k] = 0.f;
     if (s < S) {
       float w = pf[k];
       if (c.use_col) w += c.col[s];
-      const float xv = ex2(w - rms);
-      X[s] = xv;
-      sum += xv;
+      pe[k] = ex2(w - rms);
+      sum += pe[k];
     }
   }
   const float row_sum = block_sum(sum, red);
-  const float* anc = pathsums(X, Y, c);
+  float path[VPT];
+  tour_pathsums<VPT>(T2, red, tr, pe, S, path);
   float* brow = a.pibar + (size_t)row * S;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
+    const int s = threadIdx.x + k * NT;
     if (s < S) {
-      const float denom = row_sum - anc[s];
+      const float denom = row_sum - path[k];
       brow[s] = denom > 0.f ? lg2(denom) + row_max + c.mc[cb + s] : neg_inf();
     }
   }
@@ -431,7 +522,7 @@ __global__ void __launch_bounds__(512) level_forward_kernel(FwdArgs a) {
 // ------------------------------------------------------------------------------------------
 
 struct BwdArgs {
-  LevelConsts c;
+  LevelConsts c;           // c.packed: padded [4, NTV] tables (invalid child/parent -> zero column NTV-1)
   SplitCSR sp;
   const float* Pi;
   const float* Pibar;
@@ -439,7 +530,7 @@ struct BwdArgs {
   const float* dts_saved;  // [C,S] or null (recompute from the splits)
   float* acc;              // accumulated_rhs [C,S]
   float* v_out;            // [C,S] solved adjoint rows (active rows) or null
-  double* gacc;            // [10,S]: aw0..aw5, dD, dS, dM, col
+  double* slots;           // [gridDim.x, 8, NTV] fp64 per-CTA partial column sums (persist across levels)
   float threshold;
   int strict_gt;
   float side_thr;
@@ -448,365 +539,366 @@ struct BwdArgs {
   int n_rows;
 };
 
+// accumulator rows of the per-CTA column sums
+enum { G_PD = 0, G_PS, G_MT, G_E, G_EBAR, G_ES1, G_ES2, G_COL, G_N };
+
 template <int VPT>
-__global__ void __launch_bounds__(512) level_backward_kernel(BwdArgs a) {
+__global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a) {
   extern __shared__ float sm[];
   const LevelConsts& c = a.c;
   const int S = c.S;
-  float* P = sm;             // Pi row (log)
-  float* B0 = sm + S;
-  float* B1 = sm + 2 * S;
-  float* B2 = sm + 3 * S;
-  float* B3 = sm + 4 * S;
-  float* B4 = sm + 5 * S;
-  float* red = sm + 6 * S;   // >= 96 floats
-  const int b = blockIdx.x;
-  const long long row = a.sp.rows[b];
-  const long long item = c.item_idx[row];
-  const size_t cb = (size_t)(item * c.crs);
-  const size_t pb = (size_t)(item * c.prs);
-  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
-  const bool has_splits = i1 > i0;
-  const int leaf_raw = c.leaf_state[row];
-  const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
-
-  // ---- active check ----
-  float v[VPT];
-  float amax = 0.f;
-  const float* rrow = a.acc + (size_t)row * S;
+  const int NT = blockDim.x;
+  const int NTV = NT * VPT;
+  float* P = sm;               // Pi row (log; -inf on padding), later speciation cotangents
+  float* T = sm + NTV;         // Neumann term / tour (with U) / staged child rows
+  float* U = sm + 2 * NTV;     // preorder scan buffer
+  float* ACC = sm + 3 * NTV;   // G_N rows of NTV fp32 column sums (this CTA)
+  float* red = ACC + G_N * NTV;
+  unsigned cc[VPT], tr[VPT], pk[VPT], pa[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    v[k] = s < S ? rrow[s] : 0.f;
-    amax = fmaxf(amax, fabsf(v[k]));
-  }
-  amax = block_max(amax, red);
-  const bool active = a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold);
-  if (!active) return;
-
-  // ---- dts row (log) ----
-  float dv[VPT];
-  if (has_splits) {
-    if (a.dts_saved) {
+    const int s = threadIdx.x + k * NT;
+    cc[k] = c.packed[s];
+    tr[k] = c.packed[NTV + s];
+    pk[k] = c.packed[2 * NTV + s];
+    pa[k] = c.packed[3 * NTV + s];
 #pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * blockDim.x;
-        dv[k] = s < S ? a.dts_saved[(size_t)row * S + s] : neg_inf();
-      }
-    } else {
-      dts_row<VPT>(c, a.Pi, a.Pibar, a.sp, i0, i1, pb, B0, B1, dv);
+    for (int j = 0; j < G_N; ++j) ACC[j * NTV + s] = 0.f;
+  }
+  for (int b = blockIdx.x; b < a.n_rows; b += gridDim.x) {
+    const long long row = a.sp.rows[b];
+    const long long item = c.item_idx[row];
+    const size_t cb = (size_t)(item * c.crs);
+    const size_t pb = (size_t)(item * c.prs);
+    const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
+    const bool has_splits = i1 > i0;
+    const int leaf_raw = c.leaf_state[row];
+    const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
+
+    // ---- active check ----
+    float v[VPT];
+    float amax = 0.f;
+    const float* rrow = a.acc + (size_t)row * S;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * NT;
+      v[k] = s < S ? rrow[s] : 0.f;
+      amax = fmaxf(amax, fabsf(v[k]));
     }
-  }
+    amax = block_max(amax, red);
+    const bool active = a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold);
+    if (!active) continue;
 
-  // ---- precompute ----
-  const float* pirow = a.Pi + (size_t)row * S;
-  const float rmax = a.row_max[row];
-  const float rms = safe_max(rmax);
-  float pp[VPT];
-  float psum = 0.f;
-  __syncthreads();
+    // ---- dts row (log) ----
+    float dv[VPT];
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    pp[k] = 0.f;
-    if (s < S) {
-      const float pi = pirow[s];
+    for (int k = 0; k < VPT; ++k) dv[k] = neg_inf();
+    if (has_splits) {
+      if (a.dts_saved) {
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          const int s = threadIdx.x + k * NT;
+          if (s < S) dv[k] = a.dts_saved[(size_t)row * S + s];
+        }
+      } else {
+        dts_row2<VPT>(c, a.Pi, a.Pibar, a.sp, i0, i1, pb, cc, T, U, dv);
+      }
+    }
+
+    // ---- precompute: p', path sums, self-loop coefficients ----
+    const float* pirow = a.Pi + (size_t)row * S;
+    const float* pbrow = a.Pibar + (size_t)row * S;
+    const float rms = safe_max(a.row_max[row]);
+    float pp[VPT];
+    float psum = 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * NT;
+      const float pi = s < S ? pirow[s] : neg_inf();
       P[s] = pi;
       float w = pi;
-      if (c.use_col) w += c.col[s];
-      pp[k] = ex2(w - rms);
-      B0[s] = pp[k];
-      B2[s] = 0.f;
+      if (c.use_col && s < S) w += c.col[s];
+      pp[k] = s < S ? ex2(w - rms) : 0.f;
       psum += pp[k];
     }
-  }
-  const float row_sum = block_sum(psum, red);
-  const float* anc = ancestor_sum_doubling(B0, B1, c.jumps, c.K, S);
-  float diag[VPT], coef[VPT];
-  const float* pbrow = a.Pibar + (size_t)row * S;
-  const float leafv = leaf >= 0 ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
+    for (int i = threadIdx.x; i < 2 * NTV; i += NT) T[i] = 0.f;  // tour buffer (T and U)
+    const float row_sum = block_sum(psum, red);
+    float anc[VPT];
+    tour_pathsums<VPT>(T, red, tr, pp, NTV, anc);
+    const float leafv = leaf >= 0 ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
+    float diag[VPT], coef[VPT];
+    float a3v[VPT], a4v[VPT];
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    diag[k] = coef[k] = 0.f;
-    if (s < S) {
-      const float pi = P[s];
-      const float t0 = c.dl[cb + s] + pi;
-      const float t1 = pi + c.ebar[cb + s];
-      const float t2 = pbrow[s] + c.e[cb + s];
-      const int ca = c.c1[s], cbb = c.c2[s];
-      const bool av = (unsigned)ca < (unsigned)S, bv = (unsigned)cbb < (unsigned)S;
-      const float t3 = c.sl1[cb + s] + (av ? P[ca] : neg_inf());
-      const float t4 = c.sl2[cb + s] + (bv ? P[cbb] : neg_inf());
-      const float t5 = (s == leaf) ? leafv : neg_inf();
-      const float m = fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5));
-      const float ms = safe_max(m);
-      const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
-                  e5 = ex2(t5 - ms);
-      const float ssum = e0 + e1 + e2 + e3 + e4 + e5;
-      const float inv_sum = ssum > 0.f ? 1.0f / ssum : 0.f;
-      float wL = 1.0f;
-      if (has_splits) {
-        const float dlv = lg2(ssum) + m;
-        const float pm = fmaxf(dlv, dv[k]);
-        const float pms = safe_max(pm);
-        const float pnew = lg2(ex2(dlv - pms) + ex2(dv[k] - pms)) + pm;
-        wL = is_neg_inf(dlv) ? 0.f : ex2(dlv - pnew);
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * NT;
+      diag[k] = coef[k] = a3v[k] = a4v[k] = 0.f;
+      if (s < S) {
+        const float pi = P[s];
+        const float t0 = c.dl[cb + s] + pi;
+        const float t1 = pi + c.ebar[cb + s];
+        const float t2 = pbrow[s] + c.e[cb + s];
+        const float t3 = c.sl1[cb + s] + P[lo16(cc[k])];
+        const float t4 = c.sl2[cb + s] + P[hi16(cc[k])];
+        const float t5 = (s == leaf) ? leafv : neg_inf();
+        const float m = fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5));
+        const float ms = safe_max(m);
+        const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
+                    e5 = ex2(t5 - ms);
+        const float ssum = e0 + e1 + e2 + e3 + e4 + e5;
+        const float inv_sum = ssum > 0.f ? 1.0f / ssum : 0.f;
+        float wL = 1.0f;
+        if (has_splits) {
+          const float dlv = lg2(ssum) + m;
+          const float pm = fmaxf(dlv, dv[k]);
+          const float pms = safe_max(pm);
+          const float pnew = lg2(ex2(dlv - pms) + ex2(dv[k] - pms)) + pm;
+          wL = is_neg_inf(dlv) ? 0.f : ex2(dlv - pnew);
+        }
+        const float denom = row_sum - anc[k];
+        const float inv_denom = denom > 0.f ? 1.0f / denom : 0.f;
+        diag[k] = wL * (e0 + e1) * inv_sum;
+        coef[k] = wL * e2 * inv_sum * inv_denom;
+        a3v[k] = wL * e3 * inv_sum;
+        a4v[k] = wL * e4 * inv_sum;
       }
-      const float denom = row_sum - anc[s];
-      const float inv_denom = denom > 0.f ? 1.0f / denom : 0.f;
-      diag[k] = wL * (e0 + e1) * inv_sum;
-      coef[k] = wL * e2 * inv_sum * inv_denom;
-      if (av) B2[ca] = wL * e3 * inv_sum;   // edge weight of child ca (B2 = EDGE)
-      if (bv) B2[cbb] = wL * e4 * inv_sum;
     }
-  }
-  __syncthreads();
-  float edge[VPT];
+    __syncthreads();  // everyone done with the tour scan results
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    edge[k] = 0.f;
-    if (s < S) {
-      const int par = c.parent[s];
-      edge[k] = ((unsigned)par < (unsigned)S) ? B2[s] : 0.f;
-      B0[s] = v[k];  // T: current Neumann term
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * NT;
+      T[s] = a3v[k];  // edge weight (speciation into child c1) of parent column s
+      U[s] = a4v[k];  // ... into child c2
     }
-  }
-
-  // ---- Neumann series: T in B0, u scan in B1 ----
-  float* T = B0;
-  float* U = B1;
-  for (int n = 0; n < a.neumann_terms; ++n) {
+    __syncthreads();
+    float edge[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const unsigned par = lo16(pa[k]);
+      edge[k] = hi16(pa[k]) ? T[par] : U[par];  // zero column for the root / padding
+    }
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      if (s < S) U[__ldg(c.pre + s)] = T[s] * coef[k];
-    }
-    const float A = block_exclusive_scan(U, S, red);
-    float nv[VPT];
+    for (int k = 0; k < VPT; ++k) T[threadIdx.x + k * NT] = v[k];
+
+    // ---- Neumann series: T current term, U preorder scan buffer ----
+    for (int n = 0; n < a.neumann_terms; ++n) {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      nv[k] = 0.f;
-      if (s < S) {
-        const int pe = __ldg(c.pre_end + s);
-        const float sub = (pe < S ? U[pe] : A) - U[__ldg(c.pre + s)];
-        const int par = c.parent[s];
-        const float pt = ((unsigned)par < (unsigned)S) ? T[par] : 0.f;
-        nv[k] = T[s] * diag[k] + pp[k] * (A - sub) + pt * edge[k];
+      for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = T[threadIdx.x + k * NT] * coef[k];
+      __syncthreads();
+      const float A = block_exclusive_scan_ch<VPT>(U, red);
+      float nv[VPT];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int s = threadIdx.x + k * NT;
+        const float sub = U[hi16(pk[k])] - U[lo16(pk[k])];
+        nv[k] = T[s] * diag[k] + pp[k] * (A - sub) + T[lo16(pa[k])] * edge[k];
         v[k] += nv[k];
       }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) T[threadIdx.x + k * NT] = nv[k];
     }
+    if (a.v_out) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int s = threadIdx.x + k * NT;
+        if (s < S) a.v_out[(size_t)row * S + s] = v[k];
+      }
+    }
+
+    // ---- column gradient of the self-loop Pibar term ----
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      if (s < S) T[s] = nv[k];
+    for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = v[k] * coef[k];
+    __syncthreads();
+    {
+      const float A = block_exclusive_scan_ch<VPT>(U, red);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int s = threadIdx.x + k * NT;
+        const float sub = U[hi16(pk[k])] - U[lo16(pk[k])];
+        ACC[G_COL * NTV + s] += pp[k] * (A - sub);
+      }
     }
-  }
 
-  if (a.v_out) {
+    // ---- parameter cotangents of the self-loop (terms recomputed) ----
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      if (s < S) a.v_out[(size_t)row * S + s] = v[k];
-    }
-  }
-
-  // ---- column gradient of the self-loop Pibar term ----
-  float colacc[VPT];
-  __syncthreads();
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    if (s < S) U[__ldg(c.pre + s)] = v[k] * coef[k];
-  }
-  {
-    const float A = block_exclusive_scan(U, S, red);
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      colacc[k] = 0.f;
+      const int s = threadIdx.x + k * NT;
       if (s < S) {
-        const int pe = __ldg(c.pre_end + s);
-        colacc[k] = pp[k] * (A - ((pe < S ? U[pe] : A) - U[__ldg(c.pre + s)]));
-      }
-    }
-  }
-
-  // ---- parameter cotangents of the self-loop (recomputes the terms) ----
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    if (s < S) {
-      const float pi = P[s];
-      const float t0 = c.dl[cb + s] + pi;
-      const float t1 = pi + c.ebar[cb + s];
-      const float t2 = pbrow[s] + c.e[cb + s];
-      const int ca = c.c1[s], cbb = c.c2[s];
-      const float t3 = c.sl1[cb + s] + (((unsigned)ca < (unsigned)S) ? P[ca] : neg_inf());
-      const float t4 = c.sl2[cb + s] + (((unsigned)cbb < (unsigned)S) ? P[cbb] : neg_inf());
-      const float t5 = (s == leaf) ? leafv : neg_inf();
-      const float m = fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5));
-      const float ms = safe_max(m);
-      const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
-                  e5 = ex2(t5 - ms);
-      const float ssum = e0 + e1 + e2 + e3 + e4 + e5;
-      const float inv_sum = ssum > 0.f ? 1.0f / ssum : 0.f;
-      float wL = 1.0f;
-      if (has_splits) {
-        const float dlv = lg2(ssum) + m;
-        const float pm = fmaxf(dlv, dv[k]);
-        const float pms = safe_max(pm);
-        const float pnew = lg2(ex2(dlv - pms) + ex2(dv[k] - pms)) + pm;
-        wL = is_neg_inf(dlv) ? 0.f : ex2(dlv - pnew);
-      }
-      const float alpha = v[k] * wL;
-      double* g = a.gacc;
-      atomicAdd(g + 0 * (size_t)S + s, (double)(alpha * e0 * inv_sum));
-      atomicAdd(g + 1 * (size_t)S + s, (double)(alpha * e1 * inv_sum));
-      atomicAdd(g + 2 * (size_t)S + s, (double)(alpha * e2 * inv_sum));
-      atomicAdd(g + 3 * (size_t)S + s, (double)(alpha * e3 * inv_sum));
-      atomicAdd(g + 4 * (size_t)S + s, (double)(alpha * e4 * inv_sum));
-      if (leaf >= 0) atomicAdd(g + 5 * (size_t)S + s, (double)(alpha * e5 * inv_sum));
-    }
-  }
-
-  // ---- splits: cotangents of the split reduction + Pibar VJP trees ----
-  float dD[VPT], dS[VPT], dM[VPT];
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) dD[k] = dS[k] = dM[k] = 0.f;
-  float pip[VPT];
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    pip[k] = s < S ? pirow[s] : neg_inf();
-  }
-  // buffers in the split phase: B0/B1 child Pi rows, B2/B3 speciation cotangents (vd3, vd4),
-  // B4/P the left/right Pibar u_d in preorder positions (scanned in place)
-  for (long long i = i0; i < i1; ++i) {
-    const long long l = a.sp.sl[i], r = a.sp.sr[i];
-    const float lsp = a.sp.lsp[i];
-    const float* pil = a.Pi + (size_t)l * S;
-    const float* pir = a.Pi + (size_t)r * S;
-    const float* pbl = a.Pibar + (size_t)l * S;
-    const float* pbr = a.Pibar + (size_t)r * S;
-    const float rml = a.row_max[l], rmr = a.row_max[r];
-    const float rmls = safe_max(rml), rmrs = safe_max(rmr);
-    const size_t mcl = (size_t)(c.item_idx[l] * c.crs), mcr = (size_t)(c.item_idx[r] * c.crs);
-    __syncthreads();
-    for (int s = threadIdx.x; s < S; s += blockDim.x) {
-      B0[s] = pil[s];
-      B1[s] = pir[s];
-    }
-    __syncthreads();
-    float cl[VPT], cr[VPT], ppl[VPT], ppr[VPT];
-    float sabs_l = 0.f, sabs_r = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * blockDim.x;
-      cl[k] = cr[k] = ppl[k] = ppr[k] = 0.f;
-      if (s < S) {
-        const float pl = B0[s], pr = B1[s];
-        const float ld = c.log_pD[pb + s];
-        const float ls = c.log_pS[pb + s];
-        const int ca = c.c1[s], cbb = c.c2[s];
-        const bool av = (unsigned)ca < (unsigned)S, bv = (unsigned)cbb < (unsigned)S;
-        const float d0 = ld + pl + pr;
-        const float d1 = pl + pbr[s];
-        const float d2 = pr + pbl[s];
-        const float d3 = ls + (av ? B0[ca] : neg_inf()) + (bv ? B1[cbb] : neg_inf());
-        const float d4 = ls + (av ? B1[ca] : neg_inf()) + (bv ? B0[cbb] : neg_inf());
-        const float ppar = pip[k];
-        const bool pv = !is_neg_inf(ppar);
-        const float vd0 = v[k] * (pv ? ex2(lsp + d0 - ppar) : 0.f);
-        const float vd1 = v[k] * (pv ? ex2(lsp + d1 - ppar) : 0.f);
-        const float vd2 = v[k] * (pv ? ex2(lsp + d2 - ppar) : 0.f);
-        const float vd3 = v[k] * (pv ? ex2(lsp + d3 - ppar) : 0.f);
-        const float vd4 = v[k] * (pv ? ex2(lsp + d4 - ppar) : 0.f);
-        dD[k] += vd0;
-        dS[k] += vd3 + vd4;
-        dM[k] += vd1 + vd2;
-        cl[k] = vd0 + vd1;
-        cr[k] = vd0 + vd2;
-        B2[s] = vd3;
-        B3[s] = vd4;
-        const float bl = pbl[s], br = pbr[s];
-        const float udl = is_neg_inf(bl) ? 0.f : vd2 * ex2(rml + c.mc[mcl + s] - bl);
-        const float udr = is_neg_inf(br) ? 0.f : vd1 * ex2(rmr + c.mc[mcr + s] - br);
-        const int ps = __ldg(c.pre + s);
-        B4[ps] = udl;
-        P[ps] = udr;
-        sabs_l += fabsf(udl);
-        sabs_r += fabsf(udr);
-        float wl = pl, wr = pr;
-        if (c.use_col) { wl += c.col[s]; wr += c.col[s]; }
-        ppl[k] = ex2(wl - rmls);
-        ppr[k] = ex2(wr - rmrs);
-      }
-    }
-    bool side_l = true, side_r = true;
-    if (a.side_thr_enabled) {
-      sabs_l = block_sum(sabs_l, red);
-      sabs_r = block_sum(sabs_r, red);
-      side_l = sabs_l > a.side_thr;
-      side_r = sabs_r > a.side_thr;
-    }
-    float Al, Ar;
-    block_exclusive_scan2(B4, P, S, red, Al, Ar);
-    float* rl = a.acc + (size_t)l * S;
-    float* rr = a.acc + (size_t)r * S;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int x = threadIdx.x + k * blockDim.x;
-      if (x < S) {
-        const int par = c.parent[x];
-        float sl_ = 0.f, sr_ = 0.f;
-        if ((unsigned)par < (unsigned)S) {
-          const bool first = c.c1[par] == x;
-          sl_ = first ? B2[par] : B3[par];
-          sr_ = first ? B3[par] : B2[par];
+        const float pi = P[s];
+        const float t0 = c.dl[cb + s] + pi;
+        const float t1 = pi + c.ebar[cb + s];
+        const float t2 = pbrow[s] + c.e[cb + s];
+        const float t3 = c.sl1[cb + s] + P[lo16(cc[k])];
+        const float t4 = c.sl2[cb + s] + P[hi16(cc[k])];
+        const float t5 = (s == leaf) ? leafv : neg_inf();
+        const float m = fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5));
+        const float ms = safe_max(m);
+        const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
+                    e5 = ex2(t5 - ms);
+        const float ssum = e0 + e1 + e2 + e3 + e4 + e5;
+        const float inv_sum = ssum > 0.f ? 1.0f / ssum : 0.f;
+        float wL = 1.0f;
+        if (has_splits) {
+          const float dlv = lg2(ssum) + m;
+          const float pm = fmaxf(dlv, dv[k]);
+          const float pms = safe_max(pm);
+          const float pnew = lg2(ex2(dlv - pms) + ex2(dv[k] - pms)) + pm;
+          wL = is_neg_inf(dlv) ? 0.f : ex2(dlv - pnew);
         }
-        const int ps = __ldg(c.pre + x), pe = __ldg(c.pre_end + x);
-        float tl_ = 0.f, tr_ = 0.f;
-        if (side_l) tl_ = ppl[k] * (Al - ((pe < S ? B4[pe] : Al) - B4[ps]));
-        if (side_r) tr_ = ppr[k] * (Ar - ((pe < S ? P[pe] : Ar) - P[ps]));
-        colacc[k] += tl_ + tr_;
-        atomicAdd(rl + x, cl[k] + sl_ + tl_);
-        atomicAdd(rr + x, cr[k] + sr_ + tr_);
+        const float alpha = v[k] * wL;
+        const float q0 = alpha * e0 * inv_sum, q1 = alpha * e1 * inv_sum, q2 = alpha * e2 * inv_sum;
+        const float q3 = alpha * e3 * inv_sum, q4 = alpha * e4 * inv_sum, q5 = alpha * e5 * inv_sum;
+        ACC[G_PD * NTV + s] += q0;
+        ACC[G_PS * NTV + s] += q3 + q4 + q5;
+        ACC[G_MT * NTV + s] += q2;
+        ACC[G_E * NTV + s] += q0 + q2;
+        ACC[G_EBAR * NTV + s] += q1;
+        ACC[G_ES1 * NTV + s] += q4;
+        ACC[G_ES2 * NTV + s] += q3;
+      }
+    }
+
+    // ---- splits: cotangents of the split reduction and the Pibar VJP trees ----
+    if (has_splits) {
+      float pip[VPT];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) pip[k] = P[threadIdx.x + k * NT];
+      for (long long i = i0; i < i1; ++i) {
+        const long long l = a.sp.sl[i], r = a.sp.sr[i];
+        const float lsp = a.sp.lsp[i];
+        const float* pil = a.Pi + (size_t)l * S;
+        const float* pir = a.Pi + (size_t)r * S;
+        const float* pbl = a.Pibar + (size_t)l * S;
+        const float* pbr = a.Pibar + (size_t)r * S;
+        const float rml = a.row_max[l], rmr = a.row_max[r];
+        const size_t mcl = (size_t)(c.item_idx[l] * c.crs), mcr = (size_t)(c.item_idx[r] * c.crs);
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          const int s = threadIdx.x + k * NT;
+          T[s] = s < S ? pil[s] : neg_inf();
+          U[s] = s < S ? pir[s] : neg_inf();
+        }
+        __syncthreads();
+        float cl[VPT], cr[VPT], v4r[VPT], udl[VPT], udr[VPT];
+        float sabs_l = 0.f, sabs_r = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          const int s = threadIdx.x + k * NT;
+          cl[k] = cr[k] = v4r[k] = udl[k] = udr[k] = 0.f;
+          float v3 = 0.f;
+          if (s < S) {
+            const float pl = T[s], pr = U[s];
+            const float ld = c.log_pD[pb + s];
+            const float ls = c.log_pS[pb + s];
+            const unsigned ca = lo16(cc[k]), cbb = hi16(cc[k]);
+            const float d0 = ld + pl + pr;
+            const float d1 = pl + pbr[s];
+            const float d2 = pr + pbl[s];
+            const float d3 = ls + T[ca] + U[cbb];
+            const float d4 = ls + U[ca] + T[cbb];
+            const float ppar = pip[k];
+            const bool pv = !is_neg_inf(ppar);
+            const float vd0 = v[k] * (pv ? ex2(lsp + d0 - ppar) : 0.f);
+            const float vd1 = v[k] * (pv ? ex2(lsp + d1 - ppar) : 0.f);
+            const float vd2 = v[k] * (pv ? ex2(lsp + d2 - ppar) : 0.f);
+            v3 = v[k] * (pv ? ex2(lsp + d3 - ppar) : 0.f);
+            v4r[k] = v[k] * (pv ? ex2(lsp + d4 - ppar) : 0.f);
+            ACC[G_PD * NTV + s] += vd0;
+            ACC[G_PS * NTV + s] += v3 + v4r[k];
+            ACC[G_MT * NTV + s] += vd1 + vd2;
+            cl[k] = vd0 + vd1;
+            cr[k] = vd0 + vd2;
+            const float bl = pbl[s], br = pbr[s];
+            udl[k] = is_neg_inf(bl) ? 0.f : vd2 * ex2(rml + c.mc[mcl + s] - bl);
+            udr[k] = is_neg_inf(br) ? 0.f : vd1 * ex2(rmr + c.mc[mcr + s] - br);
+            sabs_l += fabsf(udl[k]);
+            sabs_r += fabsf(udr[k]);
+          }
+          P[s] = v3;  // P no longer holds Pi (pip registers do)
+        }
+        bool side_l = true, side_r = true;
+        if (a.side_thr_enabled) {
+          sabs_l = block_sum(sabs_l, red);
+          sabs_r = block_sum(sabs_r, red);
+          side_l = sabs_l > a.side_thr;
+          side_r = sabs_r > a.side_thr;
+        }
+        __syncthreads();  // staged child rows no longer read
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          T[threadIdx.x + k * NT] = v4r[k];
+          U[lo16(pk[k])] = udl[k];
+        }
+        __syncthreads();
+        float* rl = a.acc + (size_t)l * S;
+        float* rr = a.acc + (size_t)r * S;
+        const float rmls = safe_max(rml), rmrs = safe_max(rmr);
+        {  // left side
+          const float A = block_exclusive_scan_ch<VPT>(U, red);
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            const int x = threadIdx.x + k * NT;
+            if (x < S) {
+              const unsigned par = lo16(pa[k]);
+              const float st = hi16(pa[k]) ? P[par] : T[par];
+              float tl = 0.f;
+              if (side_l) {
+                float w = pil[x];
+                if (c.use_col) w += c.col[x];
+                tl = ex2(w - rmls) * (A - (U[hi16(pk[k])] - U[lo16(pk[k])]));
+              }
+              ACC[G_COL * NTV + x] += tl;
+              atomicAdd(rl + x, cl[k] + st + tl);
+            }
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = udr[k];
+        __syncthreads();
+        {  // right side
+          const float A = block_exclusive_scan_ch<VPT>(U, red);
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            const int x = threadIdx.x + k * NT;
+            if (x < S) {
+              const unsigned par = lo16(pa[k]);
+              const float st = hi16(pa[k]) ? T[par] : P[par];
+              float tr_ = 0.f;
+              if (side_r) {
+                float w = pir[x];
+                if (c.use_col) w += c.col[x];
+                tr_ = ex2(w - rmrs) * (A - (U[hi16(pk[k])] - U[lo16(pk[k])]));
+              }
+              ACC[G_COL * NTV + x] += tr_;
+              atomicAdd(rr + x, cr[k] + st + tr_);
+            }
+          }
+        }
       }
     }
   }
-  double* g = a.gacc;
+  // ---- flush this CTA's column sums into its fp64 slot ----
+  double* slot = a.slots + (size_t)blockIdx.x * G_N * NTV;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int s = threadIdx.x + k * blockDim.x;
-    if (s < S) {
-      if (has_splits) {
-        atomicAdd(g + 6 * (size_t)S + s, (double)dD[k]);
-        atomicAdd(g + 7 * (size_t)S + s, (double)dS[k]);
-        atomicAdd(g + 8 * (size_t)S + s, (double)dM[k]);
-      }
-      atomicAdd(g + 9 * (size_t)S + s, (double)colacc[k]);
-    }
+    const int s = threadIdx.x + k * NT;
+#pragma unroll
+    for (int j = 0; j < G_N; ++j) slot[(size_t)j * NTV + s] += (double)ACC[j * NTV + s];
   }
 }
 
-__global__ void finalize_grads_kernel(const double* __restrict__ g, int S, float* gpD, float* gpS, float* gmt,
-                                      float* gE, float* gEbar, float* gEs1, float* gEs2, float* gcol) {
+// Fixed-order sum of the per-CTA slots -> the eight fp32 cotangent vectors.
+__global__ void reduce_slots_kernel(const double* __restrict__ slots, int n_slots, int NTV, int S, float* out) {
+  const int j = blockIdx.y;
   for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < S; s += gridDim.x * blockDim.x) {
-    const double a0 = g[s], a1 = g[S + s], a2 = g[2 * S + s], a3 = g[3 * S + s], a4 = g[4 * S + s],
-                 a5 = g[5 * S + s], dD = g[6 * S + s], dS = g[7 * S + s], dM = g[8 * S + s], col = g[9 * S + s];
-    gpD[s] = (float)(a0 + dD);
-    gpS[s] = (float)(a3 + a4 + a5 + dS);
-    gmt[s] = (float)(a2 + dM);
-    gE[s] = (float)(a0 + a2);
-    gEbar[s] = (float)a1;
-    gEs1[s] = (float)a4;
-    gEs2[s] = (float)a3;
-    gcol[s] = (float)col;
+    double t = 0.0;
+    for (int b = 0; b < n_slots; ++b) t += slots[((size_t)b * G_N + j) * NTV + s];
+    out[(size_t)j * S + s] = (float)t;
   }
 }
 
@@ -819,6 +911,29 @@ __global__ void lin_consts_kernel(const float* dl, const float* ebar, const floa
     C1[i] = ex2(sl1[i]);
     C2[i] = ex2(sl2[i]);
   }
+}
+
+// Threads per CTA and columns per thread of the padded-row kernels; bd * vpt >= S + 1 leaves a
+// zero padding column (mirrors kbench_b200/tree.py engine_width).
+int engine_width(int S, int& bd) {
+  bd = S > 1024 ? 1024 : ((S + 31) / 32) * 32;
+  if (bd < 32) bd = 32;
+  const int v0 = (S + bd - 1) / bd;
+  int v = v0 <= 1 ? 1 : v0 <= 2 ? 2 : v0 <= 4 ? 4 : 8;
+  if (bd * v < S + 1) v *= 2;
+  return v;
+}
+
+// Up to 1024 threads per row (4 columns per thread at S = 4095).
+int vpt_pick_wide(int S, int& bd) {
+  bd = 1024;
+  if (S <= 1024) bd = ((S + 31) / 32) * 32;
+  if (bd < 32) bd = 32;
+  const int v = (S + bd - 1) / bd;
+  if (v <= 1) return 1;
+  if (v <= 2) return 2;
+  if (v <= 4) return 4;
+  return 8;
 }
 
 int vpt_pick(int S, int& bd) {
@@ -838,13 +953,14 @@ LevelConsts make_lc(const float* mc, const float* dl, const float* ebar, const f
                     const float* linC1, const float* linC2, const float* log_pD, const float* log_pS,
                     long long prs, long long crs, const float* col, int use_col, const int* parent, const int* c1,
                     const int* c2, const int* pre, const int* pre_end, const int* sub_start, const int* sub_end,
-                    const int* jumps, int K, const long long* item_idx, const int* leaf_state, int S) {
+                    const int* jumps, int K, const long long* item_idx, const int* leaf_state,
+                    const unsigned* packed, int S) {
   LevelConsts c;
   c.mc = mc; c.dl = dl; c.ebar = ebar; c.e = e; c.sl1 = sl1; c.sl2 = sl2; c.leaf_logp = leaf_logp;
   c.linA = linA; c.linB = linB; c.linC1 = linC1; c.linC2 = linC2; c.log_pD = log_pD; c.log_pS = log_pS;
   c.prs = prs; c.crs = crs; c.col = col; c.use_col = use_col; c.parent = parent; c.c1 = c1; c.c2 = c2;
   c.pre = pre; c.pre_end = pre_end; c.sub_start = sub_start; c.sub_end = sub_end; c.jumps = jumps; c.K = K;
-  c.item_idx = item_idx; c.leaf_state = leaf_state; c.S = S;
+  c.item_idx = item_idx; c.leaf_state = leaf_state; c.packed = packed; c.S = S;
   return c;
 }
 
@@ -870,8 +986,8 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
                                 long long const_row_stride, const float* col_log_probs, int use_col_weights,
                                 const int* node_parent, const int* node_child1, const int* node_child2,
                                 const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
-                                const long long* item_idx, const int* leaf_state, int pi_iters, int S,
-                                void* stream) {
+                                const long long* item_idx, const int* leaf_state, const unsigned* packed,
+                                int pi_iters, int S, void* stream) {
   if (S <= 0 || n_rows < 0 || K < 0 || pi_iters < 2) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
@@ -879,14 +995,14 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, linA, linB, linC1, linC2, log_pD, log_pS, param_row_stride,
                 const_row_stride, col_log_probs, use_col_weights, node_parent, node_child1, node_child2,
                 node_subtree_start, node_subtree_end, node_subtree_start, node_subtree_end, jumps, K, item_idx,
-                leaf_state, S);
+                leaf_state, packed, S);
   a.sp = SplitCSR{rows, split_ptr, sl, sr, lsp};
   a.Pi_src = Pi_src; a.Pibar_src = Pibar_src; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = n_rows;
   a.pi_iters = pi_iters;
   int bd;
-  const int vpt = vpt_pick(S, bd);
-  const size_t smem = (size_t)(3 * S + 128) * sizeof(float);
+  const int vpt = vpt_pick_wide(S, bd);
+  const size_t smem = (size_t)(bd * 2 * vpt + bd * vpt + 128) * sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
 #define KB_LF_CASE(V)                                                                                     \
   case V:                                                                                                 \
@@ -896,7 +1012,7 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
     level_forward_kernel<V><<<n_rows, bd, smem, st>>>(a);                                                 \
     break;
   switch (vpt) {
-    KB_LF_CASE(1) KB_LF_CASE(2) KB_LF_CASE(4) KB_LF_CASE(8) KB_LF_CASE(16)
+    KB_LF_CASE(1) KB_LF_CASE(2) KB_LF_CASE(4) KB_LF_CASE(8)
     default: return KB_ERR_SIZE;
   }
 #undef KB_LF_CASE
@@ -906,50 +1022,52 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
 extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                                  const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
                                  const float* pibar_row_max, const float* dts_saved, float* accumulated_rhs,
-                                 float* v_out, double* grad_acc, float threshold, int strict_gt, float side_threshold,
-                                 int side_threshold_enabled, int neumann_terms, const float* mc, const float* dl,
-                                 const float* ebar, const float* e, const float* sl1, const float* sl2,
-                                 const float* leaf_logp, const float* log_pD, const float* log_pS,
-                                 long long param_row_stride, long long const_row_stride, const float* col_log_probs,
-                                 int use_col_weights, const int* node_parent, const int* node_child1,
-                                 const int* node_child2, const int* node_pre, const int* node_pre_end,
-                                 const int* jumps, int K, const long long* item_idx, const int* leaf_state, int S,
-                                 void* stream) {
-  if (S <= 0 || n_rows < 0 || K < 0 || neumann_terms < 0) return KB_ERR_ARG;
+                                 float* v_out, double* grad_slots, int n_slots, float threshold, int strict_gt,
+                                 float side_threshold, int side_threshold_enabled, int neumann_terms,
+                                 const float* mc, const float* dl, const float* ebar, const float* e,
+                                 const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
+                                 const float* log_pS, long long param_row_stride, long long const_row_stride,
+                                 const float* col_log_probs, int use_col_weights, const long long* item_idx,
+                                 const int* leaf_state, const unsigned* packed_padded, int S, void* stream) {
+  if (S <= 0 || n_rows < 0 || neumann_terms < 0 || n_slots <= 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
   BwdArgs a;
   a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, nullptr, nullptr, nullptr, nullptr, log_pD, log_pS,
-                param_row_stride, const_row_stride, col_log_probs, use_col_weights, node_parent, node_child1,
-                node_child2, node_pre, node_pre_end, nullptr, nullptr, jumps, K, item_idx, leaf_state, S);
+                param_row_stride, const_row_stride, col_log_probs, use_col_weights, nullptr, nullptr, nullptr,
+                nullptr, nullptr, nullptr, nullptr, nullptr, 0, item_idx, leaf_state, packed_padded, S);
   a.sp = SplitCSR{rows, split_ptr, sl, sr, lsp};
   a.Pi = Pi; a.Pibar = Pibar; a.row_max = pibar_row_max; a.dts_saved = dts_saved; a.acc = accumulated_rhs;
-  a.v_out = v_out; a.gacc = grad_acc; a.threshold = threshold; a.strict_gt = strict_gt; a.side_thr = side_threshold;
-  a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms; a.n_rows = n_rows;
+  a.v_out = v_out; a.slots = grad_slots; a.threshold = threshold; a.strict_gt = strict_gt;
+  a.side_thr = side_threshold; a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms;
+  a.n_rows = n_rows;
   int bd;
-  const int vpt = vpt_pick(S, bd);
-  const size_t smem = (size_t)(6 * S + 128) * sizeof(float);
+  const int vpt = engine_width(S, bd);
+  const int ntv = bd * vpt;
+  const size_t smem = (size_t)((3 + G_N) * ntv + 128) * sizeof(float);
+  const int grid = n_rows < n_slots ? n_rows : n_slots;
   cudaStream_t st = (cudaStream_t)stream;
 #define KB_LB_CASE(V)                                                                                      \
   case V:                                                                                                  \
     if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_backward_kernel<V>,                   \
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))  \
       return KB_ERR_LAUNCH;                                                                                \
-    level_backward_kernel<V><<<n_rows, bd, smem, st>>>(a);                                                 \
+    level_backward_kernel<V><<<grid, bd, smem, st>>>(a);                                                   \
     break;
   switch (vpt) {
-    KB_LB_CASE(1) KB_LB_CASE(2) KB_LB_CASE(4) KB_LB_CASE(8) KB_LB_CASE(16)
+    KB_LB_CASE(1) KB_LB_CASE(2) KB_LB_CASE(4) KB_LB_CASE(8)
     default: return KB_ERR_SIZE;
   }
 #undef KB_LB_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
 
-extern "C" int kb_finalize_grads(const double* grad_acc, int S, float* grad_log_pD, float* grad_log_pS,
-                                 float* grad_mt, float* grad_E, float* grad_Ebar, float* grad_E_s1, float* grad_E_s2,
-                                 float* grad_col, void* stream) {
-  if (S <= 0) return KB_ERR_ARG;
-  finalize_grads_kernel<<<(S + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
-      grad_acc, S, grad_log_pD, grad_log_pS, grad_mt, grad_E, grad_Ebar, grad_E_s1, grad_E_s2, grad_col);
+extern "C" int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S, float* out8, void* stream) {
+  if (S <= 0 || n_slots <= 0) return KB_ERR_ARG;
+  int bd;
+  const int vpt = engine_width(S, bd);
+  dim3 grid((S + 255) / 256, G_N);
+  reduce_slots_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(grad_slots, n_slots, bd * vpt, S, out8);
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
+

@@ -94,6 +94,16 @@ def build_plan(static) -> LevelPlan:
     return plan
 
 
+_SM_COUNT: dict = {}
+
+
+def _sm_count(dev) -> int:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = int(torch.cuda.get_device_properties(idx).multi_processor_count)
+    return _SM_COUNT[idx]
+
+
 def supported(static) -> bool:
     return bool(static.statewise) and not bool(static.itemwise)
 
@@ -199,7 +209,8 @@ def forward(static, theta, col_weights, *, pi_residual_out=None):
                   lin[0].data_ptr(), lin[1].data_ptr(), lin[2].data_ptr(), lin[3].data_ptr(), pDp.data_ptr(),
                   pSp.data_ptr(), prs, crs, f32(clp).data_ptr(), int(ucw), tt.parent.data_ptr(),
                   tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
-                  tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), int(so.pi_iters), S, st)
+                  tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed.data_ptr(),
+                  int(so.pi_iters), S, st)
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
     return out, {"dts_wave": dts}
@@ -230,7 +241,9 @@ def backward(static, theta, col_weights, saved, *, v_out=None):
     acc = torch.zeros((C, S), device=dev, dtype=torch.float32)
     roots = wl["root_row_ids"]
     acc.index_copy_(0, roots, glue.root_rhs(Pi, roots))
-    gacc = torch.zeros((10, S), device=dev, dtype=torch.float64)
+    n_slots = _sm_count(dev)
+    bd, vpt = tree.engine_width(S)
+    slots = torch.zeros((n_slots, 8, bd * vpt), device=dev, dtype=torch.float64)
     dts = saved.get("dts_wave")
     leaf_state = i32(wl["leaf_state_index"])
     item_idx = i64(static.rate_item_idx)
@@ -247,17 +260,18 @@ def backward(static, theta, col_weights, saved, *, v_out=None):
         if b == a:
             continue
         _launch(static, "kb_level_backward", L, rows_ptr + 4 * a, sp_ptr + 8 * a, b - a, plan.sl.data_ptr(),
-                  plan.sr.data_ptr(), plan.lsp.data_ptr(), Pi.data_ptr(), Pibar.data_ptr(), row_max.data_ptr(),
-                  _lib.ptr(dts), acc.data_ptr(), _lib.ptr(v_out), gacc.data_ptr(), thr, int(not so.use_adjoint_pruning), side_thr,
-                  int(side_thr > 0.0), int(so.neumann_terms), k["mc"].data_ptr(), k["dl"].data_ptr(),
-                  k["ebar"].data_ptr(), k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(),
-                  k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
-                  tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(),
-                  topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(),
-                  S, st)
+                plan.sr.data_ptr(), plan.lsp.data_ptr(), Pi.data_ptr(), Pibar.data_ptr(), row_max.data_ptr(),
+                _lib.ptr(dts), acc.data_ptr(), _lib.ptr(v_out), slots.data_ptr(), n_slots, thr,
+                int(not so.use_adjoint_pruning), side_thr, int(side_thr > 0.0), int(so.neumann_terms),
+                k["mc"].data_ptr(), k["dl"].data_ptr(), k["ebar"].data_ptr(), k["e"].data_ptr(),
+                k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(),
+                prs, crs, clp.data_ptr(), int(ucw), item_idx.data_ptr(), leaf_state.data_ptr(),
+                tt.packed_pad.data_ptr(), S, st)
     static._last_acc = acc
-    static._last_gacc = gacc
+    out8 = torch.empty((8, S), device=dev, dtype=torch.float32)
+    _lib.call("kb_reduce_grad_slots", slots.data_ptr(), n_slots, S, out8.data_ptr(), st)
     g = glue.GradAccumulators(E, S, dev)
-    _lib.call("kb_finalize_grads", gacc.data_ptr(), S, g.pD.data_ptr(), g.pS.data_ptr(), g.mt.data_ptr(),
-              g.E.data_ptr(), g.Ebar.data_ptr(), g.E_s1.data_ptr(), g.E_s2.data_ptr(), g.col.data_ptr(), st)
+    for j, name in enumerate(("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2")):
+        getattr(g, name)[0].copy_(out8[j])
+    g.col.copy_(out8[7])
     return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)

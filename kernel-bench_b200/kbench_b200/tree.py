@@ -29,6 +29,77 @@ class TreeTables:
     lv_c1: torch.Tensor | None
     lv_c2: torch.Tensor | None
     n_levels: int
+    packed: torch.Tensor | None = None  # [4,S] uint32 per-column tables, see pack_columns()
+
+
+_CACHE: dict = {}
+NONE16 = 0xFFFF
+
+
+def engine_width(S: int) -> tuple[int, int]:
+    """(threads per CTA, columns per thread) of the engine kernels; their product is the padded row
+    width NTV >= S + 1 (S is odd for a binary tree, NTV is even)."""
+    bd = 1024 if S > 1024 else max(32, ((S + 31) // 32) * 32)
+    v = (S + bd - 1) // bd
+    vpt = 1 if v <= 1 else 2 if v <= 2 else 4 if v <= 4 else 8
+    if bd * vpt < S + 1:  # keep a zero padding column
+        vpt *= 2
+    return bd, vpt
+
+
+def pack_columns(parent, child1, child2, sub_start, sub_end, ntv=None):
+    """Per-column 32-bit tables (two 16-bit fields each) read once per CTA by the engine kernels:
+
+    row 0  children:   c1 | c2 << 16            (0xFFFF = no child)
+    row 1  Euler tour: enter | exit << 16        positions in the 2S-long tour (+P at enter,
+                                                 -P at exit), so the inclusive prefix at enter(x)
+                                                 is the ancestor-or-self path sum of x
+    row 2  preorder:   pre | pre_end << 16       subtree of x = preorder range [pre, pre_end)
+    row 3  parent:     parent | (x is the parent's first child) << 16   (0xFFFF = root)
+    """
+    import numpy as np
+    par = np.asarray(parent, dtype=np.int64)
+    c1 = np.asarray(child1, dtype=np.int64)
+    c2 = np.asarray(child2, dtype=np.int64)
+    pre = np.asarray(sub_start, dtype=np.int64)
+    pre_end = np.asarray(sub_end, dtype=np.int64)
+    S = par.shape[0]
+    if S >= NONE16:
+        raise ValueError("packed column tables need S < 65535")
+    depth = np.zeros(S, dtype=np.int64)
+    order = np.argsort(pre)  # preorder: parents before children
+    for x in order:
+        p = par[x]
+        if 0 <= p < S:
+            depth[x] = depth[p] + 1
+    size = pre_end - pre
+    enter = 2 * pre - depth
+    exit_ = 2 * (pre + size) - depth - 1
+    v1 = np.where((c1 >= 0) & (c1 < S), c1, NONE16)
+    v2 = np.where((c2 >= 0) & (c2 < S), c2, NONE16)
+    pv = np.where((par >= 0) & (par < S), par, NONE16)
+    first = np.zeros(S, dtype=np.int64)
+    ok = pv != NONE16
+    first[ok] = (c1[par[ok]] == np.nonzero(ok)[0]).astype(np.int64)
+    out = np.stack([v1 | (v2 << 16), enter | (exit_ << 16), pre | (pre_end << 16), pv | (first << 16)])
+    if ntv is not None:
+        # padded columns S..ntv-1 (always zero in the kernels): children/parent point at the zero
+        # column Z = ntv-1, tour slots 2S.. and preorder slots S.. are their own
+        Z = ntv - 1
+        pad = np.arange(S, ntv, dtype=np.int64)
+        ext = np.stack([Z | (Z << 16) + 0 * pad,
+                        (2 * pad) | ((2 * pad + 1) << 16),
+                        pad | (pad << 16),
+                        Z + 0 * pad])
+        real = out.copy()
+        # real columns: invalid child / parent -> Z
+        c1f = np.where(v1 == NONE16, Z, v1)
+        c2f = np.where(v2 == NONE16, Z, v2)
+        pf = np.where(pv == NONE16, Z, pv)
+        real[0] = c1f | (c2f << 16)
+        real[3] = pf | (first << 16)
+        out = np.concatenate([real, ext], axis=1)
+    return out.astype(np.uint32).view(np.int32)
 
 
 _CACHE: dict = {}
@@ -109,8 +180,16 @@ def derive_levels(node_parent, node_child1, node_child2):
 
 
 def from_helpers(sh: dict) -> TreeTables:
-    return tables(sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]),
-                  compact_level_ptr=sh.get("compact_level_ptr"),
-                  compact_level_parents=sh.get("compact_level_parents"),
-                  compact_level_child1=sh.get("compact_level_child1"),
-                  compact_level_child2=sh.get("compact_level_child2"))
+    tt = tables(sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]),
+                compact_level_ptr=sh.get("compact_level_ptr"),
+                compact_level_parents=sh.get("compact_level_parents"),
+                compact_level_child1=sh.get("compact_level_child1"),
+                compact_level_child2=sh.get("compact_level_child2"))
+    if tt.packed is None:
+        arrs = [sh[k].detach().cpu().numpy() for k in ("node_parent", "node_child1", "node_child2",
+                                                        "node_subtree_start", "node_subtree_end")]
+        dev = sh["node_parent"].device
+        tt.packed = torch.from_numpy(pack_columns(*arrs)).to(dev).contiguous()
+        bd, vpt = engine_width(int(sh["S"]))
+        tt.packed_pad = torch.from_numpy(pack_columns(*arrs, ntv=bd * vpt)).to(dev).contiguous()
+    return tt
