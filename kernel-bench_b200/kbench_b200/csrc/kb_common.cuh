@@ -296,3 +296,70 @@ __device__ __forceinline__ void block_max_minpos_sum(float& mx, float& mn, float
 }
 
 }  // namespace kb
+
+namespace kb {
+
+// Exclusive scan of buf[0 .. blockDim.x*CH) fused with a block max and sum of one value per
+// thread (mx, sm, returned block-wide).  tmp >= 96 floats.  Two barriers (after the per-warp
+// partials, after the write-back).  The caller syncs before (after writing buf).
+template <int CH>
+__device__ __forceinline__ void block_scan_ch_maxsum(float* buf, float* tmp, float& mx, float& sm) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, wid = tid >> 5, nw = (blockDim.x + 31) >> 5;
+  float v[CH];
+  float* base = buf + tid * CH;
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(base + j);
+      v[j] = q.x; v[j + 1] = q.y; v[j + 2] = q.z; v[j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) v[j] = base[j];
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) local += v[j];
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  mx = warp_max(mx);
+  sm = warp_sum(sm);
+  if (lane == 31) tmp[wid] = incl;
+  if (lane == 0) { tmp[32 + wid] = mx; tmp[64 + wid] = sm; }
+  __syncthreads();
+  float t = lane < nw ? tmp[lane] : 0.f;
+  float bm = lane < nw ? tmp[32 + lane] : 0.f;
+  float bs = lane < nw ? tmp[64 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, t, o);
+    if (lane >= o) t += y;
+  }
+  mx = warp_max(bm);
+  sm = warp_sum(bs);
+  const float prev = __shfl_up_sync(0xffffffffu, t, 1);
+  const float wbase = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : prev, wid);
+  float run = wbase + incl - local;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const float x = v[j];
+    v[j] = run;
+    run += x;
+  }
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4)
+      *reinterpret_cast<float4*>(base + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) base[j] = v[j];
+  }
+  __syncthreads();
+}
+
+}  // namespace kb

@@ -296,15 +296,15 @@ __device__ __forceinline__ void tour_pathsums(float* T2, float* tmp, const unsig
 }
 
 template <int VPT>
-__global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
+__global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
   extern __shared__ float sm[];
   const LevelConsts& c = a.c;
   const int S = c.S;
   const int NT = blockDim.x;
-  const int TN = NT * 2 * VPT;  // padded tour length >= 2S
-  float* T2 = sm;
-  float* P = sm + TN;
-  float* red = P + NT * VPT;  // 128 floats
+  const int NTV = NT * VPT;                 // padded row width (columns >= S are zero columns)
+  float* T2 = sm;                           // two Euler-tour buffers of 2*NTV floats
+  float* PB = sm + 4 * NTV;                 // two row buffers of NTV floats
+  float* red = sm + 6 * NTV;                // >= 96 floats
   const int b = blockIdx.x;
   const long long row = a.sp.rows[b];
   const long long item = c.item_idx[row];
@@ -315,24 +315,21 @@ __global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
   const bool is_leaf = (i0 == i1) && leaf_raw >= 0 && leaf_raw < S;
   const int leaf = is_leaf ? leaf_raw : -1;
   const float leafv = is_leaf ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
+  const int leafk = (leaf >= 0 && leaf % NT == (int)threadIdx.x) ? leaf / NT : -1;
 
-  // per-column topology and linear constants, loaded once
+  // per-column topology (padded: invalid child -> zero column) and linear constants, once
   unsigned cc[VPT], tr[VPT];
   float kA[VPT], kB[VPT], kC1[VPT], kC2[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
-    cc[k] = 0xFFFFFFFFu;
-    tr[k] = 0u;
-    kA[k] = kB[k] = kC1[k] = kC2[k] = 0.f;
-    if (s < S) {
-      cc[k] = c.packed[s];
-      tr[k] = c.packed[S + s];
-      kA[k] = c.linA[cb + s];
-      kB[k] = c.linB[cb + s];
-      kC1[k] = c.linC1[cb + s];
-      kC2[k] = c.linC2[cb + s];
-    }
+    cc[k] = c.packed[s];
+    tr[k] = c.packed[NTV + s];
+    const bool real = s < S;
+    kA[k] = real ? c.linA[cb + s] : 0.f;
+    kB[k] = real ? c.linB[cb + s] : 0.f;
+    kC1[k] = real ? c.linC1[cb + s] : 0.f;
+    kC2[k] = real ? c.linC2[cb + s] : 0.f;
   }
 
   // ---- initial row (log values) ----
@@ -344,7 +341,7 @@ __global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
       x[k] = s < S ? leaf_seed(c, cb, item, leaf, s) : neg_inf();
     }
   } else {
-    dts_row2<VPT>(c, a.Pi_src, a.Pibar_src, a.sp, i0, i1, pb, cc, T2, T2 + S, x);
+    dts_row2<VPT>(c, a.Pi_src, a.Pibar_src, a.sp, i0, i1, pb, cc, T2, T2 + NTV, x);
     if (a.dts_save) {
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
@@ -356,93 +353,94 @@ __global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
   float m0 = neg_inf();
 #pragma unroll
   for (int k = 0; k < VPT; ++k) m0 = fmaxf(m0, x[k]);
-  const float Rd = safe_max(block_max(m0, red));  // scale of the initial row (and of the dts term)
-  // zero the whole tour buffer (the padded tail must stay zero for the scans)
-  for (int i = threadIdx.x; i < TN; i += NT) T2[i] = 0.f;
+  const float Rd = safe_max(block_max(m0, red));  // scale of the initial row and of the dts term
 
-  // ---- linear-space iterations ----
-  float pv[VPT], td[VPT], zl[VPT];
-  float psum = 0.f;
+  // ---- linear-space iterations on unnormalised values z (true value 2^(Pi - R) = z) ----
+  // Every term of the update is linear in the row except the constant dts / leaf terms, so the
+  // normalisation by the previous iteration's max (known only after its reduction) is folded into
+  // the next update: z' = (z A + (zsum - path_z)+ B + z[c1] C1 + z[c2] C2) / zmax + dts + leaf,
+  // with the dts / leaf terms taken relative to the new scale R + log2(zmax).
+  float z[VPT], td[VPT];
+  float zmax_l = 0.f, zsum_l = 0.f;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
-    pv[k] = s < S ? ex2(x[k] - Rd) : 0.f;
-    td[k] = is_leaf ? 0.f : pv[k];
-    if (s < S) P[s] = pv[k];
-    psum += pv[k];
+    z[k] = s < S ? ex2(x[k] - Rd) : 0.f;
+    td[k] = is_leaf ? 0.f : z[k];
+    PB[s] = z[k];
+    T2[lo16(tr[k])] = z[k];
+    T2[hi16(tr[k])] = -z[k];
+    zmax_l = fmaxf(zmax_l, z[k]);
+    zsum_l += z[k];
   }
-  float sumP = block_sum(psum, red);
   float R = Rd;
   bool fallback = false;
-  float Rlast = R;
+  int cur = 0;
+  float dres = 0.f;  // last-iteration residual max|Pi_new - Pi_prev| (finite entries)
   for (int it = 1; it < a.pi_iters; ++it) {
-    float path[VPT];
-    tour_pathsums<VPT>(T2, red, tr, pv, S, path);
-    const float fd = ex2(Rd - R);
-    const float lf = is_leaf ? ex2(leafv - R) : 0.f;
-    float zmax = 0.f, zmin = 3.0e38f, zsum = 0.f;
+    float* Tc = T2 + cur * 2 * NTV;
+    float* Pc = PB + cur * NTV;
+    float* Tn = T2 + (cur ^ 1) * 2 * NTV;
+    float* Pn = PB + (cur ^ 1) * NTV;
+    __syncthreads();
+    float zmax = zmax_l, zsum = zsum_l;
+    block_scan_ch_maxsum<2 * VPT>(Tc, red, zmax, zsum);
+    const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
+    const float Rn = zmax > 0.f ? R + lg2(zmax) : R;
+    const float fd = ex2(Rd - Rn);
+    const float lf = is_leaf ? ex2(leafv - Rn) : 0.f;
+    const float thresh = 7.8886091e-31f;  // 2^-100 of the (unit) row scale
+    bool bad = false;
+    zmax_l = 0.f;
+    zsum_l = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
-      float z = 0.f;
-      if (s < S) {
-        const float D = sumP - path[k];
-        z = pv[k] * kA[k];
-        if (D > 0.f) z = fmaf(D, kB[k], z);
-        const unsigned ca = lo16(cc[k]), cbb = hi16(cc[k]);
-        if (ca < (unsigned)S) z = fmaf(P[ca], kC1[k], z);
-        if (cbb < (unsigned)S) z = fmaf(P[cbb], kC2[k], z);
-        if (s == leaf) z += lf;
-        z = fmaf(td[k], fd, z);
-        zmax = fmaxf(zmax, z);
-        if (z > 0.f) zmin = fminf(zmin, z);
-        zsum += z;
+      const float path = Tc[lo16(tr[k])] + z[k];
+      const float D = fmaxf(zsum - path, 0.f);
+      float lin = z[k] * kA[k];
+      lin = fmaf(D, kB[k], lin);
+      lin = fmaf(Pc[lo16(cc[k])], kC1[k], lin);
+      lin = fmaf(Pc[hi16(cc[k])], kC2[k], lin);
+      float zn = fmaf(lin, inv, td[k] * fd);
+      if (k == leafk) zn += lf;
+      bad |= (zn > 0.f) & (zn < thresh);
+      if (a.residual && it == a.pi_iters - 1 && zn > 0.f && z[k] > 0.f)
+        dres = fmaxf(dres, fabsf(lg2(zn) - lg2(z[k] * inv)));
+      z[k] = zn;
+      zmax_l = fmaxf(zmax_l, zn);
+      zsum_l += zn;
+      if (it < a.pi_iters - 1) {
+        Pn[s] = zn;
+        Tn[lo16(tr[k])] = zn;
+        Tn[hi16(tr[k])] = -zn;
       }
-      zl[k] = z;
     }
-    block_max_minpos_sum(zmax, zmin, zsum, red);
-    if (zmax > 0.f && zmin < zmax * 7.8886091e-31f) {  // 2^-100: fp32 linear values unsafe
+    R = Rn;
+    if (__syncthreads_or(bad)) {
       fallback = true;
       break;
     }
-    Rlast = R;
-    if (it == a.pi_iters - 1) break;  // keep zl (relative to Rlast) for the final write
-    const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
-    R = zmax > 0.f ? R + lg2(zmax) : R;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * NT;
-      pv[k] = zl[k] * inv;
-      if (s < S) P[s] = pv[k];
-    }
-    sumP = zsum * inv;
+    cur ^= 1;
   }
 
   float pf[VPT];  // final Pi (log values)
   if (!fallback) {
     if (a.residual) {
-      float d = 0.f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * NT;
-        if (s < S && zl[k] > 0.f && pv[k] > 0.f) d = fmaxf(d, fabsf(lg2(zl[k]) - lg2(pv[k])));
-      }
-      d = block_max(d, red);
+      const float d = block_max(dres, red);
       if (threadIdx.x == 0) a.residual[row] = d;
     }
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) pf[k] = lg2(zl[k]) + Rlast;
+    for (int k = 0; k < VPT; ++k) pf[k] = lg2(z[k]) + R;
   } else {
     // log-space recomputation of the whole row from its initial values (rare)
     if (threadIdx.x == 0 && a.fallback_count) atomicAdd(a.fallback_count, 1);
+    float* P = PB;
     float* X = T2;
-    float* Y = T2 + S;
+    float* Y = T2 + NTV;
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int s = threadIdx.x + k * NT;
-      if (s < S) P[s] = x[k];
-    }
+    for (int k = 0; k < VPT; ++k) P[threadIdx.x + k * NT] = x[k];
     __syncthreads();
     float nv[VPT];
     for (int it = 1; it < a.pi_iters; ++it) {
@@ -470,8 +468,6 @@ __global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
       const int s = threadIdx.x + k * NT;
       pf[k] = s < S ? P[s] : neg_inf();
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < TN; i += NT) T2[i] = 0.f;
   }
 
   // ---- final Pi, row max, Pibar (from the final log row, as the reference computes them) ----
@@ -494,23 +490,23 @@ __global__ void __launch_bounds__(1024) level_forward_kernel(FwdArgs a) {
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
-    pe[k] = 0.f;
-    if (s < S) {
-      float w = pf[k];
-      if (c.use_col) w += c.col[s];
-      pe[k] = ex2(w - rms);
-      sum += pe[k];
-    }
+    float w = pf[k];
+    if (c.use_col && s < S) w += c.col[s];
+    pe[k] = s < S ? ex2(w - rms) : 0.f;
+    T2[lo16(tr[k])] = pe[k];
+    T2[hi16(tr[k])] = -pe[k];
+    sum += pe[k];
   }
-  const float row_sum = block_sum(sum, red);
-  float path[VPT];
-  tour_pathsums<VPT>(T2, red, tr, pe, S, path);
+  __syncthreads();
+  float rmx_unused = 0.f;
+  block_scan_ch_maxsum<2 * VPT>(T2, red, rmx_unused, sum);
+  const float row_sum = sum;
   float* brow = a.pibar + (size_t)row * S;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
     if (s < S) {
-      const float denom = row_sum - path[k];
+      const float denom = row_sum - (T2[lo16(tr[k])] + pe[k]);
       brow[s] = denom > 0.f ? lg2(denom) + row_max + c.mc[cb + s] : neg_inf();
     }
   }
@@ -1001,8 +997,8 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = n_rows;
   a.pi_iters = pi_iters;
   int bd;
-  const int vpt = vpt_pick_wide(S, bd);
-  const size_t smem = (size_t)(bd * 2 * vpt + bd * vpt + 128) * sizeof(float);
+  const int vpt = engine_width(S, bd);
+  const size_t smem = (size_t)(6 * bd * vpt + 128) * sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
 #define KB_LF_CASE(V)                                                                                     \
   case V:                                                                                                 \

@@ -209,7 +209,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None):
                   lin[0].data_ptr(), lin[1].data_ptr(), lin[2].data_ptr(), lin[3].data_ptr(), pDp.data_ptr(),
                   pSp.data_ptr(), prs, crs, f32(clp).data_ptr(), int(ucw), tt.parent.data_ptr(),
                   tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
-                  tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed.data_ptr(),
+                  tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
                   int(so.pi_iters), S, st)
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
