@@ -1,0 +1,42 @@
+"""The C ABI shared library loads on the CPU host and exports every entry point the public header
+declares (no device calls: these tests run without a GPU)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kbench_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kb_solver.h"
+
+
+def test_header_parses_all_entry_points():
+    decls = _lib.parse_header()
+    text = re.sub(r"/\*.*?\*/", " ", HEADER.read_text(), flags=re.S)
+    names = set(re.findall(r"\bint\s+(kb_\w+)\s*\(", text))
+    assert names == set(decls)
+    assert {"kb_wave_step", "kb_dts_forward", "kb_e_fixed_point", "kb_wave_adjoint", "kb_level_forward",
+            "kb_level_backward"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("libkb_solver.so not built")
+    handle = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in _lib.parse_header():
+        assert hasattr(handle, name), name
+    lib = _lib.lib()
+    assert lib.kb_abi_version() == 1
+
+
+def test_invalid_sizes_are_rejected_without_a_device():
+    """Argument validation happens on the host before any launch."""
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("libkb_solver.so not built")
+    lib = _lib.lib()
+    assert lib.kb_active_mask(None, 0, -1, 4, 0.0, 0, None, None) == _lib.KB_ERR_ARG
+    assert lib.kb_e_step_forward(*([None] * 15), 0, 0, 1, 0, None) == _lib.KB_ERR_ARG
+    with pytest.raises(ValueError):
+        _lib.call("kb_active_mask", None, 0, -1, 4, 0.0, 0, None, None)
