@@ -45,6 +45,21 @@ int kb_e_fixed_point(const float* E0, float* E_out, float* E_tmp, float* E_s1, f
                      const int* node_child2, const int* jumps, int K, int S, int G, int max_iter, double tol,
                      int use_col_weights, int* iters_out, void* stream);
 
+/* Allocation-free variant of kb_e_fixed_point, for callers that cannot allocate device memory
+ * (a host that owns all device memory through its own pool, or that must not trigger an
+ * allocation at this point).  It has no counterpart in the reference.  Same inputs, outputs and
+ * semantics as kb_e_fixed_point, without the E_tmp argument: the ping-pong buffer is a file-scope
+ * device array of KB_NOALLOC_ESTEP_MAX floats (256 KiB, held by every GPU that loads the library
+ * until exit).  G*S above KB_NOALLOC_ESTEP_MAX returns KB_ERR_SIZE.  The first call on a device
+ * looks the array's address up (cudaGetSymbolAddress, no allocation) -- make it before any stream
+ * capture.  All calls share the array; calls that overlap on the GPU race. */
+#define KB_NOALLOC_ESTEP_MAX 65536
+int kb_e_fixed_point_noalloc(const float* E0, float* E_out, float* E_s1, float* E_s2, float* Ebar,
+                             const float* log_pS, const float* log_pD, const float* log_pL,
+                             const float* max_coupling, const float* col_log_probs, const int* node_parent,
+                             const int* node_child1, const int* node_child2, const int* jumps, int K, int S, int G,
+                             int max_iter, double tol, int use_col_weights, int* iters_out, void* stream);
+
 /* Replaces _launch_e_step_forward_2d (e_step.py:244-287): one E application per item row;
  * max_diff_out [G] may be NULL. */
 int kb_e_step_forward(const float* E, float* E_new, float* E_s1, float* E_s2, float* Ebar, float* max_diff_out,

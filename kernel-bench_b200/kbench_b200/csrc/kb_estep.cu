@@ -9,6 +9,8 @@
 #include "kb_common.cuh"
 #include "kb_solver.h"
 
+#include <mutex>
+
 namespace {
 
 using namespace kb;
@@ -296,5 +298,64 @@ extern "C" int kb_e_step_vjp(const float* E, const float* E_new, const float* E_
   e_step_vjp_kernel<<<1, block_for(S), smem, (cudaStream_t)stream>>>(
       E, E_new, E_s1, E_s2, Ebar, p, G, g_new, g_s1, g_s2, g_ebar, grad_E, grad_pS, grad_pD, grad_pL, grad_mc,
       grad_col, lv_ptr, n_levels, lv_par, lv_c1, lv_c2);
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant of kb_e_fixed_point.
+//
+// Some hosts cannot allocate device memory at the point where they need the E fixed point: code
+// that owns every device byte through its own pool and forbids driver allocations, or that runs
+// where an allocation (and the synchronisation it may imply) is not allowed.  Such callers still
+// pass their inputs and outputs, but the iteration's ping-pong buffer comes from this
+// file-scope device array instead of a caller-provided scratch tensor.
+//
+// The array is part of the library image: every GPU that loads the library holds these
+// KB_NOALLOC_ESTEP_MAX floats (256 KiB) until the process exits.  Host code cannot use the
+// array's name as a device address, so the first call on each device (with that device
+// current) looks the address up with cudaGetSymbolAddress and caches it; that first call should
+// happen before any stream capture.  All calls share the array and it keeps the last call's
+// contents (the iteration writes it before reading it, so nothing needs clearing); calls that
+// overlap on the GPU -- concurrent streams, or several host threads -- race on it.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+static __device__ __align__(256) float g_estep_noalloc_scratch[KB_NOALLOC_ESTEP_MAX];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_addr[kMaxDevices] = {nullptr};
+std::mutex g_scratch_mutex;
+
+int scratch_for_current_device(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KB_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_estep_noalloc_scratch) != cudaSuccess || ptr == nullptr) return KB_ERR_LAUNCH;
+    g_scratch_addr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_scratch_addr[dev];
+  return KB_OK;
+}
+
+}  // namespace
+
+extern "C" int kb_e_fixed_point_noalloc(const float* E0, float* E_out, float* E_s1, float* E_s2, float* Ebar,
+                                        const float* log_pS, const float* log_pD, const float* log_pL,
+                                        const float* max_coupling, const float* col_log_probs,
+                                        const int* node_parent, const int* node_child1, const int* node_child2,
+                                        const int* jumps, int K, int S, int G, int max_iter, double tol,
+                                        int use_col_weights, int* iters_out, void* stream) {
+  if (S <= 0 || G <= 0 || max_iter < 1 || K < 0) return KB_ERR_ARG;
+  if (S > KB_MAX_S || (long long)S * G > KB_NOALLOC_ESTEP_MAX) return KB_ERR_SIZE;
+  float* scratch = nullptr;
+  if (scratch_for_current_device(&scratch) != KB_OK) return KB_ERR_LAUNCH;
+  EParams p = make_params(log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
+                          node_child2, jumps, K, S, use_col_weights);
+  const size_t smem = (size_t)(3 * S + 64) * sizeof(float);
+  if (set_smem((const void*)e_fixed_point_kernel, smem)) return KB_ERR_LAUNCH;
+  e_fixed_point_kernel<<<1, block_for(S), smem, (cudaStream_t)stream>>>(E0, E_out, scratch, E_s1, E_s2, Ebar, p, G,
+                                                                          max_iter, tol, iters_out);
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
