@@ -2,6 +2,8 @@
 """Headline benchmark: forward + backward solves of the large single-family problem.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--config 3]
+    python bench.py --config 4 [--families F --chunk F_c]       # the batched-family workload
+    python bench.py --config 5 [--directions D]                 # forward + D-direction tangent
 
 One "step" is one full solve on every GPU: ``run_forward`` (E fixed point, every wave's split
 reduction and pi_iters sweeps, NLL) + ``run_backward`` (implicit adjoint, E-adjoint BiCGSTAB,
@@ -16,6 +18,15 @@ memory and the loss + gradients copied back every step.
 ``--impl reference`` times the reference algorithm's CPU restatement (the numpy oracle under
 ``oracle/``) on a bounded sample of the same workload (a family with the same species tree and
 fewer rows), extrapolated per row; on N>1 only rank 0 runs it.
+
+``--config 4`` measures the batched workload instead: 1024 families (S=1023, ~16k rows each)
+sharing one theta, split into contiguous blocks per rank, each block processed in chunks of
+``--chunk`` families (all 1024 families' [C,S] state, ~275 GB, does not fit one GPU), with one
+all-reduce of [loss, column accumulators] per step; ``value`` is families/s.
+
+``--config 5`` measures the tangent workload: the config-3 family's forward plus the forward-mode
+tangent of the root scores along 32 directions (one batched pass), checked against central
+finite differences of the forward; ``value`` is tangent passes/s (forward + all directions).
 """
 
 from __future__ import annotations
@@ -51,6 +62,9 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--families", type=int, default=None, help="config 4: families in the whole batch")
+    ap.add_argument("--chunk", type=int, default=128, help="config 4: families per chunk on a GPU")
+    ap.add_argument("--directions", type=int, default=32, help="config 5: tangent directions per pass")
     return ap.parse_args()
 
 
@@ -143,19 +157,19 @@ def algorithmic_bytes(plan, S):
 
 
 def cpu_sample_case(n_genes, S_species_leaves=2048):
-    """A bounded sample of the workload for the CPU oracle: the config-3 species tree (S=4095)
+    """A bounded sample of the workload for the CPU oracle: the benchmark's species tree size
     with a small gene family (same per-row work, fewer rows)."""
     from kbench_b200 import gen
     return gen.ProblemConfig("cpu_sample", S_species_leaves, n_genes, 2, max(8, n_genes // 3), 0,
                              solver_options=dict(gen.CONFIGS[3].solver_options))
 
 
-def run_cpu_oracle_sample(full_rows, seed, n_genes=512):
+def run_cpu_oracle_sample(full_rows, seed, n_genes=512, species_leaves=2048):
     """Time the oracle (forward + backward) on the sample; returns (solves/s, seconds, rows)."""
     import numpy as np
     from kbench_b200 import gen
     from oracle import kb_oracle as O
-    cap = gen.generate(cpu_sample_case(n_genes), seed=seed, as_torch=False)
+    cap = gen.generate(cpu_sample_case(n_genes, species_leaves), seed=seed, as_torch=False)
     st = dict(cap["static"])
     st["solver_options"] = cap["meta"]["solver_options"]
     t0 = time.perf_counter()
@@ -173,25 +187,302 @@ def reference_arm(args, world, rank):
     if rank != 0:
         return
     from kbench_b200 import gen
-    full_rows = int(gen.generate(args.config, as_torch=False)["meta"]["C"])
+    batched = args.config == 4
+    if batched:
+        n_total = int(args.families or gen.CONFIGS[4].n_families)
+        full_rows = int(gen.generate(4, n_families=1, as_torch=False)["meta"]["C"])  # one family
+        leaves = gen.CONFIGS[4].n_species
+    else:
+        full_rows = int(gen.generate(args.config, as_torch=False)["meta"]["C"])
+        leaves = gen.CONFIGS[3].n_species
     times = []
     for i in range(args.warmup + args.steps):
-        sps, dt, rows = run_cpu_oracle_sample(full_rows, seed=3000, n_genes=48)
+        sps, dt, rows = run_cpu_oracle_sample(full_rows, seed=3000, n_genes=48, species_leaves=leaves)
         if i >= args.warmup:
             times.append(1.0 / sps)
     solve_s = statistics.median(times)
-    value = 1.0 / solve_s
-    sample = (f"numpy oracle forward+backward of a {rows}-row family on the config-3 species tree "
-              f"(S=4095), extrapolated per row to C={full_rows}")
+    S = 2 * leaves - 1
+    if batched:
+        step_s = solve_s * n_total
+        value, unit = n_total / step_s, "families/s"
+        metric = "fwd+bwd families/sec (batched config 4: S=1023, ~16k rows per family, shared theta)"
+        what = f"extrapolated per row to one {full_rows}-row family, x{n_total} families"
+    else:
+        step_s = solve_s
+        value, unit, metric = 1.0 / solve_s, "solves/s", METRIC
+        what = f"extrapolated per row to C={full_rows}"
+    sample = (f"numpy oracle forward+backward of a {rows}-row family on the config-{args.config} species "
+              f"tree (S={S}), {what}")
     line = {
-        "metric": METRIC, "value": value, "unit": "solves/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": solve_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "strong" if batched else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)", "impl": "reference",
         "config": {"workload": f"config{args.config} family, CPU sample", "sample_rows": rows},
-        "cpu_baseline": {"value": value, "unit": "solves/s", "cores": 1, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "solves/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": 1, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def roofline_from_timers(timers, peak, peak_kind, steps):
+    """Dominant level kernel over (static, timer) pairs: algorithmic bytes / device time."""
+    from kbench_b200 import engine
+    k_ms, k_n, k_bytes = {}, {}, {}
+    for static, timer in timers:
+        plan = engine.build_plan(static)
+        fwd_b, bwd_b = algorithmic_bytes(plan, int(static.state_helpers["S"]))
+        for name, (ms, n, per) in timer.totals().items():
+            bm = fwd_b if name == "kb_level_forward" else bwd_b
+            k_ms[name] = k_ms.get(name, 0.0) + ms / steps
+            k_n[name] = k_n.get(name, 0) + n / steps
+            k_bytes[name] = k_bytes.get(name, 0.0) + sum(bm[lv] for lv, _ in per) / steps
+    dominant = max(k_ms, key=k_ms.get)
+    achieved = k_bytes[dominant] / (k_ms[dominant] * 1e-3) / 1e9
+    return {
+        "bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+        "algorithmic_bytes_per_launch": k_bytes[dominant] / k_n[dominant],
+        "avg_launch_ms": k_ms[dominant] / k_n[dominant],
+        "kernel_ms_per_step": {k: round(v, 3) for k, v in k_ms.items()},
+    }
+
+
+def batch_arm(args, world, rank, local):
+    """--config 4: families/s of the batched workload (chunked per GPU, sharded across ranks)."""
+    import torch
+    import torch.distributed as dist
+    from kbench_b200 import _lib, batch, engine, gen
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    n_total = int(args.families or gen.CONFIGS[4].n_families)
+    f0, f1 = batch.family_block(n_total, world, rank)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    workers = max(1, len(os.sched_getaffinity(0)) // max(1, local_world))
+    t0 = time.perf_counter()
+    chunks = batch.build_chunks(4, f0, f1, args.chunk, workers=workers)
+    gen_s = time.perf_counter() - t0
+    allreduce = (lambda t: dist.all_reduce(t)) if world > 1 else None
+    t0 = time.perf_counter()
+    fb = batch.FamilyBatch(chunks, n_total, batch.EngineSolver(dev), allreduce=allreduce)
+    load_s = time.perf_counter() - t0
+    theta = torch.from_numpy(chunks[0]["inputs"]["theta"]).to(dev)
+    cw = torch.from_numpy(chunks[0]["inputs"]["col_weights"]).to(dev)
+    S = int(chunks[0]["meta"]["S"])
+    rows, n_chunks = fb.rows, len(chunks)
+    del chunks
+    for _ in range(args.warmup):
+        fb.step(theta, cw)
+    torch.cuda.synchronize()
+
+    timers = [(st, engine.LevelTimer()) for st in fb.statics]
+    for st, tm in timers:
+        st._level_timer = tm
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = sum(_lib.LAUNCHES.values())
+    if sampler:
+        sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        res = fb.step(theta, cw)
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    launches = sum(_lib.LAUNCHES.values()) - launches0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    peak, peak_kind = measured_peak()
+    roofline = roofline_from_timers(timers, peak, peak_kind, args.steps) if rank == 0 else None
+    for st, _ in timers:
+        st._level_timer = None
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # end to end: theta / col_weights from pinned host memory, loss + gradients back every step
+    n_out = 1 + 3 * S + S
+    th_host, cw_host = theta.cpu().pin_memory(), cw.cpu().pin_memory()
+    out_host = torch.empty((n_out,), dtype=torch.float64).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        r = fb.step(th_host.to(dev, non_blocking=True), cw_host.to(dev, non_blocking=True))
+        out_host.copy_(torch.cat([r.loss.reshape(1), r.grad_theta.reshape(-1).double(),
+                                  r.grad_col.reshape(-1).double()]), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        float(out_host[0])
+    e1.record()
+    torch.cuda.synchronize()
+    e_t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e_ms = float(e_t.item())
+    if rank == 0:
+        line = {
+            "metric": "fwd+bwd families/sec (batched config 4: S=1023, ~16k rows per family, shared theta)",
+            "value": round(n_total * 1000.0 / ms_max, 3), "unit": "families/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded generator of the benchmark's config text)",
+            "config": {
+                "workload": f"config4: {n_total} families (S={S}); rank 0 holds families [{f0},{f1}) "
+                            f"= {rows} rows in {n_chunks} chunks of <= {args.chunk}",
+                "parallelism": f"dp{world} (family blocks), one all-reduce of [loss, 8*S accumulators] per step",
+                "l2": "state arrays far larger than L2; no flush needed",
+                "generation_s": round(gen_s, 1), "load_s": round(load_s, 1),
+            },
+            "roofline": roofline, "cpu_baseline": None,
+            "e2e": {"value": round(n_total * 1000.0 / e_ms, 3), "unit": "families/s",
+                    "h2d_bytes_per_step": int((theta.numel() + cw.numel()) * 4),
+                    "d2h_bytes_per_step": int(n_out * 8)},
+            "gpu_launches": int(launches), "clocks": clocks,
+            "loss": float(res.loss),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def tangent_arm(args, world, rank, local):
+    """--config 5: forward + batched forward-mode tangent of the config-3 family (replicas on N>1)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from kbench_b200 import _lib, engine, gen, runtime, tangent
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    cap = gen.generate(5, seed=5000 + rank)
+    S, C = int(cap["meta"]["S"]), int(cap["meta"]["C"])
+    static = runtime.make_static(cap, dev)
+    theta = cap["inputs"]["theta"].to(dev)
+    cw = cap["inputs"]["col_weights"].to(dev)
+    D = int(args.directions)
+    V = torch.from_numpy(np.stack([np.random.Generator(np.random.PCG64(5000 + k)).standard_normal((S, 3))
+                                   for k in range(D)]).astype(np.float32)).to(dev)
+    plan = engine.build_plan(static)
+
+    def step(th, vv):
+        _, saved = runtime.run_forward(static, th, cw)
+        return tangent.jvp_batch(static, th, vv, saved)
+
+    for _ in range(args.warmup):
+        step(theta, V)
+    torch.cuda.synchronize()
+    timer = engine.LevelTimer()
+    static._level_timer = timer
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = sum(_lib.LAUNCHES.values())
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(theta, V)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    launches = sum(_lib.LAUNCHES.values()) - launches0
+    totals = timer.totals()
+    static._level_timer = None
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # split forward / tangent, and the finite-difference check of two directions
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    _, saved = runtime.run_forward(static, theta, cw)
+    ev[1].record()
+    roots = tangent.jvp_batch(static, theta, V, saved)
+    ev[2].record()
+    torch.cuda.synchronize()
+    fwd_ms, tan_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    fd_err = []
+    eps = 1e-2
+    for k in range(2):
+        _, sp = runtime.run_forward(static, theta + eps * V[k], cw)
+        rp = sp["root_rows"].double()
+        del sp
+        _, sm_ = runtime.run_forward(static, theta - eps * V[k], cw)
+        fd = (rp - sm_["root_rows"].double()) / (2 * eps)
+        del sm_
+        t = roots[k].double()
+        fin = torch.isfinite(fd) & torch.isfinite(t)
+        fd_err.append(float((fd[fin] - t[fin]).norm() / fd[fin].norm()))
+    del saved, roots
+
+    # end to end: theta and the directions from pinned host memory, root tangents back
+    th_host, v_host = theta.cpu().pin_memory(), V.cpu().pin_memory()
+    out_host = torch.empty((D, int(static.wave_layout["root_row_ids"].numel()), S), dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        r = step(th_host.to(dev, non_blocking=True), v_host.to(dev, non_blocking=True))
+        out_host.copy_(r, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        float(out_host[0, 0, 0])
+    x1.record()
+    torch.cuda.synchronize()
+    x_t = torch.tensor([x0.elapsed_time(x1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(x_t, op=dist.ReduceOp.MAX)
+    e_ms = float(x_t.item())
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        k_ms = {n: v[0] / args.steps for n, v in totals.items()}
+        n_l = totals["kb_level_tangent"][1] / args.steps
+        # compulsory bytes of the tangent levels: per direction write dPi, dPibar of every row and
+        # read dPi, dPibar of each distinct child once per level; the primal rows once
+        kb = sum(4 * S * (D * (2 * (plan.level_ptr[L + 1] - plan.level_ptr[L]) + 2 * plan.children_per_level[L])
+                          + 3 * (plan.level_ptr[L + 1] - plan.level_ptr[L]))
+                 for L in range(plan.n_levels))
+        ach = kb / (k_ms["kb_level_tangent"] * 1e-3) / 1e9
+        line = {
+            "metric": f"fwd + {D}-direction tangent passes/sec (S=4095, C~131k; BASELINE tangent config)",
+            "value": round(world * 1000.0 / ms_max, 4), "unit": "passes/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator; v ~ N(0,1), seeds 5000+k)",
+            "config": {"workload": f"config5: S={S}, C={C} rows, forward + {D} tangent directions "
+                                   f"(self_iters = pi_iters = {static.solver_options.pi_iters})",
+                       "parallelism": f"replicas x{world}",
+                       "l2": "state arrays far larger than L2; no flush needed"},
+            "fwd_ms": round(fwd_ms, 3), "tangent_ms": round(tan_ms, 3),
+            "fd_check": {"eps": eps, "rel_err": fd_err, "tolerance": 1e-3},
+            "roofline": {"bound": "hbm", "kernel": "kb_level_tangent", "achieved": round(ach, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "algorithmic_bytes_per_launch": kb / n_l,
+                         "avg_launch_ms": k_ms["kb_level_tangent"] / n_l,
+                         "kernel_ms_per_step": {k2: round(v, 3) for k2, v in k_ms.items()}},
+            "cpu_baseline": None,
+            "e2e": {"value": round(world * 1000.0 / e_ms, 4), "unit": "passes/s",
+                    "h2d_bytes_per_step": int((theta.numel() + V.numel()) * 4),
+                    "d2h_bytes_per_step": int(out_host.numel() * 4)},
+            "gpu_launches": int(launches), "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -203,12 +494,18 @@ def main():
             import torch.distributed as dist
             dist.destroy_process_group()
         return
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.config == 4:
+        batch_arm(args, world, rank, local)
+        return
+    if args.config == 5:
+        tangent_arm(args, world, rank, local)
+        return
     import torch
     import torch.distributed as dist
     from kbench_b200 import _lib, engine, gen, runtime
 
-    if args.warmup < 3:
-        args.warmup = 3
     dev = torch.device("cuda", local if world > 1 else 0)
     seed = 1000 * args.config + rank
     cap = gen.generate(args.config, seed=seed)

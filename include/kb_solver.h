@@ -189,9 +189,13 @@ int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const flo
  * [split_ptr[b], split_ptr[b+1]) of (sl, sr, lsp) -- or the leaf seed for split-less leaf rows --
  * then all pi_iters iterations on chip; writes the final pi, pibar rows, pibar_row_max, the split
  * reduction (dts_save, may be NULL) and the last-iteration residual (may be NULL).
- * fallback_count (device int, may be NULL) counts rows recomputed in log space.  packed: [4,S] uint32
- * per-column tables (children, Euler-tour enter/exit, preorder start/end, parent | first-child
- * flag; two 16-bit fields each, 0xFFFF = none) -- see kbench_b200/tree.py pack_columns(). */
+ * fallback_count (device int, may be NULL) counts rows recomputed in log space.  Uniform column
+ * weights only (use_col_weights must be 0).  tour_tables: [3,NTV] uint32 tables of
+ * kbench_b200/tree.py pack_forward() (children columns, byte offsets of the children's and the
+ * column's own Euler-tour slots); when given and kb_tour_layout(S) accepts S, the tour kernel
+ * runs (dts_save must then be non-NULL).  Otherwise packed: [4,NTV] tables of pack_columns(...,
+ * ntv) with NTV from the engine width (children, Euler-tour enter/exit, preorder start/end,
+ * parent | first-child flag; two 16-bit fields each). */
 int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                      const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src, float* pi,
                      float* pibar, float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
@@ -201,8 +205,13 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
                      long long param_row_stride, long long const_row_stride, const float* col_log_probs,
                      int use_col_weights, const int* node_parent, const int* node_child1, const int* node_child2,
                      const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
-                     const long long* item_idx, const int* leaf_state, const unsigned* packed, int pi_iters, int S,
-                     void* stream);
+                     const long long* item_idx, const int* leaf_state, const unsigned* packed,
+                     const unsigned* tour_tables, int pi_iters, int S, void* stream);
+
+/* Layout of the forward tour kernel for S columns (host only): padded width NTV (smallest power
+ * of two > S, at least 64), threads per row and columns per thread.  Returns 3 (KB_ERR_SIZE) with
+ * *ntv = 0 when NTV would exceed 4096 (kb_level_forward then uses its packed-table kernel). */
+int kb_tour_layout(int S, int* ntv, int* threads, int* cols_per_thread);
 
 /* Backward of one dependency level (replaces, for the rows listed, active_mask_from_rhs_absmax_
  * fused + compute_dts_forward + wave_backward_uniform_fused + dts_cross_backward_accum_fused +
@@ -228,6 +237,78 @@ int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, c
 /* Fixed-order sum of kb_level_backward's fp64 slots -> out8 [8,S] fp32: the cotangents of
  * log_pD, log_pS, max_coupling, E, Ebar, E_s1, E_s2 and col_log_probs (in that order). */
 int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S, float* out8, void* stream);
+
+/* ---------------- forward-mode tangent (the tangent benchmark config) ---------------- */
+
+/* E-step tangent fixed point (replaces e_tangent_fixed_point, kbench/core/kernels/
+ * e_step_tangent.py:174-208, with its kernel _e_step_tangent_2d_kernel :23-150) for D directions
+ * at once: one persistent CTA per direction iterates dE <- J_E dE + J_p dp at the frozen E_star
+ * [G,S] from dE0 (NULL = zero) until max|dE_new - dE| <= tol * max(1, max|dE_new|) over the G rows
+ * or max_iter, then applies once more for dE_s1 / dE_s2 / dEbar.  Direction-major buffers
+ * [D,G,S]: dlog_pS, dlog_pD, dlog_pL, dmax_coupling, dE0, dE_out, scratch, dE_s1, dE_s2, dEbar;
+ * iters_out [D] (may be NULL).  jumps / K: the ancestor jump table of kb_build_jumps. */
+int kb_e_tangent_fixed_point(const float* E_star, const float* dlog_pS, const float* dlog_pD,
+                             const float* dlog_pL, const float* dmax_coupling, const float* log_pS,
+                             const float* log_pD, const float* log_pL, const float* max_coupling,
+                             const float* col_log_probs, int use_col_weights, const int* node_child1,
+                             const int* node_child2, const int* jumps, int K, int G, int S, int D, int max_iter,
+                             float tol, const float* dE0, float* dE_out, float* scratch, float* dE_s1,
+                             float* dE_s2, float* dEbar, int* iters_out, void* stream);
+
+/* One linearised E application (replaces _launch_e_step_tangent_2d, e_step_tangent.py:153-171)
+ * for D directions x G rows: dE_new, dE_s1, dE_s2, dEbar [D,G,S]; max_diff [D*G] (may be NULL). */
+int kb_e_tangent_step(const float* E_star, const float* dE_in, const float* dlog_pS, const float* dlog_pD,
+                      const float* dlog_pL, const float* dmax_coupling, const float* log_pS, const float* log_pD,
+                      const float* log_pL, const float* max_coupling, const float* col_log_probs,
+                      int use_col_weights, const int* node_child1, const int* node_child2, const int* jumps, int K,
+                      int G, int S, int D, float* dE_new, float* dE_s1, float* dE_s2, float* dEbar,
+                      float* max_diff, void* stream);
+
+/* Tangent of the split reduction (replaces compute_dts_tangent, kbench/core/kernels/
+ * dts_tangent.py:99-122): out[p,s] = sum over parent p's splits (order[ptr[p] .. ptr[p+1]),
+ * indices into sl / sr / log_split_probs) of sum_k 2^(t_k - dts_r[p,s]) dt_k, in that fixed order
+ * (no atomics); 0 where dts_r is -inf.  Parameters at item * param_row_stride + s, item =
+ * item_idx[item_offset + p]. */
+int kb_dts_tangent(const float* Pi, const float* Pibar, const float* dPi, const float* dPibar, const long long* sl,
+                   const long long* sr, const float* log_split_probs, const long long* order, const long long* ptr,
+                   int W, const int* node_child1, const int* node_child2, const float* log_pD,
+                   const float* log_pS, const float* dlog_pD, const float* dlog_pS, long long param_row_stride,
+                   const long long* item_idx, long long item_offset, const float* dts_r, float* out, int S,
+                   void* stream);
+
+/* Linearised wave step, n_iters in-place Jacobi steps on chip (replaces
+ * compute_wave_step_tangent_selfloop, kbench/core/kernels/wave_tangent.py:339-389, and with
+ * n_iters = 1 compute_wave_step_tangent :392-431): rows w < W read Pi_in / dPi_in at pi_ws + w,
+ * write dPi_out[w] (dPi_out already offset to the wave; may alias dPi_in's rows) and, if
+ * dPibar_out != NULL, dPibar_out[ws + w] from the last step.  Constants at item * const_row_stride
+ * + s (item = item_idx[ws + w]); leaf_state_idx NULL = no leaf term; dts_reduced / d_dts [W,S]
+ * both NULL or both given. */
+int kb_wave_tangent(const float* Pi_in, const float* dPi_in, float* dPi_out, float* dPibar_out, long long ws,
+                    long long pi_ws, int W, int S, int n_iters, const float* max_coupling, const float* dMC,
+                    const float* DL, const float* dDL, const float* Ebar, const float* dEbar, const float* E,
+                    const float* dE, const float* SL1, const float* dSL1, const float* SL2, const float* dSL2,
+                    long long const_row_stride, const float* col_log_probs, int use_col_weights,
+                    const int* node_child1, const int* node_child2, const int* jumps, int K,
+                    const int* leaf_state_idx, const float* leaf_logp, const float* dleaf_logp,
+                    const long long* item_idx, const float* dts_reduced, const float* d_dts, void* stream);
+
+/* Tangent of one dependency level for D directions (replaces, for the rows listed,
+ * compute_dts_tangent + compute_wave_step_tangent_selfloop as driven by newton/
+ * forward_tangent.py:150-193 with self_iters = n_iters): one CTA per (row, direction) computes
+ * the row's split tangent from the children's tangent rows, then n_iters Jacobi steps from a zero
+ * tangent at the frozen primal row, and writes dPi / dPibar [D, C, S] (direction stride
+ * dir_stride).  dts_saved: the forward's split reductions [C,S].  Tangent constants [D, G, S]
+ * (direction stride tangent_dir_stride).  tour_tables: kbench_b200/tree.py pack_forward(); S must
+ * be accepted by kb_tour_layout. */
+int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
+                     const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
+                     const float* dts_saved, float* dPi, float* dPibar, long long dir_stride, int D, const float* mc,
+                     const float* dl, const float* ebar, const float* e, const float* sl1, const float* sl2,
+                     const float* leaf_logp, const float* log_pD, const float* log_pS, long long param_row_stride,
+                     long long const_row_stride, const float* dMC, const float* dDL, const float* dEbar,
+                     const float* dE, const float* dSL1, const float* dSL2, const float* dleaf, const float* dpD,
+                     const float* dpS, long long tangent_dir_stride, const long long* item_idx,
+                     const int* leaf_state, const unsigned* tour_tables, int n_iters, int S, void* stream);
 
 #ifdef __cplusplus
 }

@@ -514,6 +514,628 @@ __global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
+// forward, tour-table variant (rows of up to 4096 padded columns)
+// ------------------------------------------------------------------------------------------
+//
+// Same arithmetic as level_forward_kernel, with the work per column and iteration cut down:
+//  * VF = 8 columns per thread (fewer threads per row amortise the block-wide scan);
+//  * the Euler tour lives in a swizzled layout: thread t scans the 2*VF consecutive tour entries
+//    [t*2VF, (t+1)*2VF) as float4 groups whose order inside the chunk is XOR-permuted by t, so the
+//    vector loads of a quarter-warp hit distinct banks; the host tables hold the BYTE offsets of
+//    every column's enter / exit slot and of its species children's enter slots, so a scatter or
+//    gather is one mask/shift and one shared-memory access;
+//  * the speciation gathers read the children's values from the tour buffer before it is scanned
+//    (no separate row buffer);
+//  * the leaf term is folded into the constant term (both are constants times 2^(R0 - R));
+//  * the split reduction prefetches the next split's child rows with cp.async while it reduces
+//    the current one (one barrier per split).
+
+// Tour tables of one column (host: tree.pack_forward):
+//   tb[s]         children columns c1 | c2 << 16 (missing child -> a padded column)
+//   tb[NTV + s]   byte offsets of the children's enter slots (lo | hi << 16)
+//   tb[2NTV + s]  byte offsets of the column's own enter | exit slots
+__device__ __forceinline__ const float& lds_at(const char* base, unsigned off) {
+  return *reinterpret_cast<const float*>(base + off);
+}
+__device__ __forceinline__ float& sts_at(char* base, unsigned off) { return *reinterpret_cast<float*>(base + off); }
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Exclusive scan, in place, of the swizzled tour buffer T (NT * 2VF floats), fused with the
+// block max of mx and the block sum of sm (returned to every thread).  red >= 96 floats.
+// The caller syncs before (the buffer is complete); two barriers inside, the second on exit.
+template <int VF>
+__device__ __forceinline__ void tour_scan_sw(float* T, float* red, float& mx, float& sm) {
+  constexpr int Q = VF / 2;  // float4 groups per thread chunk
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int sw = Q == 1 ? 0 : ((t / (8 / Q)) & (Q - 1));
+  float4* base = reinterpret_cast<float4*>(T) + t * Q;
+  float gs[Q];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    gs[q] = (v.x + v.y) + (v.z + v.w);
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) local += gs[q];
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  mx = warp_max(mx);
+  sm = warp_sum(sm);
+  if (lane == 31) red[wid] = incl;
+  if (lane == 0) { red[32 + wid] = mx; red[64 + wid] = sm; }
+  __syncthreads();
+  float tt = lane < nw ? red[lane] : 0.f;
+  const float bm = lane < nw ? red[32 + lane] : 0.f;
+  const float bs = lane < nw ? red[64 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, tt, o);
+    if (lane >= o) tt += y;
+  }
+  mx = warp_max(bm);
+  sm = warp_sum(bs);
+  const float prev = __shfl_up_sync(0xffffffffu, tt, 1);
+  float run = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : prev, wid) + incl - local;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    float4 o;
+    o.x = run;
+    o.y = run + v.x;
+    o.z = o.y + v.y;
+    o.w = o.z + v.z;
+    base[q ^ sw] = o;
+    run += gs[q];
+  }
+  __syncthreads();
+}
+
+struct Fwd4Args {
+  FwdArgs f;
+  const unsigned* tb;  // [3, NTV] tour tables
+};
+
+template <int VF>
+__global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args args) {
+  extern __shared__ __align__(16) float sm[];
+  const FwdArgs& a = args.f;
+  const LevelConsts& c = a.c;
+  const unsigned* __restrict__ tb = args.tb;
+  const int S = c.S;
+  const int NT = blockDim.x;
+  const int NTV = NT * VF;
+  const int TB = 2 * NTV;  // floats per tour buffer
+  float* red = sm + 2 * TB;
+  char* T0 = reinterpret_cast<char*>(sm);
+  char* T1 = reinterpret_cast<char*>(sm + TB);
+  const int tid = threadIdx.x;
+  const int b = blockIdx.x;
+  const long long row = a.sp.rows[b];
+  const long long item = c.item_idx[row];
+  const size_t cb = (size_t)(item * c.crs);
+  const size_t pb = (size_t)(item * c.prs);
+  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
+  const int leaf_raw = c.leaf_state[row];
+  const bool is_leaf = (i0 == i1) && leaf_raw >= 0 && leaf_raw < S;
+  const int leaf = is_leaf ? leaf_raw : -1;
+  const float leafv = is_leaf ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
+
+  // ---- initial row (log values): leaf seed or split reduction ----
+  float x[VF];
+  if (is_leaf) {
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      x[k] = s < S ? leaf_seed(c, cb, item, leaf, s) : neg_inf();
+    }
+  } else {
+    // staging pairs (Pl, Pr) for split parity 0 / 1; padded columns read -inf
+    float* stg = sm;
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      if (s >= S) {
+        stg[s] = neg_inf();
+        stg[NTV + s] = neg_inf();
+        stg[2 * NTV + s] = neg_inf();
+        stg[3 * NTV + s] = neg_inf();
+      }
+    }
+    unsigned ccol[VF];
+    float m[VF], acc[VF];
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      ccol[k] = __ldg(tb + tid + k * NT);
+      m[k] = neg_inf();
+      acc[k] = 0.f;
+    }
+    {  // prefetch split i0
+      const float* pil = a.Pi_src + (size_t)a.sp.sl[i0] * S;
+      const float* pir = a.Pi_src + (size_t)a.sp.sr[i0] * S;
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        if (s < S) {
+          cp_async4(stg + s, pil + s);
+          cp_async4(stg + NTV + s, pir + s);
+        }
+      }
+      cp_async_commit();
+    }
+    for (long long i = i0; i < i1; ++i) {
+      const int par = (int)((i - i0) & 1);
+      const float* Pl = stg + par * 2 * NTV;
+      const float* Pr = Pl + NTV;
+      cp_async_wait_all();
+      __syncthreads();
+      if (i + 1 < i1) {
+        float* nl = stg + (par ^ 1) * 2 * NTV;
+        const float* pil = a.Pi_src + (size_t)a.sp.sl[i + 1] * S;
+        const float* pir = a.Pi_src + (size_t)a.sp.sr[i + 1] * S;
+#pragma unroll
+        for (int k = 0; k < VF; ++k) {
+          const int s = tid + k * NT;
+          if (s < S) {
+            cp_async4(nl + s, pil + s);
+            cp_async4(nl + NTV + s, pir + s);
+          }
+        }
+        cp_async_commit();
+      }
+      const long long l = a.sp.sl[i], r = a.sp.sr[i];
+      const float* pbl = a.Pibar_src + (size_t)l * S;
+      const float* pbr = a.Pibar_src + (size_t)r * S;
+      const float lsp = a.sp.lsp[i];
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        if (s < S) {
+          const float ld = __ldg(c.log_pD + pb + s);
+          const float ls = __ldg(c.log_pS + pb + s);
+          const float vbr = __ldg(pbr + s), vbl = __ldg(pbl + s);
+          const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
+          const float pl = Pl[s], pr = Pr[s];
+          const float lss = lsp + ls;
+          const float v0 = (lsp + ld) + (pl + pr);
+          const float v1 = lsp + pl + vbr;
+          const float v2 = lsp + pr + vbl;
+          const float v3 = lss + (Pl[ca] + Pr[cbb]);
+          const float v4 = lss + (Pr[ca] + Pl[cbb]);
+          const float mx = fmaxf(fmaxf(fmaxf(m[k], v0), fmaxf(v1, v2)), fmaxf(v3, v4));
+          const float ms = safe_max(mx);
+          acc[k] = fmaf(acc[k], ex2(m[k] - ms),
+                        ((ex2(v0 - ms) + ex2(v1 - ms)) + (ex2(v2 - ms) + ex2(v3 - ms))) + ex2(v4 - ms));
+          m[k] = mx;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      x[k] = s < S ? lg2(acc[k]) + m[k] : neg_inf();
+      if (s < S) a.dts_save[(size_t)row * S + s] = x[k];
+    }
+  }
+  float m0 = neg_inf();
+#pragma unroll
+  for (int k = 0; k < VF; ++k) m0 = fmaxf(m0, x[k]);
+  const float Rd = safe_max(block_max(m0, red));  // scale of the initial row; syncs (staging done)
+
+  // ---- linear-space iterations (see level_forward_kernel) ----
+  unsigned ce[VF], tr[VF];
+  float z[VF], td[VF], kA[VF], kB[VF], kC1[VF], kC2[VF];
+  float zmax_l = 0.f, zsum_l = 0.f;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    const bool real = s < S;
+    ce[k] = __ldg(tb + NTV + s);
+    tr[k] = __ldg(tb + 2 * NTV + s);
+    kA[k] = real ? __ldg(c.linA + cb + s) : 0.f;
+    kB[k] = real ? __ldg(c.linB + cb + s) : 0.f;
+    kC1[k] = real ? __ldg(c.linC1 + cb + s) : 0.f;
+    kC2[k] = real ? __ldg(c.linC2 + cb + s) : 0.f;
+    z[k] = real ? ex2(x[k] - Rd) : 0.f;
+    td[k] = is_leaf ? (s == leaf ? ex2(leafv - Rd) : 0.f) : z[k];
+    sts_at(T0, tr[k] & 0xFFFFu) = z[k];
+    sts_at(T0, tr[k] >> 16) = -z[k];
+    zmax_l = fmaxf(zmax_l, z[k]);
+    zsum_l += z[k];
+  }
+  float R = Rd;
+  bool bad = false, fallback = false;
+  float dres = 0.f;
+  const int last = a.pi_iters - 1;
+  for (int it = 1; it <= last; ++it) {
+    char* Tc = (it & 1) ? T0 : T1;
+    char* Tn = (it & 1) ? T1 : T0;
+    if (__syncthreads_or(bad)) {
+      fallback = true;
+      break;
+    }
+    float g1[VF], g2[VF];
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      g1[k] = lds_at(Tc, ce[k] & 0xFFFFu);
+      g2[k] = lds_at(Tc, ce[k] >> 16);
+    }
+    float zmax = zmax_l, zsum = zsum_l;
+    tour_scan_sw<VF>(reinterpret_cast<float*>(Tc), red, zmax, zsum);
+    const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
+    const float Rn = zmax > 0.f ? R + lg2(zmax) : R;
+    const float fd = ex2(Rd - Rn);
+    unsigned mincode = 0xFFFFFFFFu;  // min over (bits(zn) - 1): < bits(2^-100) - 1 flags a tiny nonzero
+    zmax_l = 0.f;
+    zsum_l = 0.f;
+    const bool resid = (it == last) && (a.residual != nullptr);
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const float path = lds_at(Tc, tr[k] & 0xFFFFu) + z[k];
+      const float D = fmaxf(zsum - path, 0.f);
+      float lin = z[k] * kA[k];
+      lin = fmaf(D, kB[k], lin);
+      lin = fmaf(g1[k], kC1[k], lin);
+      lin = fmaf(g2[k], kC2[k], lin);
+      const float zn = fmaf(lin, inv, td[k] * fd);
+      mincode = min(mincode, (unsigned)__float_as_int(zn) - 1u);
+      if (resid && zn > 0.f && z[k] > 0.f) dres = fmaxf(dres, fabsf(lg2(zn) - lg2(z[k] * inv)));
+      z[k] = zn;
+      zmax_l = fmaxf(zmax_l, zn);
+      zsum_l += zn;
+      if (it < last) {
+        sts_at(Tn, tr[k] & 0xFFFFu) = zn;
+        sts_at(Tn, tr[k] >> 16) = -zn;
+      }
+    }
+    bad = mincode < 0x0D7FFFFFu;  // bits(2^-100) - 1
+    R = Rn;
+  }
+  if (!fallback && __syncthreads_or(bad)) fallback = true;
+
+  float pf[VF];  // final Pi (log values)
+  if (!fallback) {
+    if (a.residual) {
+      const float d = block_max(dres, red);
+      if (tid == 0) a.residual[row] = d;
+    }
+#pragma unroll
+    for (int k = 0; k < VF; ++k) pf[k] = lg2(z[k]) + R;
+  } else {
+    // log-space recomputation of the whole row from its initial values (rare)
+    if (tid == 0 && a.fallback_count) atomicAdd(a.fallback_count, 1);
+    float* P = sm;
+    float* X = sm + NTV;
+    float* Y = sm + 2 * NTV;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      x[k] = s >= S ? neg_inf() : (is_leaf ? leaf_seed(c, cb, item, leaf, s) : a.dts_save[(size_t)row * S + s]);
+      P[s] = x[k];
+    }
+    __syncthreads();
+    float nv[VF];
+    for (int it = 1; it < a.pi_iters; ++it) {
+      log_iter<VF>(P, X, Y, red, c, cb, leaf, leafv, is_leaf ? nullptr : x, nv);
+      if (a.residual && it == a.pi_iters - 1) {
+        float d = 0.f;
+#pragma unroll
+        for (int k = 0; k < VF; ++k) {
+          const int s = tid + k * NT;
+          if (s < S && !is_neg_inf(nv[k]) && !is_neg_inf(P[s])) d = fmaxf(d, fabsf(nv[k] - P[s]));
+        }
+        d = block_max(d, red);
+        if (tid == 0) a.residual[row] = d;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        if (s < S) P[s] = nv[k];
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      pf[k] = s < S ? P[s] : neg_inf();
+    }
+    __syncthreads();
+  }
+
+  // ---- final Pi, row max, Pibar (from the final log row, as the reference computes them) ----
+  float* prow = a.pi + (size_t)row * S;
+  float mx = neg_inf();
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    if (s < S) prow[s] = pf[k];
+    mx = fmaxf(mx, pf[k]);
+  }
+  // the tour buffer not read by the last iteration (T0 when pi_iters-1 is odd) takes the weights
+  char* Tf = fallback ? T1 : ((last & 1) ? T1 : T0);
+  float* Tff = reinterpret_cast<float*>(Tf);
+  const float row_max = block_max(mx, red);
+  const float rms = safe_max(row_max);
+  float pe[VF];
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    pe[k] = s < S ? ex2(pf[k] - rms) : 0.f;
+    sts_at(Tf, tr[k] & 0xFFFFu) = pe[k];
+    sts_at(Tf, tr[k] >> 16) = -pe[k];
+    sum += pe[k];
+  }
+  __syncthreads();
+  float unused = 0.f;
+  tour_scan_sw<VF>(Tff, red, unused, sum);
+  float* brow = a.pibar + (size_t)row * S;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    if (s < S) {
+      const float denom = sum - (lds_at(Tf, tr[k] & 0xFFFFu) + pe[k]);
+      brow[s] = denom > 0.f ? lg2(denom) + row_max + c.mc[cb + s] : neg_inf();
+    }
+  }
+  if (tid == 0) a.row_max[row] = row_max;
+}
+
+// ------------------------------------------------------------------------------------------
+// tangent (forward-mode JVP) of one dependency level, every (row, direction) pair
+// ------------------------------------------------------------------------------------------
+//
+// Restates, per row, newton/forward_tangent.py:150-193 for one wave row: the split tangent
+// reduction (kbench/core/kernels/dts_tangent.py:23-96) followed by n_iters fixed-count Jacobi
+// steps of the linearised wave step at the frozen primal row (wave_tangent.py:186-336), starting
+// from a zero tangent.  The primal weights are folded into per-column coefficients once:
+//   dPi' = cA dPi + c2 (dRS - dAS) + c3 dPi[c1] + c4 dPi[c2] + cst
+// with dRS = sum_s r dPi, dAS = ancestor-or-self sum of r dPi (one Euler-tour scan per step),
+// r = 2^(Pi - rowmax); dPibar = (dRS - dAS) / denom + dmc where the primal denominator is > 0.
+
+struct TanArgs {
+  SplitCSR sp;
+  const float* Pi;      // primal [C,S]
+  const float* Pibar;
+  const float* dts;     // primal split reductions [C,S] (rows with splits)
+  float* dPi;           // [D, C, S]
+  float* dPibar;
+  long long dstride;    // C * S
+  const float* mc;      // primal constants (item * crs + s)
+  const float* dl;
+  const float* ebar;
+  const float* e;
+  const float* sl1;
+  const float* sl2;
+  const float* leaf_logp;  // item * S + s
+  const float* log_pD;     // item * prs + s
+  const float* log_pS;
+  long long crs, prs;
+  const float* dmc;     // tangent constants: direction * tstride + item * crs + s
+  const float* ddl;
+  const float* debar;
+  const float* de;
+  const float* dsl1;
+  const float* dsl2;
+  const float* dleaf;   // direction * tstride + item * S + s
+  const float* dpD;     // direction * tstride + item * prs + s
+  const float* dpS;
+  long long tstride;
+  const long long* item_idx;
+  const int* leaf_state;
+  const unsigned* tb;   // [3, NTV] tour tables
+  int n_iters;
+  int S;
+};
+
+template <int VF>
+__global__ void __launch_bounds__(512, 1) level_tangent_kernel(TanArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const unsigned* __restrict__ tb = a.tb;
+  const int S = a.S;
+  const int NT = blockDim.x;
+  const int NTV = NT * VF;
+  const int TB = 2 * NTV;
+  char* T0 = reinterpret_cast<char*>(sm);
+  char* T1 = reinterpret_cast<char*>(sm + TB);
+  float* DP0 = sm + 2 * TB;
+  float* DP1 = DP0 + NTV;
+  float* PR = DP1 + NTV;
+  float* red = PR + NTV;
+  const int tid = threadIdx.x;
+  const int b = blockIdx.x;
+  const int d = blockIdx.y;
+  const long long row = a.sp.rows[b];
+  const long long item = a.item_idx[row];
+  const size_t cb = (size_t)(item * a.crs);
+  const size_t pb = (size_t)(item * a.prs);
+  const size_t tof = (size_t)d * a.tstride;
+  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
+  const bool has_splits = i1 > i0;
+  const int leaf_raw = a.leaf_state[row];
+  const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
+
+  unsigned ccol[VF], tr[VF];
+  float pv[VF], r[VF];
+  float m = neg_inf();
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    ccol[k] = __ldg(tb + s);
+    tr[k] = __ldg(tb + 2 * NTV + s);
+    pv[k] = s < S ? a.Pi[(size_t)row * S + s] : neg_inf();
+    PR[s] = pv[k];
+    m = fmaxf(m, pv[k]);
+  }
+  const float row_max = block_max(m, red);
+  const float rms = safe_max(row_max);
+  float rsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    r[k] = ex2(pv[k] - rms);  // 0 on padding (-inf)
+    sts_at(T0, tr[k] & 0xFFFFu) = r[k];
+    sts_at(T0, tr[k] >> 16) = -r[k];
+    rsum += r[k];
+  }
+  __syncthreads();
+  float unused = 0.f;
+  tour_scan_sw<VF>(reinterpret_cast<float*>(T0), red, unused, rsum);
+  const float row_sum = rsum;
+  float cA[VF], c2[VF], c3[VF], c4[VF], cst[VF], cD[VF], invd[VF];
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    cA[k] = c2[k] = c3[k] = c4[k] = cst[k] = cD[k] = invd[k] = 0.f;
+    if (s < S) {
+      const float denom = row_sum - (lds_at(T0, tr[k] & 0xFFFFu) + r[k]);
+      const bool pos = denom > 0.f;
+      const float sd = pos ? denom : 1.f;
+      invd[k] = pos ? 1.0f / sd : 0.f;
+      const float pibar = pos ? lg2(sd) + row_max + a.mc[cb + s] : neg_inf();
+      const float t0 = a.dl[cb + s] + pv[k];
+      const float t1 = pv[k] + a.ebar[cb + s];
+      const float t2 = pibar + a.e[cb + s];
+      const float t3 = a.sl1[cb + s] + PR[ccol[k] & 0xFFFFu];
+      const float t4 = a.sl2[cb + s] + PR[ccol[k] >> 16];
+      const bool hit = s == leaf;
+      const float t5 = hit ? a.leaf_logp[(size_t)item * S + s] : neg_inf();
+      const float dv = has_splits ? a.dts[(size_t)row * S + s] : neg_inf();
+      const float mm = fmaxf(fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5)), dv);
+      const float ms = safe_max(mm);
+      const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
+                  e5 = ex2(t5 - ms), ed = ex2(dv - ms);
+      const float tot = ((e0 + e1) + (e2 + e3)) + ((e4 + e5) + ed);
+      if (!is_neg_inf(lg2(tot) + mm)) {
+        const float inv = tot > 0.f ? 1.0f / tot : 0.f;
+        const float dt5 = hit ? a.dleaf[tof + (size_t)item * S + s] : 0.f;
+        const float dmcv = pos ? a.dmc[tof + cb + s] : 0.f;
+        const float k0 = e0 * a.ddl[tof + cb + s] + e1 * a.debar[tof + cb + s] + e2 * (dmcv + a.de[tof + cb + s]) +
+                         e3 * a.dsl1[tof + cb + s] + e4 * a.dsl2[tof + cb + s] + e5 * dt5;
+        cA[k] = (e0 + e1) * inv;
+        c2[k] = e2 * inv * invd[k];
+        c3[k] = e3 * inv;
+        c4[k] = e4 * inv;
+        cst[k] = k0 * inv;
+        cD[k] = ed * inv;
+      }
+    }
+  }
+
+  __syncthreads();  // the primal row in PR is no longer gathered: it keeps 1/denom from here on
+#pragma unroll
+  for (int k = 0; k < VF; ++k) PR[tid + k * NT] = invd[k];
+
+  // ---- split tangent reduction: d_dts[s] = sum_splits sum_k 2^(t_k - dts[s]) dt_k ----
+  if (has_splits) {
+    float* Pl = sm;  // staging in the tour buffers: Pi_l, Pi_r, dPi_l, dPi_r
+    float* Pr = sm + NTV;
+    float* Ql = sm + 2 * NTV;
+    float* Qr = sm + 3 * NTV;
+    const float* dts_row = a.dts + (size_t)row * S;
+    const float* dPi_d = a.dPi + (size_t)d * a.dstride;
+    const float* dPb_d = a.dPibar + (size_t)d * a.dstride;
+    for (long long i = i0; i < i1; ++i) {
+      const long long l = a.sp.sl[i], rr = a.sp.sr[i];
+      const float lsp = a.sp.lsp[i];
+      __syncthreads();  // previous readers of the staging buffers (or of the scan) are done
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        const bool real = s < S;
+        Pl[s] = real ? a.Pi[(size_t)l * S + s] : neg_inf();
+        Pr[s] = real ? a.Pi[(size_t)rr * S + s] : neg_inf();
+        Ql[s] = real ? dPi_d[(size_t)l * S + s] : 0.f;
+        Qr[s] = real ? dPi_d[(size_t)rr * S + s] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        const float dts = s < S ? __ldg(dts_row + s) : neg_inf();
+        if (!is_neg_inf(dts)) {
+          const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
+          const float ld = __ldg(a.log_pD + pb + s), ls = __ldg(a.log_pS + pb + s);
+          const float dld = a.dpD[tof + pb + s], dls = a.dpS[tof + pb + s];
+          const float pl = Pl[s], pr = Pr[s];
+          const float t0 = lsp + ld + pl + pr;
+          const float t1 = lsp + pl + a.Pibar[(size_t)rr * S + s];
+          const float t2 = lsp + pr + a.Pibar[(size_t)l * S + s];
+          const float t3 = lsp + ls + Pl[ca] + Pr[cbb];
+          const float t4 = lsp + ls + Pr[ca] + Pl[cbb];
+          const float dt0 = dld + Ql[s] + Qr[s];
+          const float dt1 = Ql[s] + dPb_d[(size_t)rr * S + s];
+          const float dt2 = Qr[s] + dPb_d[(size_t)l * S + s];
+          const float dt3 = dls + Ql[ca] + Qr[cbb];
+          const float dt4 = dls + Qr[ca] + Ql[cbb];
+          cst[k] = fmaf(cD[k], ex2(t0 - dts) * dt0 + ex2(t1 - dts) * dt1 + ex2(t2 - dts) * dt2 +
+                                   ex2(t3 - dts) * dt3 + ex2(t4 - dts) * dt4, cst[k]);
+        }
+      }
+    }
+  }
+
+  // ---- fixed-count Jacobi steps from a zero tangent (the first one gives dPi = cst) ----
+  float dp[VF], D[VF];
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    dp[k] = cst[k];
+    D[k] = 0.f;
+  }
+  for (int it = 1; it < a.n_iters; ++it) {
+    char* Tc = (it & 1) ? T0 : T1;
+    float* Dc = (it & 1) ? DP0 : DP1;
+    __syncthreads();  // previous step's (or the setup's) readers of Tc / Dc are done
+    float ds = 0.f;
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      const float v = r[k] * dp[k];
+      sts_at(Tc, tr[k] & 0xFFFFu) = v;
+      sts_at(Tc, tr[k] >> 16) = -v;
+      Dc[s] = dp[k];
+      ds += v;
+    }
+    __syncthreads();
+    float g1[VF], g2[VF];
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      g1[k] = Dc[ccol[k] & 0xFFFFu];
+      g2[k] = Dc[ccol[k] >> 16];
+    }
+    tour_scan_sw<VF>(reinterpret_cast<float*>(Tc), red, unused, ds);
+    const float dRS = ds;
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      D[k] = dRS - (lds_at(Tc, tr[k] & 0xFFFFu) + r[k] * dp[k]);
+      dp[k] = cA[k] * dp[k] + c2[k] * D[k] + c3[k] * g1[k] + c4[k] * g2[k] + cst[k];
+    }
+  }
+  float* outp = a.dPi + (size_t)d * a.dstride + (size_t)row * S;
+  float* outb = a.dPibar + (size_t)d * a.dstride + (size_t)row * S;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    if (s < S) {
+      outp[s] = dp[k];
+      const float iv = PR[s];
+      outb[s] = iv > 0.f ? D[k] * iv + a.dmc[tof + cb + s] : 0.f;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------
 
@@ -920,6 +1542,17 @@ int engine_width(int S, int& bd) {
   return v;
 }
 
+// Padded width, threads and columns per thread of the forward tour kernel (mirrors
+// kbench_b200/tree.py tour_layout): NTV = smallest power of two > S (>= 64); 0 when NTV > 4096.
+int tour_layout(int S, int& nt, int& vf) {
+  int ntv = 64;
+  while (ntv <= S) ntv <<= 1;
+  if (ntv > 4096) return 0;
+  vf = ntv / 32 < 8 ? ntv / 32 : 8;
+  nt = ntv / vf;
+  return ntv;
+}
+
 // Up to 1024 threads per row (4 columns per thread at S = 4095).
 int vpt_pick_wide(int S, int& bd) {
   bd = 1024;
@@ -983,8 +1616,8 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
                                 const int* node_parent, const int* node_child1, const int* node_child2,
                                 const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                                 const long long* item_idx, const int* leaf_state, const unsigned* packed,
-                                int pi_iters, int S, void* stream) {
-  if (S <= 0 || n_rows < 0 || K < 0 || pi_iters < 2) return KB_ERR_ARG;
+                                const unsigned* tour_tables, int pi_iters, int S, void* stream) {
+  if (S <= 0 || n_rows < 0 || K < 0 || pi_iters < 2 || use_col_weights != 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
   FwdArgs a;
@@ -996,10 +1629,33 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   a.Pi_src = Pi_src; a.Pibar_src = Pibar_src; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = n_rows;
   a.pi_iters = pi_iters;
+  cudaStream_t st = (cudaStream_t)stream;
+  int nt4, vf4;
+  const int ntv4 = tour_layout(S, nt4, vf4);
+  if (tour_tables != nullptr && ntv4 > 0) {
+    if (dts_save == nullptr) return KB_ERR_ARG;  // the log-space fallback re-reads the split reduction
+    Fwd4Args a4;
+    a4.f = a;
+    a4.tb = tour_tables;
+    const size_t smem4 = (size_t)(4 * ntv4 + 96) * sizeof(float);
+#define KB_LF4_CASE(V)                                                                                        \
+  case V:                                                                                                     \
+    if (smem4 > 48 * 1024 && cudaFuncSetAttribute((const void*)level_forward_tour_kernel<V>,                 \
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4)) \
+      return KB_ERR_LAUNCH;                                                                                   \
+    level_forward_tour_kernel<V><<<n_rows, nt4, smem4, st>>>(a4);                                             \
+    break;
+    switch (vf4) {
+      KB_LF4_CASE(2) KB_LF4_CASE(4) KB_LF4_CASE(8)
+      default: return KB_ERR_SIZE;
+    }
+#undef KB_LF4_CASE
+    return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+  }
+  if (packed == nullptr) return KB_ERR_ARG;
   int bd;
   const int vpt = engine_width(S, bd);
   const size_t smem = (size_t)(6 * bd * vpt + 128) * sizeof(float);
-  cudaStream_t st = (cudaStream_t)stream;
 #define KB_LF_CASE(V)                                                                                     \
   case V:                                                                                                 \
     if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_forward_kernel<V>,                   \
@@ -1067,3 +1723,54 @@ extern "C" int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
 
+extern "C" int kb_tour_layout(int S, int* ntv, int* threads, int* cols_per_thread) {
+  if (S <= 0 || ntv == nullptr || threads == nullptr || cols_per_thread == nullptr) return KB_ERR_ARG;
+  int nt = 0, vf = 0;
+  const int n = tour_layout(S, nt, vf);
+  *ntv = n;
+  *threads = nt;
+  *cols_per_thread = vf;
+  return n > 0 ? KB_OK : KB_ERR_SIZE;
+}
+
+extern "C" int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
+                                const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
+                                const float* dts_saved, float* dPi, float* dPibar, long long dir_stride, int D,
+                                const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
+                                const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
+                                long long param_row_stride, long long const_row_stride, const float* dMC,
+                                const float* dDL, const float* dEbar, const float* dE, const float* dSL1,
+                                const float* dSL2, const float* dleaf, const float* dpD, const float* dpS,
+                                long long tangent_dir_stride, const long long* item_idx, const int* leaf_state,
+                                const unsigned* tour_tables, int n_iters, int S, void* stream) {
+  if (S <= 0 || n_rows < 0 || D <= 0 || n_iters < 1 || tour_tables == nullptr || dts_saved == nullptr)
+    return KB_ERR_ARG;
+  int nt, vf;
+  const int ntv = tour_layout(S, nt, vf);
+  if (ntv == 0) return KB_ERR_SIZE;
+  if (n_rows == 0) return KB_OK;
+  TanArgs a;
+  a.sp = SplitCSR{rows, split_ptr, sl, sr, lsp};
+  a.Pi = Pi; a.Pibar = Pibar; a.dts = dts_saved; a.dPi = dPi; a.dPibar = dPibar; a.dstride = dir_stride;
+  a.mc = mc; a.dl = dl; a.ebar = ebar; a.e = e; a.sl1 = sl1; a.sl2 = sl2; a.leaf_logp = leaf_logp;
+  a.log_pD = log_pD; a.log_pS = log_pS; a.crs = const_row_stride; a.prs = param_row_stride;
+  a.dmc = dMC; a.ddl = dDL; a.debar = dEbar; a.de = dE; a.dsl1 = dSL1; a.dsl2 = dSL2; a.dleaf = dleaf;
+  a.dpD = dpD; a.dpS = dpS; a.tstride = tangent_dir_stride; a.item_idx = item_idx; a.leaf_state = leaf_state;
+  a.tb = tour_tables; a.n_iters = n_iters; a.S = S;
+  const size_t smem = (size_t)(7 * ntv + 96) * sizeof(float);
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid(n_rows, D);
+#define KB_LT_CASE(V)                                                                                          \
+  case V:                                                                                                      \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_tangent_kernel<V>,                        \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))     \
+      return KB_ERR_LAUNCH;                                                                                    \
+    level_tangent_kernel<V><<<grid, nt, smem, st>>>(a);                                                        \
+    break;
+  switch (vf) {
+    KB_LT_CASE(2) KB_LT_CASE(4) KB_LT_CASE(8)
+    default: return KB_ERR_SIZE;
+  }
+#undef KB_LT_CASE
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}

@@ -138,7 +138,7 @@ class LevelTimer:
         a.record()
         fn()
         b.record()
-        self.events[name].append((level, a, b))
+        self.events.setdefault(name, []).append((level, a, b))
 
     def totals(self):
         """{kernel: (total_ms, n_launches, per-level list of (level, ms))} after a sync."""
@@ -161,9 +161,46 @@ def _launch(static, name, level, *args):
         timer.wrap(name, level, lambda: _lib.call(name, *args))
 
 
-def forward(static, theta, col_weights, *, pi_residual_out=None):
+@dataclass
+class Prep:
+    """Everything the level kernels need that depends only on theta and the species tree (so it
+    is shared by every chunk of a family batch): parameters, the E fixed point and the per-column
+    constants of the row update."""
+    pS: torch.Tensor
+    pD: torch.Tensor
+    pL: torch.Tensor
+    mc: torch.Tensor
+    clp: torch.Tensor
+    ucw: bool
+    E: torch.Tensor
+    E_s1: torch.Tensor
+    E_s2: torch.Tensor
+    Ebar: torch.Tensor
+    k: dict
+    lin: torch.Tensor
+
+
+@torch.no_grad()
+def prepare(static, theta, col_weights) -> Prep:
+    """Parameters, E fixed point (``glue.solve_parameters`` / ``glue.solve_e``) and the linear
+    constants ``2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2`` of the forward's row update."""
+    S = int(static.state_helpers["S"])
+    pS, pD, pL, mc, clp, ucw = glue.solve_parameters(static, theta, col_weights)
+    E, E_s1, E_s2, Ebar = glue.solve_e(static, pS, pD, pL, mc, clp, ucw, theta)
+    k = glue.wave_constants(E, Ebar, E_s1, E_s2, pS, pD, mc, S)
+    dev = E.device
+    G = int(E.shape[0])
+    lin = torch.empty((4, G, S), device=dev, dtype=torch.float32)
+    _lib.call("kb_lin_consts", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(), k["e"].data_ptr(),
+              k["sl1"].data_ptr(), k["sl2"].data_ptr(), G * S, lin[0].data_ptr(), lin[1].data_ptr(),
+              lin[2].data_ptr(), lin[3].data_ptr(), _lib.stream_handle(dev))
+    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin)
+
+
+def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | None = None):
     """theta -> the 13 forward intermediates (same order as ``glue.solve_e_pi``) and the saved
-    split reductions ``dts_wave`` [C,S] for the backward."""
+    split reductions ``dts_wave`` [C,S] for the backward.  ``prep`` (from :func:`prepare` on the
+    same theta and species tree) skips the parameter / E-step stage."""
     if not supported(static):
         return glue.solve_e_pi(static, theta, col_weights, pi_residual_out=pi_residual_out), {}
     so = static.solver_options
@@ -173,16 +210,19 @@ def forward(static, theta, col_weights, *, pi_residual_out=None):
     tt = topo.tt
     sh, wl = static.state_helpers, static.wave_layout
     S = int(sh["S"])
-    pS, pD, pL, mc, clp, ucw = glue.solve_parameters(static, theta, col_weights)
-    E, E_s1, E_s2, Ebar = glue.solve_e(static, pS, pD, pL, mc, clp, ucw, theta)
-    k = glue.wave_constants(E, Ebar, E_s1, E_s2, pS, pD, mc, S)
+    if prep is None:
+        if not glue.col_weights_are_uniform(col_weights):
+            # the level kernels' linear-space update assumes uniform column weights (the layout of
+            # every benchmark config); weighted columns take the wrapper-by-wrapper driver
+            return glue.solve_e_pi(static, theta, col_weights, pi_residual_out=pi_residual_out), {}
+        prep = prepare(static, theta, col_weights)
+    elif prep.ucw:
+        raise ValueError("the fused engine needs uniform column weights")
+    pS, pD, pL, mc, clp, ucw = prep.pS, prep.pD, prep.pL, prep.mc, prep.clp, prep.ucw
+    E, E_s1, E_s2, Ebar, k, lin = prep.E, prep.E_s1, prep.E_s2, prep.Ebar, prep.k, prep.lin
     dev = E.device
     G = int(E.shape[0])
     st = _lib.stream_handle(dev)
-    lin = torch.empty((4, G, S), device=dev, dtype=torch.float32)
-    _lib.call("kb_lin_consts", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(), k["e"].data_ptr(),
-              k["sl1"].data_ptr(), k["sl2"].data_ptr(), G * S, lin[0].data_ptr(), lin[1].data_ptr(),
-              lin[2].data_ptr(), lin[3].data_ptr(), st)
     C = int(wl["leaf_state_index"].numel())
     pi = torch.empty((C, S), device=dev, dtype=torch.float32)
     pibar = torch.empty((C, S), device=dev, dtype=torch.float32)
@@ -210,16 +250,36 @@ def forward(static, theta, col_weights, *, pi_residual_out=None):
                   pSp.data_ptr(), prs, crs, f32(clp).data_ptr(), int(ucw), tt.parent.data_ptr(),
                   tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
                   tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
-                  int(so.pi_iters), S, st)
+                  _lib.ptr(tt.tour if getattr(static, "_tour_forward", True) else None), int(so.pi_iters), S, st)
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
     return out, {"dts_wave": dts}
 
 
+def new_grad_slots(static, dev) -> torch.Tensor:
+    """Zeroed fp64 per-CTA accumulators ``[n_slots, 8, NTV]`` of the backward's column sums
+    (rows: pD, pS, mt, E, Ebar, E_s1, E_s2, col)."""
+    bd, vpt = tree.engine_width(int(static.state_helpers["S"]))
+    return torch.zeros((_sm_count(dev), 8, bd * vpt), device=dev, dtype=torch.float64)
+
+
+def grad_accumulators_from(E, S, acc8) -> glue.GradAccumulators:
+    """``GradAccumulators`` from the reduced column sums ``acc8`` [8, >=S] (any float dtype)."""
+    g = glue.GradAccumulators(E, S, E.device)
+    for j, name in enumerate(("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2")):
+        getattr(g, name)[0].copy_(acc8[j, :S])
+    g.col.copy_(acc8[7, :S])
+    return g
+
+
 @torch.no_grad()
-def backward(static, theta, col_weights, saved, *, v_out=None):
+def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finish=True):
     """(forward intermediates) -> (grad_theta, grad_col); uses ``saved["dts_wave"]`` when the
-    forward was run by this engine, otherwise recomputes the split reductions."""
+    forward was run by this engine, otherwise recomputes the split reductions.
+
+    ``slots`` (from :func:`new_grad_slots`) accumulates the column sums into caller-owned fp64
+    accumulators, so several chunks of a family batch add into one set; with ``finish=False``
+    the E-adjoint / theta VJP is left to the caller and ``None`` is returned."""
     if not supported(static):
         return glue.implicit_grad(static, theta, col_weights, saved)
     so = static.solver_options
@@ -235,15 +295,22 @@ def backward(static, theta, col_weights, saved, *, v_out=None):
     st = _lib.stream_handle(dev)
     E = saved["E"]
     ucw = not glue.col_weights_are_uniform(col_weights)
+    if ucw:
+        if not finish:
+            raise ValueError("the fused engine needs uniform column weights")
+        return glue.implicit_grad(static, theta, col_weights, saved)
     k = glue.wave_constants(E, saved["Ebar"], saved["E_s1"], saved["E_s2"], saved["log_pS"], saved["log_pD"],
                             saved["max_coupling"], S)
     G = int(E.shape[0])
     acc = torch.zeros((C, S), device=dev, dtype=torch.float32)
     roots = wl["root_row_ids"]
     acc.index_copy_(0, roots, glue.root_rhs(Pi, roots))
-    n_slots = _sm_count(dev)
+    if slots is None:
+        slots = new_grad_slots(static, dev)
+    n_slots = int(slots.shape[0])
     bd, vpt = tree.engine_width(S)
-    slots = torch.zeros((n_slots, 8, bd * vpt), device=dev, dtype=torch.float64)
+    if tuple(slots.shape[1:]) != (8, bd * vpt) or slots.dtype != torch.float64:
+        raise ValueError("grad slots must be float64 [n_slots, 8, NTV] (engine.new_grad_slots)")
     dts = saved.get("dts_wave")
     leaf_state = i32(wl["leaf_state_index"])
     item_idx = i64(static.rate_item_idx)
@@ -268,10 +335,9 @@ def backward(static, theta, col_weights, saved, *, v_out=None):
                 prs, crs, clp.data_ptr(), int(ucw), item_idx.data_ptr(), leaf_state.data_ptr(),
                 tt.packed_pad.data_ptr(), S, st)
     static._last_acc = acc
+    if not finish:
+        return None
     out8 = torch.empty((8, S), device=dev, dtype=torch.float32)
     _lib.call("kb_reduce_grad_slots", slots.data_ptr(), n_slots, S, out8.data_ptr(), st)
-    g = glue.GradAccumulators(E, S, dev)
-    for j, name in enumerate(("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2")):
-        getattr(g, name)[0].copy_(out8[j])
-    g.col.copy_(out8[7])
+    g = grad_accumulators_from(E, S, out8)
     return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)

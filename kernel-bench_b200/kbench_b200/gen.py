@@ -177,22 +177,25 @@ def make_species_tree(n_leaves: int, seed: int) -> dict:
 # ----------------------------------------------------------------------------------------------
 
 def _nni(left, right, parent, root, n_moves, rng):
-    """Random nearest-neighbour interchanges, in place: for a random internal node v with an
-    internal parent u, swap one child of v with v's sibling.  The root is unchanged."""
-    internal = np.nonzero(left >= 0)[0]
+    """Random nearest-neighbour interchanges, in place (Python lists): for a random internal node
+    v with an internal parent u, swap one child of v with v's sibling.  The root is unchanged."""
+    internal = [i for i, x in enumerate(left) if x >= 0]
+    n_int = len(internal)
+    integers, random = rng.integers, rng.random
     for _ in range(n_moves):
-        v = int(internal[int(rng.integers(internal.shape[0]))])
-        u = int(parent[v])
+        v = internal[int(integers(n_int))]
+        u = parent[v]
         if u < 0:
             continue
-        w = int(right[u]) if int(left[u]) == v else int(left[u])
-        if rng.random() < 0.5:
-            b = int(left[v])
+        lu = left[u]
+        w = right[u] if lu == v else lu
+        if random() < 0.5:
+            b = left[v]
             left[v] = w
         else:
-            b = int(right[v])
+            b = right[v]
             right[v] = w
-        if int(left[u]) == w:
+        if left[u] == w:
             left[u] = b
         else:
             right[u] = b
@@ -202,28 +205,33 @@ def _nni(left, right, parent, root, n_moves, rng):
 
 
 def _clades(left, right, root, weights):
-    """Postorder clade hashes. Returns list of (hash, size, hash_left, hash_right) per internal
-    node plus the leaf hashes."""
-    n_nodes = left.shape[0]
+    """Postorder clade hashes (Python lists in, ``weights`` the leaf hashes as ints). Returns
+    list of (hash, size, hash_left, hash_right) per internal node."""
+    n_nodes = len(left)
     h = [0] * n_nodes
     sz = [1] * n_nodes
     out = []
-    stack = [(root, False)]
+    append = out.append
+    stack = [root]
+    pop, push = stack.pop, stack.append
     while stack:
-        node, done = stack.pop()
-        lc = int(left[node])
-        if lc < 0:
-            h[node] = int(weights[node])
+        node = pop()
+        if node < 0:                      # second visit of an internal node (encoded ~node)
+            node = ~node
+            lc, rc = left[node], right[node]
+            hx = (h[lc] + h[rc]) & MASK64
+            h[node] = hx
+            sx = sz[lc] + sz[rc]
+            sz[node] = sx
+            append((hx, sx, h[lc], h[rc]))
             continue
-        rc = int(right[node])
-        if done:
-            h[node] = (h[lc] + h[rc]) & MASK64
-            sz[node] = sz[lc] + sz[rc]
-            out.append((h[node], sz[node], h[lc], h[rc]))
-        else:
-            stack.append((node, True))
-            stack.append((rc, False))
-            stack.append((lc, False))
+        lc = left[node]
+        if lc < 0:
+            h[node] = weights[node]
+            continue
+        push(~node)
+        push(right[node])
+        push(lc)
     return out
 
 
@@ -235,41 +243,50 @@ def make_family(cfg: ProblemConfig, species: dict, seed: int, *, alpha: float = 
     weights = rng.integers(0, 2 ** 63, size=G, dtype=np.int64).astype(np.uint64) * _U64(2) + _U64(1)
     leaf_species = species["_species_leaves"][rng.integers(0, len(species["_species_leaves"]), size=G)]
     base_l, base_r, base_p, base_root = _random_merge_tree(G, rng)
+    base_l, base_r, base_p = base_l.tolist(), base_r.tolist(), base_p.tolist()
+    wlist = [int(w) for w in weights]
     clade_size = {}
     clade_count = {}
     splits = {}        # clade hash -> {split key: observed count}
     for t in range(cfg.n_topologies):
-        left, right, parent = base_l.copy(), base_r.copy(), base_p.copy()
+        left, right, parent = list(base_l), list(base_r), list(base_p)
         root = base_root
         if t > 0:
             root = _nni(left, right, parent, root, cfg.spr_moves, rng)
-        for hx, sx, ha, hb in _clades(left, right, root, weights):
+        for hx, sx, ha, hb in _clades(left, right, root, wlist):
             clade_size[hx] = sx
             clade_count[hx] = clade_count.get(hx, 0) + 1
             key = (ha, hb) if ha < hb else (hb, ha)
             d = splits.setdefault(hx, {})
             d[key] = d.get(key, 0) + 1
-        root_hash = int(sum(int(w) for w in weights) & MASK64)
-    leaf_hashes = [int(w) for w in weights]
+    root_hash = sum(wlist) & MASK64
+    leaf_hashes = wlist
     for g, hw in enumerate(leaf_hashes):
         clade_size[hw] = 1
     # amalgamation: splits a few rearrangements away whose parts are both clades
+    cs_get = clade_size.get
+    sp_get = splits.get
     for _round in range(amalg_rounds):
         added = {}
         for hx, d in splits.items():
             extra = {}
-            for (ha, hb) in list(d.keys()):
+            for (ha, hb) in list(d):
                 for (hc, ho) in ((ha, hb), (hb, ha)):
-                    sub = splits.get(hc)
+                    sub = sp_get(hc)
                     if not sub:
                         continue
-                    for (h1, h2) in sub.keys():
-                        for (keep, move) in ((h1, h2), (h2, h1)):
-                            hy = (move + ho) & MASK64
-                            if clade_size.get(hy, 0) == clade_size[move] + clade_size[ho]:
-                                key = (keep, hy) if keep < hy else (hy, keep)
-                                if key not in d:
-                                    extra[key] = 0
+                    s_ho = clade_size[ho]
+                    for (h1, h2) in sub:
+                        hy = (h2 + ho) & MASK64     # move h2 next to ho, keep h1
+                        if cs_get(hy, 0) == clade_size[h2] + s_ho:
+                            key = (h1, hy) if h1 < hy else (hy, h1)
+                            if key not in d:
+                                extra[key] = 0
+                        hy = (h1 + ho) & MASK64     # move h1 next to ho, keep h2
+                        if cs_get(hy, 0) == clade_size[h1] + s_ho:
+                            key = (h2, hy) if h2 < hy else (hy, h2)
+                            if key not in d:
+                                extra[key] = 0
             if extra:
                 added[hx] = extra
         if not added:

@@ -47,6 +47,58 @@ def engine_width(S: int) -> tuple[int, int]:
     return bd, vpt
 
 
+def tour_layout(S: int):
+    """(NTV, threads, columns per thread) of the forward tour kernel, or None where it does not
+    apply (rows wider than 4096 padded columns): NTV is the smallest power of two > S (at least
+    64), 8 columns per thread where the row is wide enough.  Mirrors ``tour_layout`` in
+    csrc/kb_engine.cu."""
+    ntv = max(64, 1 << int(S).bit_length())
+    if ntv > 4096:
+        return None
+    vf = min(8, ntv // 32)
+    return ntv, ntv // vf, vf
+
+
+def tour_phys(i, vf: int):
+    """Swizzled shared-memory position of logical tour index i in the forward tour kernel: thread
+    t scans the 2*vf entries [t*2vf, (t+1)*2vf) as vf/2 float4 groups whose order inside the chunk
+    is XOR-permuted by (t // (8 // groups)) so a quarter-warp's vector loads hit distinct banks."""
+    import numpy as np
+    i = np.asarray(i, dtype=np.int64)
+    ch = 2 * vf
+    q_n = ch // 4
+    if q_n == 1:
+        return i
+    t, j = i // ch, i % ch
+    q, r = j // 4, j % 4
+    sw = (t // (8 // q_n)) & (q_n - 1)
+    return t * ch + 4 * (q ^ sw) + r
+
+
+def pack_forward(parent, child1, child2, sub_start, sub_end):
+    """[3, NTV] uint32 tables (viewed as int32) of the forward tour kernel, for NTV, VF =
+    tour_layout(S):
+
+    row 0  children columns c1 | c2 << 16 (a missing child -> the zero column Z = NTV-1)
+    row 1  BYTE offsets of the children's enter slots in a tour buffer (lo | hi << 16)
+    row 2  BYTE offsets of the column's own enter | exit slots
+    """
+    import numpy as np
+    S = len(parent)
+    lay = tour_layout(S)
+    if lay is None:
+        raise ValueError("row too wide for the forward tour kernel")
+    ntv, _, vf = lay
+    pk = pack_columns(parent, child1, child2, sub_start, sub_end, ntv=ntv).view(np.uint32).astype(np.int64)
+    c1, c2 = pk[0] & 0xFFFF, pk[0] >> 16
+    enter, exit_ = pk[1] & 0xFFFF, pk[1] >> 16
+    be, bx = 4 * tour_phys(enter, vf), 4 * tour_phys(exit_, vf)
+    if max(be.max(), bx.max()) > 0xFFFF:
+        raise ValueError("tour byte offsets exceed 16 bits")
+    out = np.stack([c1 | (c2 << 16), be[c1] | (be[c2] << 16), be | (bx << 16)])
+    return out.astype(np.uint32).view(np.int32)
+
+
 def pack_columns(parent, child1, child2, sub_start, sub_end, ntv=None):
     """Per-column 32-bit tables (two 16-bit fields each) read once per CTA by the engine kernels:
 
@@ -192,4 +244,6 @@ def from_helpers(sh: dict) -> TreeTables:
         tt.packed = torch.from_numpy(pack_columns(*arrs)).to(dev).contiguous()
         bd, vpt = engine_width(int(sh["S"]))
         tt.packed_pad = torch.from_numpy(pack_columns(*arrs, ntv=bd * vpt)).to(dev).contiguous()
+        tt.tour = (torch.from_numpy(pack_forward(*arrs)).to(dev).contiguous()
+                   if tour_layout(int(sh["S"])) is not None else None)
     return tt

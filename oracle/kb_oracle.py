@@ -695,6 +695,17 @@ def backward(static: dict, theta, col_weights, saved: dict):
     """(forward intermediates) -> (grad_theta, grad_col): ``kbench/runtime.py:77-115`` ->
     ``kbench/api/_implicit_grad.py:98-370`` (reverse wave loop) and ``:373-475`` (E adjoint and
     theta VJP). Uniform column weights (``use_col_weights=False``)."""
+    acc = backward_accumulators(static, saved)
+    n_fam = int(np.asarray(static["wave_layout"]["root_row_ids"]).shape[0])
+    return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, Tree(static["state_helpers"]),
+                                   acc["E"], acc["Ebar"], acc["E_s1"], acc["E_s2"], acc["pD"], acc["pS"],
+                                   acc["mt"], acc["col"], n_fam=n_fam)
+
+
+def backward_accumulators(static: dict, saved: dict) -> dict:
+    """The reverse wave loop of ``kbench/api/_implicit_grad.py:98-370`` alone: the fp32 column
+    accumulators ``pD, pS, mt, E, Ebar, E_s1, E_s2, col`` (``:144-158``) that the E adjoint and
+    theta VJP consume."""
     sh = static["state_helpers"]
     wl = static["wave_layout"]
     so = static["solver_options"]
@@ -742,9 +753,8 @@ def backward(static: dict, theta, col_weights, saved: dict):
                                              grad_mt=g_mt, mt=mc, row_max_all=row_max)
             pibar_vjp_tree(Pi, col_logp, ud, A, side, meta, tree, acc, active=act,
                            row_max_all=row_max, grad_col=g_col)
-    return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree, g_E, g_Ebar, g_Es1,
-                                   g_Es2, g_pD, g_pS, g_mt, g_col,
-                                   n_fam=int(roots.shape[0]))
+    return {"pD": g_pD, "pS": g_pS, "mt": g_mt, "E": g_E, "Ebar": g_Ebar, "E_s1": g_Es1, "E_s2": g_Es2,
+            "col": g_col}
 
 
 def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree: Tree, g_E, g_Ebar, g_Es1,

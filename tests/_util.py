@@ -49,3 +49,24 @@ def assert_close(name, got, ref, rtol=RTOL, atol=ATOL):
 
 def assert_loss(got, ref, rtol=LOSS_RTOL):
     assert abs(float(got) - float(ref)) <= rtol * abs(float(ref)), f"loss {got} vs {ref}"
+
+
+def assert_close_rows(name, got, ref, rtol=RTOL, atol=ATOL):
+    """Tangent rows: |got - ref| <= atol + rtol * max|ref[row, :]| per element.
+
+    A tangent element is a softmax-weighted sum of signed tangents, and the Pibar tangent is a
+    difference (dRS - dAS) / denom; elements near zero are the result of cancellation, whose
+    rounding noise scales with the row's magnitude, not with the element.  Tolerating rtol of the
+    row's largest entry is still ten times stricter than the benchmark's own acceptance check for
+    tangents (central finite differences at rel 1e-3)."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64).reshape(got.shape)
+    assert not np.isnan(got).any(), f"{name}: NaN in result"
+    scale = np.abs(ref).max(axis=-1, keepdims=True)
+    tol = atol + rtol * scale
+    d = np.abs(got - ref)
+    bad = d > tol
+    if bad.any():
+        i = np.unravel_index(int(np.argmax(d / tol)), d.shape)
+        raise AssertionError(f"{name}: {int(bad.sum())} elements out of tolerance; worst |d|={d[i]:.3e} "
+                             f"ref={ref[i]:.6e} row scale={float(scale[i[:-1]][0]):.3e}")

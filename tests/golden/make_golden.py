@@ -17,7 +17,14 @@ What it does, per case:
      backward fed the forward's own intermediates, as ``bench/backward.py`` does);
   4. saves the static layout, the inputs and every checked output.
 
-Usage:  python tests/golden/make_golden.py --reference <path-to-reference-checkout>
+Tangent fixtures (``--tangent``): for each forward fixture already in this folder, the
+reference's forward-mode tangent ``newton/forward_tangent.py`` ``jvp_root_scores`` (its own
+``kbench/core/kernels/{e_step_tangent,dts_tangent,wave_tangent}.py`` kernels, fused fixed-count
+self-loop with ``self_iters = pi_iters``), evaluated at the fixture's saved forward intermediates
+along two seeded directions ``v ~ N(0,1)`` of theta's shape (seed 5000 + k); saved as
+``tangent/<case>.npz``.
+
+Usage:  python tests/golden/make_golden.py --reference <path-to-reference-checkout> [--tangent]
 """
 
 from __future__ import annotations
@@ -108,16 +115,55 @@ def run_case(runtime, name, cfg, seed, overrides):
           f"loss={float(loss):.6f} fwd {t1 - t0:.1f}s bwd {t2 - t1:.1f}s")
 
 
+TANGENT_DIRECTIONS = 2
+
+
+def tangent_direction(S: int, k: int) -> np.ndarray:
+    """Seeded tangent direction ``v ~ N(0,1)`` of theta's shape [S,3] (seed 5000 + k)."""
+    rng = np.random.Generator(np.random.PCG64(5000 + k))
+    return rng.standard_normal((S, 3)).astype(np.float32)
+
+
+def run_tangent_case(runtime, name):
+    from kbench_b200.problem_io import unflatten_case
+    from newton.forward_tangent import jvp_root_scores
+    cap, out = unflatten_case(np.load(HERE / f"{name}.npz"))
+    cap = gen.to_torch(cap)
+    static = runtime.make_static(cap, "cpu")
+    theta = cap["inputs"]["theta"]
+    S = int(theta.shape[0])
+    sv = {k: torch.from_numpy(np.asarray(v)) for k, v in out.items() if k not in ("loss", "grad_theta", "grad_col")}
+    iters = int(cap["meta"]["solver_options"]["pi_iters"])
+    arrays = {}
+    t0 = time.time()
+    for k in range(TANGENT_DIRECTIONS):
+        v = torch.from_numpy(tangent_direction(S, k))
+        roots, full = jvp_root_scores(static, theta, v, sv, self_iters=iters, return_full=True)
+        arrays[f"v{k}"] = v.numpy()
+        arrays[f"roots{k}"] = roots.numpy()
+        arrays[f"dPi{k}"] = full["dPi"].numpy()
+        arrays[f"dPibar{k}"] = full["dPibar"].numpy()
+        for key in ("dE", "dE_s1", "dE_s2", "dEbar", "dlog_pS", "dlog_pD", "dlog_pL", "dmax_coupling"):
+            arrays[f"{key}{k}"] = full[key].reshape(-1).numpy()
+    (HERE / "tangent").mkdir(exist_ok=True)
+    np.savez_compressed(HERE / "tangent" / f"{name}.npz", self_iters=np.asarray(iters), **arrays)
+    print(f"[tangent {name}] S={S} directions={TANGENT_DIRECTIONS} {time.time() - t0:.1f}s")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--cases", default=",".join(CASES))
+    ap.add_argument("--tangent", action="store_true", help="tangent fixtures from the forward fixtures")
     args = ap.parse_args()
     torch.set_num_threads(1)
     runtime = install_pristine(args.reference.resolve())
     for name in args.cases.split(","):
-        cfg, seed, ov = CASES[name]
-        run_case(runtime, name, cfg, seed, ov)
+        if args.tangent:
+            run_tangent_case(runtime, name)
+        else:
+            cfg, seed, ov = CASES[name]
+            run_case(runtime, name, cfg, seed, ov)
 
 
 if __name__ == "__main__":

@@ -40,3 +40,21 @@ def test_invalid_sizes_are_rejected_without_a_device():
     assert lib.kb_e_step_forward(*([None] * 15), 0, 0, 1, 0, None) == _lib.KB_ERR_ARG
     with pytest.raises(ValueError):
         _lib.call("kb_active_mask", None, 0, -1, 4, 0.0, 0, None, None)
+
+
+def test_tour_layout_matches_host_tables():
+    """The forward tour kernel's layout in the library equals the one the host tables are built
+    for (kbench_b200.tree.tour_layout), for every S up to the library maximum."""
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("libkb_solver.so not built")
+    from kbench_b200 import tree
+    lib = _lib.lib()
+    ntv, nt, vf = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    for S in list(range(1, 300)) + [511, 1023, 2047, 4095, 4096, 8191]:
+        st = lib.kb_tour_layout(S, ctypes.byref(ntv), ctypes.byref(nt), ctypes.byref(vf))
+        want = tree.tour_layout(S)
+        if want is None:
+            assert st == _lib.KB_ERR_SIZE and ntv.value == 0
+        else:
+            assert st == _lib.KB_OK and (ntv.value, nt.value, vf.value) == want
+            assert nt.value % 32 == 0 and vf.value in (2, 4, 8) and ntv.value > S
