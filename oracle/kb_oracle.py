@@ -691,21 +691,26 @@ def bicgstab(Av, b, *, max_iter=500, tol=1e-7, breakdown_tol=1e-30):
                        f"(relative residual {rel:.3e})")
 
 
-def backward(static: dict, theta, col_weights, saved: dict):
+def backward(static: dict, theta, col_weights, saved: dict, acc_dtype=F32):
     """(forward intermediates) -> (grad_theta, grad_col): ``kbench/runtime.py:77-115`` ->
     ``kbench/api/_implicit_grad.py:98-370`` (reverse wave loop) and ``:373-475`` (E adjoint and
     theta VJP). Uniform column weights (``use_col_weights=False``)."""
-    acc = backward_accumulators(static, saved)
+    acc = backward_accumulators(static, saved, acc_dtype)
     n_fam = int(np.asarray(static["wave_layout"]["root_row_ids"]).shape[0])
     return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, Tree(static["state_helpers"]),
                                    acc["E"], acc["Ebar"], acc["E_s1"], acc["E_s2"], acc["pD"], acc["pS"],
                                    acc["mt"], acc["col"], n_fam=n_fam)
 
 
-def backward_accumulators(static: dict, saved: dict) -> dict:
+def backward_accumulators(static: dict, saved: dict, acc_dtype=F32) -> dict:
     """The reverse wave loop of ``kbench/api/_implicit_grad.py:98-370`` alone: the fp32 column
     accumulators ``pD, pS, mt, E, Ebar, E_s1, E_s2, col`` (``:144-158``) that the E adjoint and
-    theta VJP consume."""
+    theta VJP consume.
+
+    ``acc_dtype=np.float64`` keeps every per-wave / per-split fp32 partial as the reference
+    computes it but adds them into float64 running sums: the accumulation-exact evaluation of the
+    same algorithm (the reference's fp32 running sums lose low-order bits of small contributions
+    once the sums have grown)."""
     sh = static["state_helpers"]
     wl = static["wave_layout"]
     so = static["solver_options"]
@@ -722,10 +727,10 @@ def backward_accumulators(static: dict, saved: dict) -> dict:
     consts = {"dl": (F32(1.0) + pD + E).astype(F32), "ebar": Ebar, "e": E,
               "sl1": (pS + E_s2).astype(F32), "sl2": (pS + E_s1).astype(F32), "mc": mc}
     acc = np.zeros((C, S), dtype=F32)
-    g_pD = np.zeros(S, F32); g_pS = np.zeros(S, F32); g_mt = np.zeros(S, F32)
-    g_col = np.zeros(S, F32)
-    g_E = np.zeros(S, F32); g_Ebar = np.zeros(S, F32); g_Es1 = np.zeros(S, F32)
-    g_Es2 = np.zeros(S, F32)
+    g_pD = np.zeros(S, acc_dtype); g_pS = np.zeros(S, acc_dtype); g_mt = np.zeros(S, acc_dtype)
+    g_col = np.zeros(S, acc_dtype)
+    g_E = np.zeros(S, acc_dtype); g_Ebar = np.zeros(S, acc_dtype); g_Es1 = np.zeros(S, acc_dtype)
+    g_Es2 = np.zeros(S, acc_dtype)
     roots = np.asarray(wl["root_row_ids"], dtype=np.int64)
     rp = Pi[roots]
     acc[roots] = -_safe_exp2_ratio(rp, lse_rows(rp)[:, None])
@@ -753,8 +758,9 @@ def backward_accumulators(static: dict, saved: dict) -> dict:
                                              grad_mt=g_mt, mt=mc, row_max_all=row_max)
             pibar_vjp_tree(Pi, col_logp, ud, A, side, meta, tree, acc, active=act,
                            row_max_all=row_max, grad_col=g_col)
-    return {"pD": g_pD, "pS": g_pS, "mt": g_mt, "E": g_E, "Ebar": g_Ebar, "E_s1": g_Es1, "E_s2": g_Es2,
-            "col": g_col}
+    out = {"pD": g_pD, "pS": g_pS, "mt": g_mt, "E": g_E, "Ebar": g_Ebar, "E_s1": g_Es1, "E_s2": g_Es2,
+           "col": g_col}
+    return {k: v.astype(F32) for k, v in out.items()}
 
 
 def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree: Tree, g_E, g_Ebar, g_Es1,
