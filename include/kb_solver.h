@@ -193,7 +193,7 @@ int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const flo
  * weights only (use_col_weights must be 0).  tour_tables: [3,NTV] uint32 tables of
  * kbench_b200/tree.py pack_forward() (children columns, byte offsets of the children's and the
  * column's own Euler-tour slots); when given and kb_tour_layout(S) accepts S, the tour kernel
- * runs (dts_save must then be non-NULL).  Otherwise packed: [4,NTV] tables of pack_columns(...,
+ * runs (dts_save and tour_consts, from kb_lin_consts_tour, must then be non-NULL).  Otherwise packed: [4,NTV] tables of pack_columns(...,
  * ntv) with NTV from the engine width (children, Euler-tour enter/exit, preorder start/end,
  * parent | first-child flag; two 16-bit fields each). */
 int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
@@ -206,7 +206,12 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
                      int use_col_weights, const int* node_parent, const int* node_child1, const int* node_child2,
                      const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                      const long long* item_idx, const int* leaf_state, const unsigned* packed,
-                     const unsigned* tour_tables, int pi_iters, int S, void* stream);
+                     const unsigned* tour_tables, const float* tour_consts, int pi_iters, int S, void* stream);
+
+/* The tour kernel's per-column constants, interleaved and zero-padded to NTV = kb_tour_layout(S):
+ * out4 [G, NTV, 4] = (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2) from the [G,S] constant rows. */
+int kb_lin_consts_tour(const float* dl, const float* ebar, const float* mc, const float* e, const float* sl1,
+                       const float* sl2, int G, int S, float* out4, void* stream);
 
 /* Layout of the forward tour kernel for S columns (host only): padded width NTV (smallest power
  * of two > S, at least 64), threads per row and columns per thread.  Returns 3 (KB_ERR_SIZE) with

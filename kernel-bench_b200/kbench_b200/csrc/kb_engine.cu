@@ -603,11 +603,13 @@ __device__ __forceinline__ void tour_scan_sw(float* T, float* red, float& mx, fl
 
 struct Fwd4Args {
   FwdArgs f;
-  const unsigned* tb;  // [3, NTV] tour tables
+  const unsigned* tb;   // [3, NTV] tour tables
+  const float4* k4;     // [G, NTV] (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2), zero on padded columns
+  long long k4_rows;    // row stride of k4 in float4 (0: one shared item row)
 };
 
 template <int VF>
-__global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args args) {
+__global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args args) {
   extern __shared__ __align__(16) float sm[];
   const FwdArgs& a = args.f;
   const LevelConsts& c = a.c;
@@ -733,8 +735,10 @@ __global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args arg
   const float Rd = safe_max(block_max(m0, red));  // scale of the initial row; syncs (staging done)
 
   // ---- linear-space iterations (see level_forward_kernel) ----
+  // per-column constants stay in L1 (shared by every row of the SM): (kA, kB) and (kC1, kC2) pairs
+  const float2* __restrict__ kab = reinterpret_cast<const float2*>(args.k4 + (size_t)(item * args.k4_rows));
   unsigned ce[VF], tr[VF];
-  float z[VF], td[VF], kA[VF], kB[VF], kC1[VF], kC2[VF];
+  float z[VF], td[VF];
   float zmax_l = 0.f, zsum_l = 0.f;
 #pragma unroll
   for (int k = 0; k < VF; ++k) {
@@ -742,10 +746,6 @@ __global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args arg
     const bool real = s < S;
     ce[k] = __ldg(tb + NTV + s);
     tr[k] = __ldg(tb + 2 * NTV + s);
-    kA[k] = real ? __ldg(c.linA + cb + s) : 0.f;
-    kB[k] = real ? __ldg(c.linB + cb + s) : 0.f;
-    kC1[k] = real ? __ldg(c.linC1 + cb + s) : 0.f;
-    kC2[k] = real ? __ldg(c.linC2 + cb + s) : 0.f;
     z[k] = real ? ex2(x[k] - Rd) : 0.f;
     td[k] = is_leaf ? (s == leaf ? ex2(leafv - Rd) : 0.f) : z[k];
     sts_at(T0, tr[k] & 0xFFFFu) = z[k];
@@ -764,11 +764,11 @@ __global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args arg
       fallback = true;
       break;
     }
-    float g1[VF], g2[VF];
+    float part[VF];  // speciation terms z[c1] 2^sl1 + z[c2] 2^sl2, gathered before the scan
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
-      g1[k] = lds_at(Tc, ce[k] & 0xFFFFu);
-      g2[k] = lds_at(Tc, ce[k] >> 16);
+      const float2 kc = __ldg(kab + 2 * (tid + k * NT) + 1);
+      part[k] = fmaf(lds_at(Tc, ce[k] & 0xFFFFu), kc.x, lds_at(Tc, ce[k] >> 16) * kc.y);
     }
     float zmax = zmax_l, zsum = zsum_l;
     tour_scan_sw<VF>(reinterpret_cast<float*>(Tc), red, zmax, zsum);
@@ -781,12 +781,10 @@ __global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args arg
     const bool resid = (it == last) && (a.residual != nullptr);
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
+      const float2 kk = __ldg(kab + 2 * (tid + k * NT));
       const float path = lds_at(Tc, tr[k] & 0xFFFFu) + z[k];
       const float D = fmaxf(zsum - path, 0.f);
-      float lin = z[k] * kA[k];
-      lin = fmaf(D, kB[k], lin);
-      lin = fmaf(g1[k], kC1[k], lin);
-      lin = fmaf(g2[k], kC2[k], lin);
+      const float lin = fmaf(D, kk.y, fmaf(z[k], kk.x, part[k]));
       const float zn = fmaf(lin, inv, td[k] * fd);
       mincode = min(mincode, (unsigned)__float_as_int(zn) - 1u);
       if (resid && zn > 0.f && z[k] > 0.f) dres = fmaxf(dres, fabsf(lg2(zn) - lg2(z[k] * inv)));
@@ -1531,6 +1529,25 @@ __global__ void lin_consts_kernel(const float* dl, const float* ebar, const floa
   }
 }
 
+// The forward tour kernel's per-column constants, interleaved and padded: out[g * ntv + s] =
+// (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2) for s < S, zero for S <= s < ntv.
+__global__ void lin_consts4_kernel(const float* dl, const float* ebar, const float* mc, const float* e,
+                                   const float* sl1, const float* sl2, int G, int S, int ntv, float4* out) {
+  const int n = G * ntv;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int g = i / ntv, s = i - g * ntv;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s < S) {
+      const int j = g * S + s;
+      v.x = ex2(dl[j]) + ex2(ebar[j]);
+      v.y = ex2(mc[j] + e[j]);
+      v.z = ex2(sl1[j]);
+      v.w = ex2(sl2[j]);
+    }
+    out[i] = v;
+  }
+}
+
 // Threads per CTA and columns per thread of the padded-row kernels; bd * vpt >= S + 1 leaves a
 // zero padding column (mirrors kbench_b200/tree.py engine_width).
 int engine_width(int S, int& bd) {
@@ -1605,6 +1622,19 @@ extern "C" int kb_lin_consts(const float* dl, const float* ebar, const float* mc
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
 
+extern "C" int kb_lin_consts_tour(const float* dl, const float* ebar, const float* mc, const float* e,
+                                  const float* sl1, const float* sl2, int G, int S, float* out4, void* stream) {
+  int nt, vf;
+  const int ntv = tour_layout(S, nt, vf);
+  if (G <= 0 || S <= 0 || out4 == nullptr) return KB_ERR_ARG;
+  if (ntv == 0) return KB_ERR_SIZE;
+  const int n = G * ntv;
+  const int bd = 256;
+  lin_consts4_kernel<<<(n + bd - 1) / bd, bd, 0, (cudaStream_t)stream>>>(dl, ebar, mc, e, sl1, sl2, G, S, ntv,
+                                                                         reinterpret_cast<float4*>(out4));
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
 extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                                 const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src,
                                 float* pi, float* pibar, float* pibar_row_max, float* dts_save, float* residual,
@@ -1616,7 +1646,8 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
                                 const int* node_parent, const int* node_child1, const int* node_child2,
                                 const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                                 const long long* item_idx, const int* leaf_state, const unsigned* packed,
-                                const unsigned* tour_tables, int pi_iters, int S, void* stream) {
+                                const unsigned* tour_tables, const float* tour_consts, int pi_iters, int S,
+                                void* stream) {
   if (S <= 0 || n_rows < 0 || K < 0 || pi_iters < 2 || use_col_weights != 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
@@ -1633,10 +1664,13 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   int nt4, vf4;
   const int ntv4 = tour_layout(S, nt4, vf4);
   if (tour_tables != nullptr && ntv4 > 0) {
-    if (dts_save == nullptr) return KB_ERR_ARG;  // the log-space fallback re-reads the split reduction
+    // the log-space fallback re-reads the split reduction; the constants come interleaved
+    if (dts_save == nullptr || tour_consts == nullptr) return KB_ERR_ARG;
     Fwd4Args a4;
     a4.f = a;
     a4.tb = tour_tables;
+    a4.k4 = reinterpret_cast<const float4*>(tour_consts);
+    a4.k4_rows = const_row_stride == 0 ? 0 : ntv4;
     const size_t smem4 = (size_t)(4 * ntv4 + 96) * sizeof(float);
 #define KB_LF4_CASE(V)                                                                                        \
   case V:                                                                                                     \

@@ -178,6 +178,7 @@ class Prep:
     Ebar: torch.Tensor
     k: dict
     lin: torch.Tensor
+    k4: torch.Tensor | None   # tour kernel constants [G, NTV, 4] (None where the tour kernel does not apply)
 
 
 @torch.no_grad()
@@ -194,7 +195,14 @@ def prepare(static, theta, col_weights) -> Prep:
     _lib.call("kb_lin_consts", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(), k["e"].data_ptr(),
               k["sl1"].data_ptr(), k["sl2"].data_ptr(), G * S, lin[0].data_ptr(), lin[1].data_ptr(),
               lin[2].data_ptr(), lin[3].data_ptr(), _lib.stream_handle(dev))
-    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin)
+    k4 = None
+    lay = tree.tour_layout(S)
+    if lay is not None:
+        k4 = torch.empty((G, lay[0], 4), device=dev, dtype=torch.float32)
+        _lib.call("kb_lin_consts_tour", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(),
+                  k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), G, S, k4.data_ptr(),
+                  _lib.stream_handle(dev))
+    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin, k4)
 
 
 def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | None = None):
@@ -237,6 +245,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
     static._fallback_rows = fallback
     rows_ptr = plan.rows.data_ptr()
     sp_ptr = plan.split_ptr.data_ptr()
+    use_tour = getattr(static, "_tour_forward", True) and tt.tour is not None and prep.k4 is not None
     for L in range(plan.n_levels):
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
@@ -250,7 +259,8 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                   pSp.data_ptr(), prs, crs, f32(clp).data_ptr(), int(ucw), tt.parent.data_ptr(),
                   tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
                   tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
-                  _lib.ptr(tt.tour if getattr(static, "_tour_forward", True) else None), int(so.pi_iters), S, st)
+                  _lib.ptr(tt.tour if use_tour else None), _lib.ptr(prep.k4 if use_tour else None),
+                  int(so.pi_iters), S, st)
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
     return out, {"dts_wave": dts}
