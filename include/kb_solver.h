@@ -208,6 +208,27 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
                      const long long* item_idx, const int* leaf_state, const unsigned* packed,
                      const unsigned* tour_tables, const float* tour_consts, int pi_iters, int S, void* stream);
 
+/* The whole forward wave sweep in ONE persistent launch with a dataflow schedule (replaces the
+ * per-level kb_level_forward launches, same per-row arithmetic as its tour kernel): a row starts
+ * as soon as all of its child rows are final instead of after the whole previous level.
+ * Rows' splits: row_split_ptr [C+1] into sl / sr / lsp (row-id order).  dep0 [C]: number of
+ * distinct child rows; ready0 [n_ready0]: the rows with dep0 = 0; par_ptr [C+1] / par_idx: the
+ * distinct parent rows of each row.  Scratch: queue [C], remaining [C] (int), counters [3]
+ * (head, tail, error flag; error != 0 after the launch means a wait gave up after max_polls
+ * polls: results are then invalid).  Pi / Pibar child rows are read from pi / pibar (in place).
+ * Other arguments as kb_level_forward's tour path. */
+int kb_flow_forward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                    const float* lsp, const int* dep0, const int* ready0, int n_ready0, const long long* par_ptr,
+                    const int* par_idx, int* queue, int* remaining, unsigned* counters, long long max_polls,
+                    float* pi, float* pibar, float* pibar_row_max, float* dts_save, float* residual,
+                    int* fallback_count, const float* mc, const float* dl, const float* ebar, const float* e,
+                    const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
+                    const float* log_pS, long long param_row_stride, long long const_row_stride,
+                    const int* node_parent, const int* node_child1, const int* node_child2,
+                    const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
+                    const long long* item_idx, const int* leaf_state, const unsigned* tour_tables,
+                    const float* tour_consts, int pi_iters, int S, void* stream);
+
 /* The tour kernel's per-column constants, interleaved and zero-padded to NTV = kb_tour_layout(S):
  * out4 [G, NTV, 4] = (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2) from the [G,S] constant rows. */
 int kb_lin_consts_tour(const float* dl, const float* ebar, const float* mc, const float* e, const float* sl1,
@@ -304,7 +325,9 @@ int kb_wave_tangent(const float* Pi_in, const float* dPi_in, float* dPi_out, flo
  * tangent at the frozen primal row, and writes dPi / dPibar [D, C, S] (direction stride
  * dir_stride).  dts_saved: the forward's split reductions [C,S].  Tangent constants [D, G, S]
  * (direction stride tangent_dir_stride).  tour_tables: kbench_b200/tree.py pack_forward(); S must
- * be accepted by kb_tour_layout. */
+ * be accepted by kb_tour_layout.  pair_tables (may be NULL): pack_tour_pair(), the enter / exit
+ * offsets of the two-direction layout; when given, directions run in pairs per CTA (sharing the
+ * primal weights and the addressing) and an odd last direction alone. */
 int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                      const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
                      const float* dts_saved, float* dPi, float* dPibar, long long dir_stride, int D, const float* mc,
@@ -313,7 +336,8 @@ int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, co
                      long long const_row_stride, const float* dMC, const float* dDL, const float* dEbar,
                      const float* dE, const float* dSL1, const float* dSL2, const float* dleaf, const float* dpD,
                      const float* dpS, long long tangent_dir_stride, const long long* item_idx,
-                     const int* leaf_state, const unsigned* tour_tables, int n_iters, int S, void* stream);
+                     const int* leaf_state, const unsigned* tour_tables, const unsigned* pair_tables,
+                     int n_iters, int S, void* stream);
 
 #ifdef __cplusplus
 }

@@ -608,9 +608,21 @@ struct Fwd4Args {
   long long k4_rows;    // row stride of k4 in float4 (0: one shared item row)
 };
 
-template <int VF>
-__global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args args) {
-  extern __shared__ __align__(16) float sm[];
+// Loads of rows that other CTAs of the SAME launch produce (the dataflow schedule) bypass L1:
+// L1 is not coherent across SMs, and a row's first and last cache lines are shared with its
+// neighbours.  Level launches keep the cached / asynchronous paths.
+template <bool DF>
+__device__ __forceinline__ float ld_row(const float* p) {
+  if constexpr (DF) return __ldcg(p);
+  else return __ldg(p);
+}
+
+// One row of the forward tour kernel (the body of level_forward_tour_kernel and of the dataflow
+// kernel): split reduction or leaf seed, pi_iters linear-space iterations, final Pi / Pibar.
+// Splits [i0, i1) of the split arrays; sm: the CTA's dynamic shared memory.
+template <int VF, bool DF>
+__device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long row, long long i0, long long i1,
+                                                 float* sm) {
   const FwdArgs& a = args.f;
   const LevelConsts& c = a.c;
   const unsigned* __restrict__ tb = args.tb;
@@ -622,12 +634,9 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
   char* T0 = reinterpret_cast<char*>(sm);
   char* T1 = reinterpret_cast<char*>(sm + TB);
   const int tid = threadIdx.x;
-  const int b = blockIdx.x;
-  const long long row = a.sp.rows[b];
   const long long item = c.item_idx[row];
   const size_t cb = (size_t)(item * c.crs);
   const size_t pb = (size_t)(item * c.prs);
-  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
   const int leaf_raw = c.leaf_state[row];
   const bool is_leaf = (i0 == i1) && leaf_raw >= 0 && leaf_raw < S;
   const int leaf = is_leaf ? leaf_raw : -1;
@@ -662,7 +671,7 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
       m[k] = neg_inf();
       acc[k] = 0.f;
     }
-    {  // prefetch split i0
+    if (!DF) {  // prefetch split i0
       const float* pil = a.Pi_src + (size_t)a.sp.sl[i0] * S;
       const float* pir = a.Pi_src + (size_t)a.sp.sr[i0] * S;
 #pragma unroll
@@ -676,12 +685,26 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
       cp_async_commit();
     }
     for (long long i = i0; i < i1; ++i) {
-      const int par = (int)((i - i0) & 1);
-      const float* Pl = stg + par * 2 * NTV;
-      const float* Pr = Pl + NTV;
-      cp_async_wait_all();
+      const int par = DF ? 0 : (int)((i - i0) & 1);
+      float* Pl = stg + par * 2 * NTV;
+      float* Pr = Pl + NTV;
+      if (DF) {
+        __syncthreads();  // the previous split's readers are done
+        const float* pil = a.Pi_src + (size_t)a.sp.sl[i] * S;
+        const float* pir = a.Pi_src + (size_t)a.sp.sr[i] * S;
+#pragma unroll
+        for (int k = 0; k < VF; ++k) {
+          const int s = tid + k * NT;
+          if (s < S) {
+            Pl[s] = __ldcg(pil + s);
+            Pr[s] = __ldcg(pir + s);
+          }
+        }
+      } else {
+        cp_async_wait_all();
+      }
       __syncthreads();
-      if (i + 1 < i1) {
+      if (!DF && i + 1 < i1) {
         float* nl = stg + (par ^ 1) * 2 * NTV;
         const float* pil = a.Pi_src + (size_t)a.sp.sl[i + 1] * S;
         const float* pir = a.Pi_src + (size_t)a.sp.sr[i + 1] * S;
@@ -705,7 +728,7 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
         if (s < S) {
           const float ld = __ldg(c.log_pD + pb + s);
           const float ls = __ldg(c.log_pS + pb + s);
-          const float vbr = __ldg(pbr + s), vbl = __ldg(pbl + s);
+          const float vbr = ld_row<DF>(pbr + s), vbl = ld_row<DF>(pbl + s);
           const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
           const float pl = Pl[s], pr = Pr[s];
           const float lss = lsp + ls;
@@ -891,6 +914,107 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
   if (tid == 0) a.row_max[row] = row_max;
 }
 
+template <int VF>
+__global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args args) {
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.x;
+  forward_tour_row<VF, false>(args, args.f.sp.rows[b], args.f.sp.split_ptr[b], args.f.sp.split_ptr[b + 1], sm);
+}
+
+// ------------------------------------------------------------------------------------------
+// dataflow schedule: one persistent launch, rows start when their children are done
+// ------------------------------------------------------------------------------------------
+//
+// Level launches make every row of a level wait for the slowest row of the previous level; near
+// the root most levels hold fewer rows than there are SMs, so most of the GPU idles.  Here each
+// row keeps a count of unfinished child rows; a CTA that finishes a row decrements the counts of
+// the row's parents and appends those that reach zero to a device queue; persistent CTAs take
+// queue slots in order.  Every wait on a queue slot is bounded: past the limit the CTA records an
+// error and leaves (the host then reports the failure; it never hangs).
+
+struct Flow {
+  int* queue;              // [C] rows in start order; -1 = slot not yet filled
+  int* remaining;          // [C] unfinished children per row
+  unsigned* head;          // next slot to take
+  unsigned* tail;          // next slot to fill
+  int* error;              // set to 1 when a wait gave up
+  const long long* par_ptr;  // [C+1] CSR: distinct parent rows of each row
+  const int* par_idx;
+  const long long* row_split_ptr;  // [C+1] splits of each row (row-id order)
+  int C;
+  long long max_polls;
+};
+
+// Claims the next queue slot and waits (bounded) until it holds a row.  Returns the row, -1 when
+// every row has been taken, -2 on a timeout (error recorded).  Called by all threads.
+__device__ __forceinline__ int flow_next_row(const Flow& f, int* shared_slot) {
+  if (threadIdx.x == 0) {
+    const unsigned idx = atomicAdd(f.head, 1u);
+    int row = -1;
+    if (idx < (unsigned)f.C) {
+      const volatile int* q = f.queue + idx;
+      long long polls = 0;
+      row = *q;
+      while (row < 0) {
+        if (++polls > f.max_polls || *(volatile int*)f.error) {
+          atomicExch(f.error, 1);
+          row = -2;
+          break;
+        }
+        __nanosleep(128);
+        row = *q;
+      }
+      __threadfence();  // the row's children, written before it was queued, are visible
+    }
+    *shared_slot = row;
+  }
+  __syncthreads();
+  const int row = *shared_slot;
+  __syncthreads();
+  return row;
+}
+
+// After a row's outputs are written by the whole CTA: release its parents.
+__device__ __forceinline__ void flow_finish_row(const Flow& f, int row) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this row's outputs before any parent is queued
+    for (long long j = f.par_ptr[row]; j < f.par_ptr[row + 1]; ++j) {
+      const int p = f.par_idx[j];
+      if (atomicSub(f.remaining + p, 1) == 1) {
+        const unsigned slot = atomicAdd(f.tail, 1u);
+        atomicExch(f.queue + slot, p);
+      }
+    }
+  }
+}
+
+template <int VF>
+__global__ void __launch_bounds__(512, 2) flow_forward_kernel(Fwd4Args args, Flow f) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int slot;
+  for (;;) {
+    const int row = flow_next_row(f, &slot);
+    if (row < 0) break;
+    forward_tour_row<VF, true>(args, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], sm);
+    flow_finish_row(f, row);
+  }
+}
+
+// Queue / counter initialisation of one dataflow run: remaining = dep0, queue = the rows ready
+// at the start (n0 of them, given in ready0) followed by -1, head = 0, tail = n0, error = 0.
+__global__ void flow_init_kernel(Flow f, const int* dep0, const int* ready0, int n0) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < f.C; i += gridDim.x * blockDim.x) {
+    f.remaining[i] = dep0[i];
+    f.queue[i] = i < n0 ? ready0[i] : -1;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *f.head = 0u;
+    *f.tail = (unsigned)n0;
+    *f.error = 0;
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // tangent (forward-mode JVP) of one dependency level, every (row, direction) pair
 // ------------------------------------------------------------------------------------------
@@ -934,6 +1058,7 @@ struct TanArgs {
   const long long* item_idx;
   const int* leaf_state;
   const unsigned* tb;   // [3, NTV] tour tables
+  const unsigned* tb2;  // [NTV] enter | exit byte offsets of the float2 (direction pair) tour layout
   int n_iters;
   int S;
 };
@@ -1129,6 +1254,325 @@ __global__ void __launch_bounds__(512, 1) level_tangent_kernel(TanArgs a) {
       outp[s] = dp[k];
       const float iv = PR[s];
       outb[s] = iv > 0.f ? D[k] * iv + a.dmc[tof + cb + s] : 0.f;
+    }
+  }
+}
+
+// Exclusive scan, in place, of a tour buffer of float2 entries (two tangent directions), in the
+// swizzled pair layout (thread t scans the 2*VF consecutive entries of its chunk as VF float4
+// groups XOR-permuted by t), fused with the block sums of sa and sb.  red >= 128 floats; the
+// caller syncs before; two barriers inside, the second on exit.
+template <int VF>
+__device__ __forceinline__ void tour_scan_pair(float2* T, float* red, float& sa, float& sb) {
+  constexpr int Q = VF;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int sw = Q == 1 ? 0 : ((t / (8 / Q)) & (Q - 1));
+  float4* base = reinterpret_cast<float4*>(T) + t * Q;
+  float ga[Q], gb[Q];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    ga[q] = v.x + v.z;
+    gb[q] = v.y + v.w;
+  }
+  float la = 0.f, lb = 0.f;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    la += ga[q];
+    lb += gb[q];
+  }
+  float ia = la, ib = lb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, ia, o);
+    const float yb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ya;
+      ib += yb;
+    }
+  }
+  sa = warp_sum(sa);
+  sb = warp_sum(sb);
+  if (lane == 31) { red[wid] = ia; red[32 + wid] = ib; }
+  if (lane == 0) { red[64 + wid] = sa; red[96 + wid] = sb; }
+  __syncthreads();
+  float ta = lane < nw ? red[lane] : 0.f;
+  float tb2 = lane < nw ? red[32 + lane] : 0.f;
+  const float bsa = lane < nw ? red[64 + lane] : 0.f;
+  const float bsb = lane < nw ? red[96 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, ta, o);
+    const float yb = __shfl_up_sync(0xffffffffu, tb2, o);
+    if (lane >= o) {
+      ta += ya;
+      tb2 += yb;
+    }
+  }
+  sa = warp_sum(bsa);
+  sb = warp_sum(bsb);
+  const float pa = __shfl_up_sync(0xffffffffu, ta, 1);
+  const float pb = __shfl_up_sync(0xffffffffu, tb2, 1);
+  float ra = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : pa, wid) + ia - la;
+  float rb = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : pb, wid) + ib - lb;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    base[q ^ sw] = make_float4(ra, rb, ra + v.x, rb + v.y);
+    ra += ga[q];
+    rb += gb[q];
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ float2& pair_at(float2* base, unsigned off) {
+  return *reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + off);
+}
+
+// Tangent of one level for a PAIR of directions per CTA (blockIdx.y = pair index): the primal
+// weights, the Euler-tour addressing and the split weights are shared by the two directions,
+// which travel together as float2 through the tour scan and the gathers.  Same arithmetic as
+// level_tangent_kernel.
+template <int VF>
+__global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const unsigned* __restrict__ tb = a.tb;
+  const unsigned* __restrict__ tp = a.tb2;
+  const int S = a.S;
+  const int NT = blockDim.x;
+  const int NTV = NT * VF;
+  float2* T0 = reinterpret_cast<float2*>(sm);
+  float2* T1 = T0 + 2 * NTV;
+  float2* DP0 = T1 + 2 * NTV;
+  float2* DP1 = DP0 + NTV;
+  float* PR = reinterpret_cast<float*>(DP1 + NTV);
+  float* red = PR + NTV;
+  const int tid = threadIdx.x;
+  const int b = blockIdx.x;
+  const int d0 = 2 * blockIdx.y;
+  const long long row = a.sp.rows[b];
+  const long long item = a.item_idx[row];
+  const size_t cb = (size_t)(item * a.crs);
+  const size_t pb = (size_t)(item * a.prs);
+  const size_t tofa = (size_t)d0 * a.tstride, tofb = tofa + (size_t)a.tstride;
+  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
+  const bool has_splits = i1 > i0;
+  const int leaf_raw = a.leaf_state[row];
+  const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
+
+  unsigned ccol[VF], tr[VF];
+  float pv[VF], r[VF];
+  float m = neg_inf();
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    ccol[k] = __ldg(tb + s);
+    tr[k] = __ldg(tp + s);
+    pv[k] = s < S ? a.Pi[(size_t)row * S + s] : neg_inf();
+    PR[s] = pv[k];
+    m = fmaxf(m, pv[k]);
+  }
+  const float row_max = block_max(m, red);
+  const float rms = safe_max(row_max);
+  float rsum = 0.f, zero = 0.f;
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    r[k] = ex2(pv[k] - rms);
+    pair_at(T0, tr[k] & 0xFFFFu) = make_float2(r[k], 0.f);
+    pair_at(T0, tr[k] >> 16) = make_float2(-r[k], 0.f);
+    rsum += r[k];
+  }
+  __syncthreads();
+  tour_scan_pair<VF>(T0, red, rsum, zero);
+  const float row_sum = rsum;
+  float cA[VF], c2[VF], c3[VF], c4[VF], ca_[VF], cb_[VF], cD[VF], invd[VF];
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    cA[k] = c2[k] = c3[k] = c4[k] = ca_[k] = cb_[k] = cD[k] = invd[k] = 0.f;
+    if (s < S) {
+      const float denom = row_sum - (pair_at(T0, tr[k] & 0xFFFFu).x + r[k]);
+      const bool pos = denom > 0.f;
+      const float sd = pos ? denom : 1.f;
+      invd[k] = pos ? 1.0f / sd : 0.f;
+      const float pibar = pos ? lg2(sd) + row_max + a.mc[cb + s] : neg_inf();
+      const float t0 = a.dl[cb + s] + pv[k];
+      const float t1 = pv[k] + a.ebar[cb + s];
+      const float t2 = pibar + a.e[cb + s];
+      const float t3 = a.sl1[cb + s] + PR[ccol[k] & 0xFFFFu];
+      const float t4 = a.sl2[cb + s] + PR[ccol[k] >> 16];
+      const bool hit = s == leaf;
+      const float t5 = hit ? a.leaf_logp[(size_t)item * S + s] : neg_inf();
+      const float dv = has_splits ? a.dts[(size_t)row * S + s] : neg_inf();
+      const float mm = fmaxf(fmaxf(fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)), fmaxf(t4, t5)), dv);
+      const float ms = safe_max(mm);
+      const float e0 = ex2(t0 - ms), e1 = ex2(t1 - ms), e2 = ex2(t2 - ms), e3 = ex2(t3 - ms), e4 = ex2(t4 - ms),
+                  e5 = ex2(t5 - ms), ed = ex2(dv - ms);
+      const float tot = ((e0 + e1) + (e2 + e3)) + ((e4 + e5) + ed);
+      if (!is_neg_inf(lg2(tot) + mm)) {
+        const float inv = tot > 0.f ? 1.0f / tot : 0.f;
+        cA[k] = (e0 + e1) * inv;
+        c2[k] = e2 * inv * invd[k];
+        c3[k] = e3 * inv;
+        c4[k] = e4 * inv;
+        cD[k] = ed * inv;
+        const size_t ia = tofa + cb + s, ib = tofb + cb + s;
+        const float dta5 = hit ? a.dleaf[tofa + (size_t)item * S + s] : 0.f;
+        const float dtb5 = hit ? a.dleaf[tofb + (size_t)item * S + s] : 0.f;
+        const float dmca = pos ? a.dmc[ia] : 0.f, dmcb = pos ? a.dmc[ib] : 0.f;
+        ca_[k] = inv * (e0 * a.ddl[ia] + e1 * a.debar[ia] + e2 * (dmca + a.de[ia]) + e3 * a.dsl1[ia] +
+                        e4 * a.dsl2[ia] + e5 * dta5);
+        cb_[k] = inv * (e0 * a.ddl[ib] + e1 * a.debar[ib] + e2 * (dmcb + a.de[ib]) + e3 * a.dsl1[ib] +
+                        e4 * a.dsl2[ib] + e5 * dtb5);
+      }
+    }
+  }
+  __syncthreads();  // PR (primal row) no longer gathered: it keeps 1/denom from here on
+  float* stash = reinterpret_cast<float*>(DP0);  // self-loop coefficients, parked during the splits
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    PR[s] = invd[k];
+    stash[s] = cA[k];
+    stash[NTV + s] = c2[k];
+    stash[2 * NTV + s] = c3[k];
+    stash[3 * NTV + s] = c4[k];
+  }
+
+  // ---- split tangent reduction, the weights shared by both directions ----
+  if (has_splits) {
+    float* Pl = sm;
+    float* Pr = sm + NTV;
+    float* Qla = sm + 2 * NTV;
+    float* Qra = sm + 3 * NTV;
+    float* Qlb = sm + 4 * NTV;
+    float* Qrb = sm + 5 * NTV;
+    const float* dPa = a.dPi + (size_t)d0 * a.dstride;
+    const float* dPb = dPa + a.dstride;
+    const float* dBa = a.dPibar + (size_t)d0 * a.dstride;
+    const float* dBb = dBa + a.dstride;
+    const float* dts_row = a.dts + (size_t)row * S;
+    for (long long i = i0; i < i1; ++i) {
+      const long long l = a.sp.sl[i], rr = a.sp.sr[i];
+      const float lsp = a.sp.lsp[i];
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        const bool real = s < S;
+        const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
+        Pl[s] = real ? a.Pi[ol] : neg_inf();
+        Pr[s] = real ? a.Pi[orr] : neg_inf();
+        Qla[s] = real ? dPa[ol] : 0.f;
+        Qra[s] = real ? dPa[orr] : 0.f;
+        Qlb[s] = real ? dPb[ol] : 0.f;
+        Qrb[s] = real ? dPb[orr] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        const float dts = s < S ? __ldg(dts_row + s) : neg_inf();
+        if (!is_neg_inf(dts)) {
+          const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
+          const float ld = __ldg(a.log_pD + pb + s), ls = __ldg(a.log_pS + pb + s);
+          const float pl = Pl[s], pr = Pr[s];
+          const float w0 = ex2(lsp + ld + pl + pr - dts);
+          const float w1 = ex2(lsp + pl + a.Pibar[(size_t)rr * S + s] - dts);
+          const float w2 = ex2(lsp + pr + a.Pibar[(size_t)l * S + s] - dts);
+          const float w3 = ex2(lsp + ls + Pl[ca] + Pr[cbb] - dts);
+          const float w4 = ex2(lsp + ls + Pr[ca] + Pl[cbb] - dts);
+          const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
+          const float xa = w0 * (a.dpD[tofa + pb + s] + Qla[s] + Qra[s]) + w1 * (Qla[s] + dBa[orr]) +
+                           w2 * (Qra[s] + dBa[ol]) + w3 * (a.dpS[tofa + pb + s] + Qla[ca] + Qra[cbb]) +
+                           w4 * (a.dpS[tofa + pb + s] + Qra[ca] + Qla[cbb]);
+          const float xb = w0 * (a.dpD[tofb + pb + s] + Qlb[s] + Qrb[s]) + w1 * (Qlb[s] + dBb[orr]) +
+                           w2 * (Qrb[s] + dBb[ol]) + w3 * (a.dpS[tofb + pb + s] + Qlb[ca] + Qrb[cbb]) +
+                           w4 * (a.dpS[tofb + pb + s] + Qrb[ca] + Qlb[cbb]);
+          ca_[k] = fmaf(cD[k], xa, ca_[k]);
+          cb_[k] = fmaf(cD[k], xb, cb_[k]);
+        }
+      }
+    }
+  }
+
+  // ---- fixed-count Jacobi steps from a zero tangent (the first one gives dPi = cst) ----
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {  // own columns only: no barrier needed before the reload
+    const int s = tid + k * NT;
+    cA[k] = stash[s];
+    c2[k] = stash[NTV + s];
+    c3[k] = stash[2 * NTV + s];
+    c4[k] = stash[3 * NTV + s];
+  }
+  float* outpa = a.dPi + (size_t)d0 * a.dstride + (size_t)row * S;
+  float* outpb = outpa + a.dstride;
+  float* outba = a.dPibar + (size_t)d0 * a.dstride + (size_t)row * S;
+  float* outbb = outba + a.dstride;
+  float dpa[VF], dpb[VF];
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    dpa[k] = ca_[k];
+    dpb[k] = cb_[k];
+  }
+  const int last = a.n_iters - 1;
+  if (last == 0) {  // one step: dPibar of the zero tangent
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const int s = tid + k * NT;
+      if (s < S) {
+        const float iv = PR[s];
+        outba[s] = iv > 0.f ? a.dmc[tofa + cb + s] : 0.f;
+        outbb[s] = iv > 0.f ? a.dmc[tofb + cb + s] : 0.f;
+      }
+    }
+  }
+  for (int it = 1; it <= last; ++it) {
+    float2* Tc = (it & 1) ? T0 : T1;
+    float2* Dc = (it & 1) ? DP0 : DP1;
+    __syncthreads();  // the previous step's (or the setup's) readers of Tc / Dc are done
+    float sa = 0.f, sbv = 0.f;
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const float va = r[k] * dpa[k], vb = r[k] * dpb[k];
+      pair_at(Tc, tr[k] & 0xFFFFu) = make_float2(va, vb);
+      pair_at(Tc, tr[k] >> 16) = make_float2(-va, -vb);
+      Dc[tid + k * NT] = make_float2(dpa[k], dpb[k]);
+      sa += va;
+      sbv += vb;
+    }
+    __syncthreads();
+    float pa[VF], pbv[VF];  // speciation terms, gathered before the scan
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const float2 g1 = Dc[ccol[k] & 0xFFFFu], g2 = Dc[ccol[k] >> 16];
+      pa[k] = fmaf(c3[k], g1.x, c4[k] * g2.x);
+      pbv[k] = fmaf(c3[k], g1.y, c4[k] * g2.y);
+    }
+    tour_scan_pair<VF>(Tc, red, sa, sbv);
+#pragma unroll
+    for (int k = 0; k < VF; ++k) {
+      const float2 p = pair_at(Tc, tr[k] & 0xFFFFu);
+      const float Da = sa - (p.x + r[k] * dpa[k]);
+      const float Db = sbv - (p.y + r[k] * dpb[k]);
+      dpa[k] = cA[k] * dpa[k] + c2[k] * Da + pa[k] + ca_[k];
+      dpb[k] = cA[k] * dpb[k] + c2[k] * Db + pbv[k] + cb_[k];
+      if (it == last) {
+        const int s = tid + k * NT;
+        if (s < S) {
+          const float iv = PR[s];
+          outba[s] = iv > 0.f ? Da * iv + a.dmc[tofa + cb + s] : 0.f;
+          outbb[s] = iv > 0.f ? Db * iv + a.dmc[tofb + cb + s] : 0.f;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VF; ++k) {
+    const int s = tid + k * NT;
+    if (s < S) {
+      outpa[s] = dpa[k];
+      outpb[s] = dpb[k];
     }
   }
 }
@@ -1776,7 +2220,8 @@ extern "C" int kb_level_tangent(const int* rows, const long long* split_ptr, int
                                 const float* dDL, const float* dEbar, const float* dE, const float* dSL1,
                                 const float* dSL2, const float* dleaf, const float* dpD, const float* dpS,
                                 long long tangent_dir_stride, const long long* item_idx, const int* leaf_state,
-                                const unsigned* tour_tables, int n_iters, int S, void* stream) {
+                                const unsigned* tour_tables, const unsigned* pair_tables, int n_iters, int S,
+                                void* stream) {
   if (S <= 0 || n_rows < 0 || D <= 0 || n_iters < 1 || tour_tables == nullptr || dts_saved == nullptr)
     return KB_ERR_ARG;
   int nt, vf;
@@ -1790,10 +2235,35 @@ extern "C" int kb_level_tangent(const int* rows, const long long* split_ptr, int
   a.log_pD = log_pD; a.log_pS = log_pS; a.crs = const_row_stride; a.prs = param_row_stride;
   a.dmc = dMC; a.ddl = dDL; a.debar = dEbar; a.de = dE; a.dsl1 = dSL1; a.dsl2 = dSL2; a.dleaf = dleaf;
   a.dpD = dpD; a.dpS = dpS; a.tstride = tangent_dir_stride; a.item_idx = item_idx; a.leaf_state = leaf_state;
-  a.tb = tour_tables; a.n_iters = n_iters; a.S = S;
-  const size_t smem = (size_t)(7 * ntv + 96) * sizeof(float);
+  a.tb = tour_tables; a.tb2 = pair_tables; a.n_iters = n_iters; a.S = S;
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid(n_rows, D);
+  int D1 = D;  // directions left for the one-direction kernel
+  if (pair_tables != nullptr && D >= 2) {
+    const size_t smem2 = (size_t)(13 * ntv + 128) * sizeof(float);
+    dim3 grid2(n_rows, D / 2);
+#define KB_LT2_CASE(V)                                                                                         \
+  case V:                                                                                                      \
+    if (smem2 > 48 * 1024 && cudaFuncSetAttribute((const void*)level_tangent2_kernel<V>,                      \
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2))   \
+      return KB_ERR_LAUNCH;                                                                                    \
+    level_tangent2_kernel<V><<<grid2, nt, smem2, st>>>(a);                                                     \
+    break;
+    switch (vf) {
+      KB_LT2_CASE(2) KB_LT2_CASE(4) KB_LT2_CASE(8)
+      default: return KB_ERR_SIZE;
+    }
+#undef KB_LT2_CASE
+    if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
+    D1 = D % 2;
+    if (D1 == 0) return KB_OK;
+    // the odd last direction runs alone below
+    const size_t od = (size_t)(D - 1) * dir_stride, ot = (size_t)(D - 1) * tangent_dir_stride;
+    a.dPi += od; a.dPibar += od;
+    a.dmc += ot; a.ddl += ot; a.debar += ot; a.de += ot; a.dsl1 += ot; a.dsl2 += ot; a.dleaf += ot;
+    a.dpD += ot; a.dpS += ot;
+  }
+  const size_t smem = (size_t)(7 * ntv + 96) * sizeof(float);
+  dim3 grid(n_rows, D1);
 #define KB_LT_CASE(V)                                                                                          \
   case V:                                                                                                      \
     if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_tangent_kernel<V>,                        \
@@ -1806,5 +2276,65 @@ extern "C" int kb_level_tangent(const int* rows, const long long* split_ptr, int
     default: return KB_ERR_SIZE;
   }
 #undef KB_LT_CASE
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                               const float* lsp, const int* dep0, const int* ready0, int n_ready0,
+                               const long long* par_ptr, const int* par_idx, int* queue, int* remaining,
+                               unsigned* counters, long long max_polls, float* pi, float* pibar,
+                               float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
+                               const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
+                               const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
+                               long long param_row_stride, long long const_row_stride, const int* node_parent,
+                               const int* node_child1, const int* node_child2, const int* node_subtree_start,
+                               const int* node_subtree_end, const int* jumps, int K, const long long* item_idx,
+                               const int* leaf_state, const unsigned* tour_tables, const float* tour_consts,
+                               int pi_iters, int S, void* stream) {
+  if (S <= 0 || C < 0 || K < 0 || pi_iters < 2 || n_ready0 < 0 || n_ready0 > C || max_polls < 1) return KB_ERR_ARG;
+  if (tour_tables == nullptr || tour_consts == nullptr || dts_save == nullptr || counters == nullptr) return KB_ERR_ARG;
+  int nt, vf;
+  const int ntv = tour_layout(S, nt, vf);
+  if (ntv == 0) return KB_ERR_SIZE;
+  if (C == 0) return KB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  FwdArgs a;
+  a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, nullptr, nullptr, nullptr, nullptr, log_pD, log_pS,
+                param_row_stride, const_row_stride, nullptr, 0, node_parent, node_child1, node_child2,
+                node_subtree_start, node_subtree_end, node_subtree_start, node_subtree_end, jumps, K, item_idx,
+                leaf_state, nullptr, S);
+  a.sp = SplitCSR{nullptr, nullptr, sl, sr, lsp};
+  a.Pi_src = pi; a.Pibar_src = pibar; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
+  a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = C;
+  a.pi_iters = pi_iters;
+  Fwd4Args a4;
+  a4.f = a;
+  a4.tb = tour_tables;
+  a4.k4 = reinterpret_cast<const float4*>(tour_consts);
+  a4.k4_rows = const_row_stride == 0 ? 0 : ntv;
+  Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), par_ptr, par_idx,
+         row_split_ptr, C, max_polls};
+  flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
+  if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
+  const size_t smem = (size_t)(4 * ntv + 96) * sizeof(float);
+  int dev = 0, n_sm = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KB_ERR_LAUNCH;
+#define KB_FF_CASE(V)                                                                                        \
+  case V:                                                                                                    \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)flow_forward_kernel<V>,                       \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))   \
+      return KB_ERR_LAUNCH;                                                                                  \
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flow_forward_kernel<V>, nt, smem) !=          \
+            cudaSuccess || per_sm < 1)                                                                       \
+      return KB_ERR_LAUNCH;                                                                                  \
+    flow_forward_kernel<V><<<(C < n_sm * per_sm ? C : n_sm * per_sm), nt, smem, st>>>(a4, f);                \
+    break;
+  switch (vf) {
+    KB_FF_CASE(2) KB_FF_CASE(4) KB_FF_CASE(8)
+    default: return KB_ERR_SIZE;
+  }
+#undef KB_FF_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }

@@ -36,6 +36,15 @@ class LevelPlan:
     level_of: np.ndarray       # level of every row (host)
     children_per_level: list   # distinct child rows referenced per level (for the traffic model)
     n_splits: int
+    # dataflow schedule (one persistent launch): splits in row-id order, dependency counts, parents
+    row_split_ptr: torch.Tensor  # int64 [C+1]
+    sl_r: torch.Tensor           # int64 [N]
+    sr_r: torch.Tensor
+    lsp_r: torch.Tensor          # f32 [N]
+    dep0: torch.Tensor           # int32 [C] distinct child rows
+    ready0: torch.Tensor         # int32 rows with dep0 == 0
+    par_ptr: torch.Tensor        # int64 [C+1] distinct parent rows of each row
+    par_idx: torch.Tensor        # int32
 
 
 def build_plan(static) -> LevelPlan:
@@ -81,6 +90,19 @@ def build_plan(static) -> LevelPlan:
     for L in range(n_levels):
         m = lv_of_split == L
         children.append(int(np.unique(np.concatenate([s_l[m], s_r[m]])).shape[0]) if m.any() else 0)
+    # dataflow arrays
+    order_r = np.lexsort((np.arange(par.shape[0]), par)) if par.shape[0] else np.zeros(0, np.int64)
+    cnt_r = np.bincount(par, minlength=C) if par.shape[0] else np.zeros(C, np.int64)
+    row_split_ptr = np.concatenate([[0], np.cumsum(cnt_r)]).astype(np.int64)
+    if par.shape[0]:
+        pairs = np.unique(np.stack([np.concatenate([par, par]), np.concatenate([sls, srs])], axis=1), axis=0)
+    else:
+        pairs = np.zeros((0, 2), np.int64)
+    dep0 = np.bincount(pairs[:, 0], minlength=C).astype(np.int32) if pairs.shape[0] else np.zeros(C, np.int32)
+    by_child = pairs[np.lexsort((pairs[:, 0], pairs[:, 1]))] if pairs.shape[0] else pairs
+    cnt_c = np.bincount(by_child[:, 1], minlength=C) if pairs.shape[0] else np.zeros(C, np.int64)
+    par_ptr = np.concatenate([[0], np.cumsum(cnt_c)]).astype(np.int64)
+    ready0 = np.nonzero(dep0 == 0)[0].astype(np.int32)
     plan = LevelPlan(
         n_levels=n_levels, level_ptr=level_ptr,
         rows=torch.from_numpy(order_rows.astype(np.int32)).to(dev),
@@ -89,6 +111,13 @@ def build_plan(static) -> LevelPlan:
         sr=torch.from_numpy(s_r.astype(np.int64)).to(dev),
         lsp=torch.from_numpy(lsps[order_splits].astype(np.float32)).to(dev),
         level_of=level, children_per_level=children, n_splits=int(par.shape[0]),
+        row_split_ptr=torch.from_numpy(row_split_ptr).to(dev),
+        sl_r=torch.from_numpy(sls[order_r].astype(np.int64)).to(dev),
+        sr_r=torch.from_numpy(srs[order_r].astype(np.int64)).to(dev),
+        lsp_r=torch.from_numpy(lsps[order_r].astype(np.float32)).to(dev),
+        dep0=torch.from_numpy(dep0).to(dev), ready0=torch.from_numpy(ready0).to(dev),
+        par_ptr=torch.from_numpy(par_ptr).to(dev),
+        par_idx=torch.from_numpy(by_child[:, 0].astype(np.int32)).to(dev),
     )
     static._plan = plan
     return plan
@@ -246,6 +275,23 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
     rows_ptr = plan.rows.data_ptr()
     sp_ptr = plan.split_ptr.data_ptr()
     use_tour = getattr(static, "_tour_forward", True) and tt.tour is not None and prep.k4 is not None
+    if use_tour and getattr(static, "_flow", True):
+        fl = _flow_scratch(static, C, dev)
+        _launch(static, "kb_flow_forward", 0, C, plan.row_split_ptr.data_ptr(), plan.sl_r.data_ptr(),
+                plan.sr_r.data_ptr(), plan.lsp_r.data_ptr(), plan.dep0.data_ptr(), plan.ready0.data_ptr(),
+                int(plan.ready0.numel()), plan.par_ptr.data_ptr(), plan.par_idx.data_ptr(), fl["queue"].data_ptr(),
+                fl["remaining"].data_ptr(), fl["counters"].data_ptr(), FLOW_MAX_POLLS, pi.data_ptr(),
+                pibar.data_ptr(), row_max.data_ptr(), dts.data_ptr(), _lib.ptr(pi_residual_out),
+                fallback.data_ptr(), k["mc"].data_ptr(), k["dl"].data_ptr(), k["ebar"].data_ptr(),
+                k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(),
+                pSp.data_ptr(), prs, crs, tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
+                topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
+                leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), int(so.pi_iters), S, st)
+        if int(fl["counters"][2].item()) != 0:
+            raise RuntimeError("kb_flow_forward: a dataflow wait gave up (dependency counts inconsistent)")
+        roots = pi[wl["root_row_ids"]]
+        out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
+        return out, {"dts_wave": dts}
     for L in range(plan.n_levels):
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
@@ -264,6 +310,22 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
     return out, {"dts_wave": dts}
+
+
+# Bound on one dataflow wait (polls of ~0.1-0.2 us each): far above any legitimate wait, so a
+# broken dependency structure ends the launch with an error instead of hanging the GPU.
+FLOW_MAX_POLLS = 1 << 25
+
+
+def _flow_scratch(static, C, dev) -> dict:
+    """Device scratch of the dataflow schedule (cached on the static)."""
+    fl = getattr(static, "_flow_scratch", None)
+    if fl is None or int(fl["queue"].numel()) != C or fl["queue"].device != dev:
+        fl = {"queue": torch.empty((C,), device=dev, dtype=torch.int32),
+              "remaining": torch.empty((C,), device=dev, dtype=torch.int32),
+              "counters": torch.zeros((3,), device=dev, dtype=torch.int32)}
+        static._flow_scratch = fl
+    return fl
 
 
 def new_grad_slots(static, dev) -> torch.Tensor:

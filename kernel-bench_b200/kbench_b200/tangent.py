@@ -226,7 +226,8 @@ def jvp_batch(static, theta, V, saved, *, self_iters=None, e_tol=None, return_fu
                        k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, 0, dmc.data_ptr(), dDL.data_ptr(),
                        dEbar.data_ptr(), dE.data_ptr(), dSL1.data_ptr(), dSL2.data_ptr(), dpS.data_ptr(),
                        dpD.data_ptr(), dpS.data_ptr(), S, item_idx.data_ptr(), leaf_state.data_ptr(),
-                       tt.tour.data_ptr(), n_it, S, st)
+                       tt.tour.data_ptr(), _lib.ptr(tt.tour_pair if getattr(static, "_tangent_pairs", True) else None),
+                       n_it, S, st)
     roots = dPi.index_select(1, wl["root_row_ids"])
     if return_full:
         return roots, {"dPi": dPi, "dPibar": dPibar, "dE": dE, "dE_s1": dE_s1, "dE_s2": dE_s2, "dEbar": dEbar,

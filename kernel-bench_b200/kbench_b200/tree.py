@@ -99,6 +99,36 @@ def pack_forward(parent, child1, child2, sub_start, sub_end):
     return out.astype(np.uint32).view(np.int32)
 
 
+def tour_phys_pair(i, vf: int):
+    """Swizzled position (in float2 entries) of logical tour index i in the two-direction tour layout
+    of the tangent kernel: thread t scans the 2*vf entries [t*2vf, (t+1)*2vf) as vf float4 groups
+    (two entries each) whose order inside the chunk is XOR-permuted by (t // (8 // vf))."""
+    import numpy as np
+    i = np.asarray(i, dtype=np.int64)
+    ch = 2 * vf
+    t, j = i // ch, i % ch
+    q, r = j // 2, j % 2
+    sw = 0 if vf == 1 else (t // (8 // vf)) & (vf - 1)
+    return t * ch + 2 * (q ^ sw) + r
+
+
+def pack_tour_pair(parent, child1, child2, sub_start, sub_end):
+    """[NTV] uint32 (viewed as int32): byte offsets of each column's enter | exit << 16 slots in
+    the two-direction (float2) tour layout, for NTV, VF = tour_layout(S)."""
+    import numpy as np
+    S = len(parent)
+    lay = tour_layout(S)
+    if lay is None:
+        raise ValueError("row too wide for the tour kernels")
+    ntv, _, vf = lay
+    pk = pack_columns(parent, child1, child2, sub_start, sub_end, ntv=ntv).view(np.uint32).astype(np.int64)
+    be = 8 * tour_phys_pair(pk[1] & 0xFFFF, vf)
+    bx = 8 * tour_phys_pair(pk[1] >> 16, vf)
+    if max(be.max(), bx.max()) > 0xFFFF:
+        raise ValueError("pair tour byte offsets exceed 16 bits")
+    return (be | (bx << 16)).astype(np.uint32).view(np.int32)
+
+
 def pack_columns(parent, child1, child2, sub_start, sub_end, ntv=None):
     """Per-column 32-bit tables (two 16-bit fields each) read once per CTA by the engine kernels:
 
@@ -246,4 +276,6 @@ def from_helpers(sh: dict) -> TreeTables:
         tt.packed_pad = torch.from_numpy(pack_columns(*arrs, ntv=bd * vpt)).to(dev).contiguous()
         tt.tour = (torch.from_numpy(pack_forward(*arrs)).to(dev).contiguous()
                    if tour_layout(int(sh["S"])) is not None else None)
+        tt.tour_pair = (torch.from_numpy(pack_tour_pair(*arrs)).to(dev).contiguous()
+                        if tour_layout(int(sh["S"])) is not None else None)
     return tt
