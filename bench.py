@@ -156,6 +156,15 @@ def algorithmic_bytes(plan, S):
     return fwd, bwd
 
 
+def kernel_bytes(name, per, fwd_b, bwd_b):
+    """Algorithmic bytes of the launches ``per`` [(level, ms)] of one engine kernel: a level launch
+    covers its level, a dataflow launch (kb_flow_*) the whole sweep."""
+    bm = fwd_b if "forward" in name else bwd_b
+    if name.startswith("kb_flow_"):
+        return len(per) * sum(bm.values())
+    return sum(bm[lv] for lv, _ in per)
+
+
 def cpu_sample_case(n_genes, S_species_leaves=2048):
     """A bounded sample of the workload for the CPU oracle: the benchmark's species tree size
     with a small gene family (same per-row work, fewer rows)."""
@@ -233,10 +242,11 @@ def roofline_from_timers(timers, peak, peak_kind, steps):
         plan = engine.build_plan(static)
         fwd_b, bwd_b = algorithmic_bytes(plan, int(static.state_helpers["S"]))
         for name, (ms, n, per) in timer.totals().items():
-            bm = fwd_b if name == "kb_level_forward" else bwd_b
+            if n == 0:
+                continue
             k_ms[name] = k_ms.get(name, 0.0) + ms / steps
             k_n[name] = k_n.get(name, 0) + n / steps
-            k_bytes[name] = k_bytes.get(name, 0.0) + sum(bm[lv] for lv, _ in per) / steps
+            k_bytes[name] = k_bytes.get(name, 0.0) + kernel_bytes(name, per, fwd_b, bwd_b) / steps
     dominant = max(k_ms, key=k_ms.get)
     achieved = k_bytes[dominant] / (k_ms[dominant] * 1e-3) / 1e9
     return {
@@ -605,8 +615,7 @@ def main():
         k_tot = {name: v[0] / args.steps for name, v in totals.items()}
         dominant = max(k_tot, key=k_tot.get)
         per = totals[dominant][2]
-        bytes_map = fwd_b if dominant == "kb_level_forward" else bwd_b
-        alg_bytes = sum(bytes_map[lv] for lv, _ in per) / args.steps
+        alg_bytes = kernel_bytes(dominant, per, fwd_b, bwd_b) / args.steps
         k_ms = k_tot[dominant]
         achieved = alg_bytes / (k_ms * 1e-3) / 1e9
         n_launch = totals[dominant][1] / args.steps
@@ -616,7 +625,7 @@ def main():
             "traffic": None,
             "algorithmic_bytes_per_launch": alg_bytes / n_launch,
             "avg_launch_ms": k_ms / n_launch,
-            "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items()},
+            "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items() if v > 0},
         }
         cpu = None
         if world == 1 and not args.no_cpu_baseline:

@@ -260,6 +260,26 @@ int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, c
                       int use_col_weights, const long long* item_idx, const int* leaf_state,
                       const unsigned* packed_padded, int S, void* stream);
 
+/* The whole backward in ONE persistent launch with a dataflow schedule (replaces the per-level
+ * kb_level_backward launches, same per-row arithmetic): a row starts as soon as every row that
+ * lists it as a split child (its parents) has added its cotangents.  row_split_ptr [C+1] into sl /
+ * sr / lsp (row-id order); dep0 [C]: number of distinct parent rows; ready0 [n_ready0]: rows
+ * without parents (the roots); child_ptr [C+1] / child_idx: the distinct child rows of each row.
+ * Scratch queue [C], remaining [C], counters [3] (head, tail, error: nonzero after the launch =
+ * a wait gave up after max_polls polls, results invalid).  grad_slots [n_slots, 8, NTV]: one per
+ * persistent CTA (n_slots CTAs run).  Other arguments as kb_level_backward. */
+int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                     const float* lsp, const int* dep0, const int* ready0, int n_ready0, const long long* child_ptr,
+                     const int* child_idx, int* queue, int* remaining, unsigned* counters, long long max_polls,
+                     const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts_saved,
+                     float* accumulated_rhs, float* v_out, double* grad_slots, int n_slots, float threshold,
+                     int strict_gt, float side_threshold, int side_threshold_enabled, int neumann_terms,
+                     const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
+                     const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
+                     long long param_row_stride, long long const_row_stride, const float* col_log_probs,
+                     int use_col_weights, const long long* item_idx, const int* leaf_state,
+                     const unsigned* packed_padded, int S, void* stream);
+
 /* Fixed-order sum of kb_level_backward's fp64 slots -> out8 [8,S] fp32: the cotangents of
  * log_pD, log_pS, max_coupling, E, Ebar, E_s1, E_s2 and col_log_probs (in that order). */
 int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S, float* out8, void* stream);

@@ -731,12 +731,14 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
           const float vbr = ld_row<DF>(pbr + s), vbl = ld_row<DF>(pbl + s);
           const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
           const float pl = Pl[s], pr = Pr[s];
+          // left-to-right sums, as the reference forms the terms (dts_fused.py:54-60): at log
+          // magnitudes ~1e2 a different association moves the terms by an ulp (~1e-5)
           const float lss = lsp + ls;
-          const float v0 = (lsp + ld) + (pl + pr);
+          const float v0 = lsp + ld + pl + pr;
           const float v1 = lsp + pl + vbr;
           const float v2 = lsp + pr + vbl;
-          const float v3 = lss + (Pl[ca] + Pr[cbb]);
-          const float v4 = lss + (Pr[ca] + Pl[cbb]);
+          const float v3 = lss + Pl[ca] + Pr[cbb];
+          const float v4 = lss + Pr[ca] + Pl[cbb];
           const float mx = fmaxf(fmaxf(fmaxf(m[k], v0), fmaxf(v1, v2)), fmaxf(v3, v4));
           const float ms = safe_max(mx);
           acc[k] = fmaf(acc[k], ex2(m[k] - ms),
@@ -974,11 +976,11 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, int* shared_slot) {
   return row;
 }
 
-// After a row's outputs are written by the whole CTA: release its parents.
+// After a row's outputs are written by the whole CTA: release the rows that wait on it.
 __device__ __forceinline__ void flow_finish_row(const Flow& f, int row) {
-  __syncthreads();
+  __threadfence();  // every thread's outputs (stores and atomics) are device-visible ...
+  __syncthreads();  // ... before thread 0 releases the dependent rows
   if (threadIdx.x == 0) {
-    __threadfence();  // this row's outputs before any parent is queued
     for (long long j = f.par_ptr[row]; j < f.par_ptr[row + 1]; ++j) {
       const int p = f.par_idx[j];
       if (atomicSub(f.remaining + p, 1) == 1) {
@@ -1602,8 +1604,12 @@ struct BwdArgs {
 // accumulator rows of the per-CTA column sums
 enum { G_PD = 0, G_PS, G_MT, G_E, G_EBAR, G_ES1, G_ES2, G_COL, G_N };
 
-template <int VPT>
-__global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a) {
+#define KB_FLOW_FLUSH_ROWS 8
+
+// DF = the dataflow schedule (one persistent launch; f.par_ptr / par_idx then list each row's
+// distinct CHILD rows, released when the row is done; a row is ready once all its parents ran).
+template <int VPT, bool DF>
+__global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a, Flow f) {
   extern __shared__ float sm[];
   const LevelConsts& c = a.c;
   const int S = c.S;
@@ -1625,12 +1631,27 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a) {
 #pragma unroll
     for (int j = 0; j < G_N; ++j) ACC[j * NTV + s] = 0.f;
   }
-  for (int b = blockIdx.x; b < a.n_rows; b += gridDim.x) {
-    const long long row = a.sp.rows[b];
+  __shared__ int flow_slot;
+  int b = blockIdx.x;
+  int since_flush = 0;  // DF: rows accumulated in the fp32 shared sums since the last fp64 flush
+  for (;;) {
+    long long row, i0, i1;
+    if (DF) {
+      const int r = flow_next_row(f, &flow_slot);
+      if (r < 0) break;
+      row = r;
+      i0 = f.row_split_ptr[r];
+      i1 = f.row_split_ptr[r + 1];
+    } else {
+      if (b >= a.n_rows) break;
+      row = a.sp.rows[b];
+      i0 = a.sp.split_ptr[b];
+      i1 = a.sp.split_ptr[b + 1];
+      b += gridDim.x;
+    }
     const long long item = c.item_idx[row];
     const size_t cb = (size_t)(item * c.crs);
     const size_t pb = (size_t)(item * c.prs);
-    const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
     const bool has_splits = i1 > i0;
     const int leaf_raw = c.leaf_state[row];
     const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
@@ -1642,12 +1663,15 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a) {
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
-      v[k] = s < S ? rrow[s] : 0.f;
+      v[k] = s < S ? (DF ? __ldcg(rrow + s) : rrow[s]) : 0.f;  // DF: parents add with atomics (L2)
       amax = fmaxf(amax, fabsf(v[k]));
     }
     amax = block_max(amax, red);
     const bool active = a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold);
-    if (!active) continue;
+    if (!active) {
+      if (DF) flow_finish_row(f, (int)row);
+      continue;
+    }
 
     // ---- dts row (log) ----
     float dv[VPT];
@@ -1941,6 +1965,24 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a) {
         }
       }
     }
+    if (DF) {
+      flow_finish_row(f, (int)row);
+      // A persistent CTA runs hundreds of rows: keep the fp32 partial sums short (as a level launch
+      // does) by moving them into the fp64 slot every few rows.  Own columns only: no barrier.
+      if (++since_flush == KB_FLOW_FLUSH_ROWS) {
+        since_flush = 0;
+        double* slot = a.slots + (size_t)blockIdx.x * G_N * NTV;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          const int s = threadIdx.x + k * NT;
+#pragma unroll
+          for (int j = 0; j < G_N; ++j) {
+            slot[(size_t)j * NTV + s] += (double)ACC[j * NTV + s];
+            ACC[j * NTV + s] = 0.f;
+          }
+        }
+      }
+    }
   }
   // ---- flush this CTA's column sums into its fp64 slot ----
   double* slot = a.slots + (size_t)blockIdx.x * G_N * NTV;
@@ -2177,12 +2219,13 @@ extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, in
   const size_t smem = (size_t)((3 + G_N) * ntv + 128) * sizeof(float);
   const int grid = n_rows < n_slots ? n_rows : n_slots;
   cudaStream_t st = (cudaStream_t)stream;
+  const Flow nof{};
 #define KB_LB_CASE(V)                                                                                      \
   case V:                                                                                                  \
-    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_backward_kernel<V>,                   \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_backward_kernel<V, false>,            \
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))  \
       return KB_ERR_LAUNCH;                                                                                \
-    level_backward_kernel<V><<<grid, bd, smem, st>>>(a);                                                   \
+    level_backward_kernel<V, false><<<grid, bd, smem, st>>>(a, nof);                                       \
     break;
   switch (vpt) {
     KB_LB_CASE(1) KB_LB_CASE(2) KB_LB_CASE(4) KB_LB_CASE(8)
@@ -2336,5 +2379,56 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
     default: return KB_ERR_SIZE;
   }
 #undef KB_FF_CASE
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                                const float* lsp, const int* dep0, const int* ready0, int n_ready0,
+                                const long long* child_ptr, const int* child_idx, int* queue, int* remaining,
+                                unsigned* counters, long long max_polls, const float* Pi, const float* Pibar,
+                                const float* pibar_row_max, const float* dts_saved, float* accumulated_rhs,
+                                float* v_out, double* grad_slots, int n_slots, float threshold, int strict_gt,
+                                float side_threshold, int side_threshold_enabled, int neumann_terms,
+                                const float* mc, const float* dl, const float* ebar, const float* e,
+                                const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
+                                const float* log_pS, long long param_row_stride, long long const_row_stride,
+                                const float* col_log_probs, int use_col_weights, const long long* item_idx,
+                                const int* leaf_state, const unsigned* packed_padded, int S, void* stream) {
+  if (S <= 0 || C < 0 || neumann_terms < 0 || n_slots <= 0 || n_ready0 < 0 || n_ready0 > C || max_polls < 1 ||
+      counters == nullptr)
+    return KB_ERR_ARG;
+  if (S > KB_MAX_S) return KB_ERR_SIZE;
+  if (C == 0) return KB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  BwdArgs a;
+  a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, nullptr, nullptr, nullptr, nullptr, log_pD, log_pS,
+                param_row_stride, const_row_stride, col_log_probs, use_col_weights, nullptr, nullptr, nullptr,
+                nullptr, nullptr, nullptr, nullptr, nullptr, 0, item_idx, leaf_state, packed_padded, S);
+  a.sp = SplitCSR{nullptr, nullptr, sl, sr, lsp};
+  a.Pi = Pi; a.Pibar = Pibar; a.row_max = pibar_row_max; a.dts_saved = dts_saved; a.acc = accumulated_rhs;
+  a.v_out = v_out; a.slots = grad_slots; a.threshold = threshold; a.strict_gt = strict_gt;
+  a.side_thr = side_threshold; a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms;
+  a.n_rows = C;
+  Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), child_ptr, child_idx,
+         row_split_ptr, C, max_polls};
+  flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
+  if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
+  int bd;
+  const int vpt = engine_width(S, bd);
+  const int ntv = bd * vpt;
+  const size_t smem = (size_t)((3 + G_N) * ntv + 128) * sizeof(float);
+  const int grid = C < n_slots ? C : n_slots;  // persistent CTAs, one fp64 slot each
+#define KB_FB_CASE(V)                                                                                      \
+  case V:                                                                                                  \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_backward_kernel<V, true>,             \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))  \
+      return KB_ERR_LAUNCH;                                                                                \
+    level_backward_kernel<V, true><<<grid, bd, smem, st>>>(a, f);                                          \
+    break;
+  switch (vpt) {
+    KB_FB_CASE(1) KB_FB_CASE(2) KB_FB_CASE(4) KB_FB_CASE(8)
+    default: return KB_ERR_SIZE;
+  }
+#undef KB_FB_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }

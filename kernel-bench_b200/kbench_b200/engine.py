@@ -45,6 +45,10 @@ class LevelPlan:
     ready0: torch.Tensor         # int32 rows with dep0 == 0
     par_ptr: torch.Tensor        # int64 [C+1] distinct parent rows of each row
     par_idx: torch.Tensor        # int32
+    dep_b: torch.Tensor          # int32 [C] distinct parent rows (backward dependencies)
+    ready_b: torch.Tensor        # int32 rows without parents
+    child_ptr: torch.Tensor      # int64 [C+1] distinct child rows of each row
+    child_idx: torch.Tensor      # int32
 
 
 def build_plan(static) -> LevelPlan:
@@ -103,6 +107,10 @@ def build_plan(static) -> LevelPlan:
     cnt_c = np.bincount(by_child[:, 1], minlength=C) if pairs.shape[0] else np.zeros(C, np.int64)
     par_ptr = np.concatenate([[0], np.cumsum(cnt_c)]).astype(np.int64)
     ready0 = np.nonzero(dep0 == 0)[0].astype(np.int32)
+    dep_b = cnt_c.astype(np.int32)
+    ready_b = np.nonzero(dep_b == 0)[0].astype(np.int32)
+    cnt_p = np.bincount(pairs[:, 0], minlength=C) if pairs.shape[0] else np.zeros(C, np.int64)
+    child_ptr = np.concatenate([[0], np.cumsum(cnt_p)]).astype(np.int64)  # pairs are sorted by parent
     plan = LevelPlan(
         n_levels=n_levels, level_ptr=level_ptr,
         rows=torch.from_numpy(order_rows.astype(np.int32)).to(dev),
@@ -118,6 +126,9 @@ def build_plan(static) -> LevelPlan:
         dep0=torch.from_numpy(dep0).to(dev), ready0=torch.from_numpy(ready0).to(dev),
         par_ptr=torch.from_numpy(par_ptr).to(dev),
         par_idx=torch.from_numpy(by_child[:, 0].astype(np.int32)).to(dev),
+        dep_b=torch.from_numpy(dep_b).to(dev), ready_b=torch.from_numpy(ready_b).to(dev),
+        child_ptr=torch.from_numpy(child_ptr).to(dev),
+        child_idx=torch.from_numpy(pairs[:, 1].astype(np.int32)).to(dev),
     )
     static._plan = plan
     return plan
@@ -394,6 +405,35 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
     rows_ptr = plan.rows.data_ptr()
     sp_ptr = plan.split_ptr.data_ptr()
     clp = f32(saved["col_log_probs"])
+    if getattr(static, "_flow", True):
+        fl = _flow_scratch(static, C, dev)
+        _launch(static, "kb_flow_backward", 0, C, plan.row_split_ptr.data_ptr(), plan.sl_r.data_ptr(),
+                plan.sr_r.data_ptr(), plan.lsp_r.data_ptr(), plan.dep_b.data_ptr(), plan.ready_b.data_ptr(),
+                int(plan.ready_b.numel()), plan.child_ptr.data_ptr(), plan.child_idx.data_ptr(),
+                fl["queue"].data_ptr(), fl["remaining"].data_ptr(), fl["counters"].data_ptr(), FLOW_MAX_POLLS,
+                Pi.data_ptr(), Pibar.data_ptr(), row_max.data_ptr(), _lib.ptr(dts), acc.data_ptr(),
+                _lib.ptr(v_out), slots.data_ptr(), n_slots, thr, int(not so.use_adjoint_pruning), side_thr,
+                int(side_thr > 0.0), int(so.neumann_terms), k["mc"].data_ptr(), k["dl"].data_ptr(),
+                k["ebar"].data_ptr(), k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(),
+                k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
+                item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(), S, st)
+        if int(fl["counters"][2].item()) != 0:
+            raise RuntimeError("kb_flow_backward: a dataflow wait gave up (dependency counts inconsistent)")
+    else:
+        _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr,
+                         so, side_thr, k, pDp, pSp, prs, crs, clp, ucw, item_idx, leaf_state, tt, S, st)
+    static._last_acc = acc
+    if not finish:
+        return None
+    out8 = torch.empty((8, S), device=dev, dtype=torch.float32)
+    _lib.call("kb_reduce_grad_slots", slots.data_ptr(), n_slots, S, out8.data_ptr(), st)
+    g = grad_accumulators_from(E, S, out8)
+    return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
+
+
+def _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr, so,
+                     side_thr, k, pDp, pSp, prs, crs, clp, ucw, item_idx, leaf_state, tt, S, st):
+    """The level-by-level backward schedule (one kb_level_backward launch per level)."""
     for L in reversed(range(plan.n_levels)):
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
@@ -406,10 +446,3 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
                 k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(),
                 prs, crs, clp.data_ptr(), int(ucw), item_idx.data_ptr(), leaf_state.data_ptr(),
                 tt.packed_pad.data_ptr(), S, st)
-    static._last_acc = acc
-    if not finish:
-        return None
-    out8 = torch.empty((8, S), device=dev, dtype=torch.float32)
-    _lib.call("kb_reduce_grad_slots", slots.data_ptr(), n_slots, S, out8.data_ptr(), st)
-    g = grad_accumulators_from(E, S, out8)
-    return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
