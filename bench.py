@@ -459,14 +459,15 @@ def tangent_arm(args, world, rank, local):
     e_ms = float(x_t.item())
     if rank == 0:
         peak, peak_kind = measured_peak()
-        k_ms = {n: v[0] / args.steps for n, v in totals.items()}
-        n_l = totals["kb_level_tangent"][1] / args.steps
-        # compulsory bytes of the tangent levels: per direction write dPi, dPibar of every row and
+        k_ms = {n: v[0] / args.steps for n, v in totals.items() if v[1] > 0}
+        tname = "kb_flow_tangent" if "kb_flow_tangent" in k_ms else "kb_level_tangent"
+        n_l = totals[tname][1] / args.steps
+        # compulsory bytes of the tangent sweep: per direction write dPi, dPibar of every row and
         # read dPi, dPibar of each distinct child once per level; the primal rows once
         kb = sum(4 * S * (D * (2 * (plan.level_ptr[L + 1] - plan.level_ptr[L]) + 2 * plan.children_per_level[L])
                           + 3 * (plan.level_ptr[L + 1] - plan.level_ptr[L]))
                  for L in range(plan.n_levels))
-        ach = kb / (k_ms["kb_level_tangent"] * 1e-3) / 1e9
+        ach = kb / (k_ms[tname] * 1e-3) / 1e9
         line = {
             "metric": f"fwd + {D}-direction tangent passes/sec (S=4095, C~131k; BASELINE tangent config)",
             "value": round(world * 1000.0 / ms_max, 4), "unit": "passes/s", "n_gpus": world, "steps": args.steps,
@@ -478,10 +479,10 @@ def tangent_arm(args, world, rank, local):
                        "l2": "state arrays far larger than L2; no flush needed"},
             "fwd_ms": round(fwd_ms, 3), "tangent_ms": round(tan_ms, 3),
             "fd_check": {"eps": eps, "rel_err": fd_err, "tolerance": 1e-3},
-            "roofline": {"bound": "hbm", "kernel": "kb_level_tangent", "achieved": round(ach, 1), "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": tname, "achieved": round(ach, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": None, "algorithmic_bytes_per_launch": kb / n_l,
-                         "avg_launch_ms": k_ms["kb_level_tangent"] / n_l,
+                         "avg_launch_ms": k_ms[tname] / n_l,
                          "kernel_ms_per_step": {k2: round(v, 3) for k2, v in k_ms.items()}},
             "cpu_baseline": None,
             "e2e": {"value": round(world * 1000.0 / e_ms, 4), "unit": "passes/s",

@@ -359,6 +359,25 @@ int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, co
                      const int* leaf_state, const unsigned* tour_tables, const unsigned* pair_tables,
                      int n_iters, int S, void* stream);
 
+/* The whole tangent sweep for D (even) directions in ONE persistent launch with a dataflow
+ * schedule (replaces the per-level kb_level_tangent launches, same per-row arithmetic as its
+ * two-direction kernel): work items are (direction pair, row); an item starts when the same
+ * pair's child rows are done.  Dependency arrays as kb_flow_forward (dep0 = distinct child rows,
+ * ready0 = rows with none, par_ptr / par_idx = distinct parents).  Scratch queue / remaining
+ * [C * D/2] int, counters [3] (head, tail, error; error != 0 = a wait gave up, results invalid).
+ * pair_tables required.  Other arguments as kb_level_tangent. */
+int kb_flow_tangent(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                    const float* lsp, const int* dep0, const int* ready0, int n_ready0, const long long* par_ptr,
+                    const int* par_idx, int* queue, int* remaining, unsigned* counters, long long max_polls,
+                    const float* Pi, const float* Pibar, const float* dts_saved, float* dPi, float* dPibar,
+                    long long dir_stride, int D, const float* mc, const float* dl, const float* ebar, const float* e,
+                    const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
+                    const float* log_pS, long long param_row_stride, long long const_row_stride, const float* dMC,
+                    const float* dDL, const float* dEbar, const float* dE, const float* dSL1, const float* dSL2,
+                    const float* dleaf, const float* dpD, const float* dpS, long long tangent_dir_stride,
+                    const long long* item_idx, const int* leaf_state, const unsigned* tour_tables,
+                    const unsigned* pair_tables, int n_iters, int S, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -934,17 +934,20 @@ __global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args arg
 // queue slots in order.  Every wait on a queue slot is bounded: past the limit the CTA records an
 // error and leaves (the host then reports the failure; it never hangs).
 
+// Work items are (group, row) pairs, item = group * C + row: one group for the forward and the
+// backward, one per tangent direction pair; an item waits for the same group's dependencies.
 struct Flow {
-  int* queue;              // [C] rows in start order; -1 = slot not yet filled
-  int* remaining;          // [C] unfinished children per row
+  int* queue;              // [n_items] items in start order; -1 = slot not yet filled
+  int* remaining;          // [n_items] unfinished dependencies per item
   unsigned* head;          // next slot to take
   unsigned* tail;          // next slot to fill
   int* error;              // set to 1 when a wait gave up
-  const long long* par_ptr;  // [C+1] CSR: distinct parent rows of each row
+  const long long* par_ptr;  // [C+1] CSR: the rows released by each row
   const int* par_idx;
   const long long* row_split_ptr;  // [C+1] splits of each row (row-id order)
   int C;
   long long max_polls;
+  int n_items;             // C * groups
 };
 
 // Claims the next queue slot and waits (bounded) until it holds a row.  Returns the row, -1 when
@@ -953,7 +956,7 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, int* shared_slot) {
   if (threadIdx.x == 0) {
     const unsigned idx = atomicAdd(f.head, 1u);
     int row = -1;
-    if (idx < (unsigned)f.C) {
+    if (idx < (unsigned)f.n_items) {
       const volatile int* q = f.queue + idx;
       long long polls = 0;
       row = *q;
@@ -981,8 +984,10 @@ __device__ __forceinline__ void flow_finish_row(const Flow& f, int row) {
   __threadfence();  // every thread's outputs (stores and atomics) are device-visible ...
   __syncthreads();  // ... before thread 0 releases the dependent rows
   if (threadIdx.x == 0) {
-    for (long long j = f.par_ptr[row]; j < f.par_ptr[row + 1]; ++j) {
-      const int p = f.par_idx[j];
+    const int grp = row / f.C;
+    const int r = row - grp * f.C;
+    for (long long j = f.par_ptr[r]; j < f.par_ptr[r + 1]; ++j) {
+      const int p = grp * f.C + f.par_idx[j];
       if (atomicSub(f.remaining + p, 1) == 1) {
         const unsigned slot = atomicAdd(f.tail, 1u);
         atomicExch(f.queue + slot, p);
@@ -1003,16 +1008,18 @@ __global__ void __launch_bounds__(512, 2) flow_forward_kernel(Fwd4Args args, Flo
   }
 }
 
-// Queue / counter initialisation of one dataflow run: remaining = dep0, queue = the rows ready
-// at the start (n0 of them, given in ready0) followed by -1, head = 0, tail = n0, error = 0.
+// Queue / counter initialisation of one dataflow run: remaining = dep0 of each item's row, queue =
+// the ready rows (n0 of them, given in ready0) of every group followed by -1, head = 0, tail =
+// n0 * groups, error = 0.
 __global__ void flow_init_kernel(Flow f, const int* dep0, const int* ready0, int n0) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < f.C; i += gridDim.x * blockDim.x) {
-    f.remaining[i] = dep0[i];
-    f.queue[i] = i < n0 ? ready0[i] : -1;
+  const int groups = f.n_items / f.C;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < f.n_items; i += gridDim.x * blockDim.x) {
+    f.remaining[i] = dep0[i % f.C];
+    f.queue[i] = i < n0 * groups ? (i / n0) * f.C + ready0[i % n0] : -1;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *f.head = 0u;
-    *f.tail = (unsigned)n0;
+    *f.tail = (unsigned)(n0 * groups);
     *f.error = 0;
   }
 }
@@ -1335,9 +1342,9 @@ __device__ __forceinline__ float2& pair_at(float2* base, unsigned off) {
 // weights, the Euler-tour addressing and the split weights are shared by the two directions,
 // which travel together as float2 through the tour scan and the gathers.  Same arithmetic as
 // level_tangent_kernel.
-template <int VF>
-__global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
-  extern __shared__ __align__(16) float sm[];
+template <int VF, bool DF>
+__device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row, long long i0, long long i1, int d0,
+                                                 float* sm) {
   const unsigned* __restrict__ tb = a.tb;
   const unsigned* __restrict__ tp = a.tb2;
   const int S = a.S;
@@ -1350,14 +1357,10 @@ __global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
   float* PR = reinterpret_cast<float*>(DP1 + NTV);
   float* red = PR + NTV;
   const int tid = threadIdx.x;
-  const int b = blockIdx.x;
-  const int d0 = 2 * blockIdx.y;
-  const long long row = a.sp.rows[b];
   const long long item = a.item_idx[row];
   const size_t cb = (size_t)(item * a.crs);
   const size_t pb = (size_t)(item * a.prs);
   const size_t tofa = (size_t)d0 * a.tstride, tofb = tofa + (size_t)a.tstride;
-  const long long i0 = a.sp.split_ptr[b], i1 = a.sp.split_ptr[b + 1];
   const bool has_splits = i1 > i0;
   const int leaf_raw = a.leaf_state[row];
   const int leaf = (!has_splits && leaf_raw >= 0 && leaf_raw < S) ? leaf_raw : -1;
@@ -1465,10 +1468,10 @@ __global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
         const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
         Pl[s] = real ? a.Pi[ol] : neg_inf();
         Pr[s] = real ? a.Pi[orr] : neg_inf();
-        Qla[s] = real ? dPa[ol] : 0.f;
-        Qra[s] = real ? dPa[orr] : 0.f;
-        Qlb[s] = real ? dPb[ol] : 0.f;
-        Qrb[s] = real ? dPb[orr] : 0.f;
+        Qla[s] = real ? (DF ? __ldcg(dPa + ol) : dPa[ol]) : 0.f;  // DF: children written in this launch
+        Qra[s] = real ? (DF ? __ldcg(dPa + orr) : dPa[orr]) : 0.f;
+        Qlb[s] = real ? (DF ? __ldcg(dPb + ol) : dPb[ol]) : 0.f;
+        Qrb[s] = real ? (DF ? __ldcg(dPb + orr) : dPb[orr]) : 0.f;
       }
       __syncthreads();
 #pragma unroll
@@ -1485,11 +1488,13 @@ __global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
           const float w3 = ex2(lsp + ls + Pl[ca] + Pr[cbb] - dts);
           const float w4 = ex2(lsp + ls + Pr[ca] + Pl[cbb] - dts);
           const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
-          const float xa = w0 * (a.dpD[tofa + pb + s] + Qla[s] + Qra[s]) + w1 * (Qla[s] + dBa[orr]) +
-                           w2 * (Qra[s] + dBa[ol]) + w3 * (a.dpS[tofa + pb + s] + Qla[ca] + Qra[cbb]) +
+          const float bar_a = DF ? __ldcg(dBa + orr) : dBa[orr], bal_a = DF ? __ldcg(dBa + ol) : dBa[ol];
+          const float bar_b = DF ? __ldcg(dBb + orr) : dBb[orr], bal_b = DF ? __ldcg(dBb + ol) : dBb[ol];
+          const float xa = w0 * (a.dpD[tofa + pb + s] + Qla[s] + Qra[s]) + w1 * (Qla[s] + bar_a) +
+                           w2 * (Qra[s] + bal_a) + w3 * (a.dpS[tofa + pb + s] + Qla[ca] + Qra[cbb]) +
                            w4 * (a.dpS[tofa + pb + s] + Qra[ca] + Qla[cbb]);
-          const float xb = w0 * (a.dpD[tofb + pb + s] + Qlb[s] + Qrb[s]) + w1 * (Qlb[s] + dBb[orr]) +
-                           w2 * (Qrb[s] + dBb[ol]) + w3 * (a.dpS[tofb + pb + s] + Qlb[ca] + Qrb[cbb]) +
+          const float xb = w0 * (a.dpD[tofb + pb + s] + Qlb[s] + Qrb[s]) + w1 * (Qlb[s] + bar_b) +
+                           w2 * (Qrb[s] + bal_b) + w3 * (a.dpS[tofb + pb + s] + Qlb[ca] + Qrb[cbb]) +
                            w4 * (a.dpS[tofb + pb + s] + Qrb[ca] + Qlb[cbb]);
           ca_[k] = fmaf(cD[k], xa, ca_[k]);
           cb_[k] = fmaf(cD[k], xb, cb_[k]);
@@ -1576,6 +1581,28 @@ __global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
       outpa[s] = dpa[k];
       outpb[s] = dpb[k];
     }
+  }
+}
+
+template <int VF>
+__global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int b = blockIdx.x;
+  tangent_pair_row<VF, false>(a, a.sp.rows[b], a.sp.split_ptr[b], a.sp.split_ptr[b + 1], 2 * (int)blockIdx.y, sm);
+}
+
+// Dataflow tangent: items (direction pair, row); an item starts when the same pair's child rows
+// are done.
+template <int VF>
+__global__ void __launch_bounds__(512, 1) flow_tangent2_kernel(TanArgs a, Flow f) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int slot;
+  for (;;) {
+    const int itm = flow_next_row(f, &slot);
+    if (itm < 0) break;
+    const int pair = itm / f.C, row = itm - pair * f.C;
+    tangent_pair_row<VF, true>(a, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], 2 * pair, sm);
+    flow_finish_row(f, itm);
   }
 }
 
@@ -2356,7 +2383,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
   a4.k4 = reinterpret_cast<const float4*>(tour_consts);
   a4.k4_rows = const_row_stride == 0 ? 0 : ntv;
   Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), par_ptr, par_idx,
-         row_split_ptr, C, max_polls};
+         row_split_ptr, C, max_polls, C};
   flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
   const size_t smem = (size_t)(4 * ntv + 96) * sizeof(float);
@@ -2410,7 +2437,7 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   a.side_thr = side_threshold; a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms;
   a.n_rows = C;
   Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), child_ptr, child_idx,
-         row_split_ptr, C, max_polls};
+         row_split_ptr, C, max_polls, C};
   flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
   int bd;
@@ -2430,5 +2457,64 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
     default: return KB_ERR_SIZE;
   }
 #undef KB_FB_CASE
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_flow_tangent(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
+                               const float* lsp, const int* dep0, const int* ready0, int n_ready0,
+                               const long long* par_ptr, const int* par_idx, int* queue, int* remaining,
+                               unsigned* counters, long long max_polls, const float* Pi, const float* Pibar,
+                               const float* dts_saved, float* dPi, float* dPibar, long long dir_stride, int D,
+                               const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
+                               const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
+                               long long param_row_stride, long long const_row_stride, const float* dMC,
+                               const float* dDL, const float* dEbar, const float* dE, const float* dSL1,
+                               const float* dSL2, const float* dleaf, const float* dpD, const float* dpS,
+                               long long tangent_dir_stride, const long long* item_idx, const int* leaf_state,
+                               const unsigned* tour_tables, const unsigned* pair_tables, int n_iters, int S,
+                               void* stream) {
+  if (S <= 0 || C < 0 || D <= 0 || (D & 1) || n_iters < 1 || tour_tables == nullptr || pair_tables == nullptr ||
+      dts_saved == nullptr || counters == nullptr || n_ready0 < 0 || n_ready0 > C || max_polls < 1)
+    return KB_ERR_ARG;
+  int nt, vf;
+  const int ntv = tour_layout(S, nt, vf);
+  if (ntv == 0) return KB_ERR_SIZE;
+  if (C == 0) return KB_OK;
+  if ((long long)C * (D / 2) > 0x7FFFFFFFLL) return KB_ERR_SIZE;
+  TanArgs a;
+  a.sp = SplitCSR{nullptr, nullptr, sl, sr, lsp};
+  a.Pi = Pi; a.Pibar = Pibar; a.dts = dts_saved; a.dPi = dPi; a.dPibar = dPibar; a.dstride = dir_stride;
+  a.mc = mc; a.dl = dl; a.ebar = ebar; a.e = e; a.sl1 = sl1; a.sl2 = sl2; a.leaf_logp = leaf_logp;
+  a.log_pD = log_pD; a.log_pS = log_pS; a.crs = const_row_stride; a.prs = param_row_stride;
+  a.dmc = dMC; a.ddl = dDL; a.debar = dEbar; a.de = dE; a.dsl1 = dSL1; a.dsl2 = dSL2; a.dleaf = dleaf;
+  a.dpD = dpD; a.dpS = dpS; a.tstride = tangent_dir_stride; a.item_idx = item_idx; a.leaf_state = leaf_state;
+  a.tb = tour_tables; a.tb2 = pair_tables; a.n_iters = n_iters; a.S = S;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int n_items = C * (D / 2);
+  Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), par_ptr, par_idx,
+         row_split_ptr, C, max_polls, n_items};
+  flow_init_kernel<<<(n_items + 255) / 256 < 65535 ? (n_items + 255) / 256 : 65535, 256, 0, st>>>(f, dep0, ready0,
+                                                                                                   n_ready0);
+  if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
+  const size_t smem = (size_t)(13 * ntv + 128) * sizeof(float);
+  int dev = 0, n_sm = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KB_ERR_LAUNCH;
+#define KB_FT_CASE(V)                                                                                        \
+  case V:                                                                                                    \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)flow_tangent2_kernel<V>,                      \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))   \
+      return KB_ERR_LAUNCH;                                                                                  \
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flow_tangent2_kernel<V>, nt, smem) !=         \
+            cudaSuccess || per_sm < 1)                                                                       \
+      return KB_ERR_LAUNCH;                                                                                  \
+    flow_tangent2_kernel<V><<<(n_items < n_sm * per_sm ? n_items : n_sm * per_sm), nt, smem, st>>>(a, f);    \
+    break;
+  switch (vf) {
+    KB_FT_CASE(2) KB_FT_CASE(4) KB_FT_CASE(8)
+    default: return KB_ERR_SIZE;
+  }
+#undef KB_FT_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }

@@ -215,7 +215,27 @@ def jvp_batch(static, theta, V, saved, *, self_iters=None, e_tol=None, return_fu
     leaf_state = i32(wl["leaf_state_index"])
     item_idx = i64(static.rate_item_idx)
     rows_ptr, sp_ptr = plan.rows.data_ptr(), plan.split_ptr.data_ptr()
-    for L in range(plan.n_levels):
+    if getattr(static, "_flow", True) and getattr(static, "_tangent_pairs", True) and D % 2 == 0:
+        n_items = C * (D // 2)
+        queue = torch.empty((n_items,), device=dev, dtype=torch.int32)
+        remaining = torch.empty((n_items,), device=dev, dtype=torch.int32)
+        counters = torch.zeros((3,), device=dev, dtype=torch.int32)
+        engine._launch(static, "kb_flow_tangent", 0, C, plan.row_split_ptr.data_ptr(), plan.sl_r.data_ptr(),
+                       plan.sr_r.data_ptr(), plan.lsp_r.data_ptr(), plan.dep0.data_ptr(), plan.ready0.data_ptr(),
+                       int(plan.ready0.numel()), plan.par_ptr.data_ptr(), plan.par_idx.data_ptr(), queue.data_ptr(),
+                       remaining.data_ptr(), counters.data_ptr(), engine.FLOW_MAX_POLLS, Pi.data_ptr(),
+                       Pibar.data_ptr(), dts.data_ptr(), dPi.data_ptr(), dPibar.data_ptr(), C * S, D,
+                       k["mc"].data_ptr(), k["dl"].data_ptr(), k["ebar"].data_ptr(), k["e"].data_ptr(),
+                       k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(),
+                       prs, 0, dmc.data_ptr(), dDL.data_ptr(), dEbar.data_ptr(), dE.data_ptr(), dSL1.data_ptr(),
+                       dSL2.data_ptr(), dpS.data_ptr(), dpD.data_ptr(), dpS.data_ptr(), S, item_idx.data_ptr(),
+                       leaf_state.data_ptr(), tt.tour.data_ptr(), tt.tour_pair.data_ptr(), n_it, S, st)
+        if int(counters[2].item()) != 0:
+            raise RuntimeError("kb_flow_tangent: a dataflow wait gave up (dependency counts inconsistent)")
+        L_range = ()
+    else:
+        L_range = range(plan.n_levels)
+    for L in L_range:
         a, b = plan.level_ptr[L], plan.level_ptr[L + 1]
         if b == a:
             continue
