@@ -539,10 +539,6 @@ __device__ __forceinline__ const float& lds_at(const char* base, unsigned off) {
 }
 __device__ __forceinline__ float& sts_at(char* base, unsigned off) { return *reinterpret_cast<float*>(base + off); }
 
-__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gsrc) : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
@@ -608,6 +604,29 @@ struct Fwd4Args {
   long long k4_rows;    // row stride of k4 in float4 (0: one shared item row)
 };
 
+__device__ __forceinline__ void cp_async16_cg(void* smem_dst, const void* gsrc) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+
+// Starts copying one row of S floats at src (4-byte aligned) into the shared slot B (16-byte
+// aligned, >= NTV + 4 floats) and returns the row's view P (P[s] = src[s]): the 16-byte aligned
+// body goes by asynchronous L2 copies (cp.async.cg: no L1, so rows written earlier in the same
+// launch are read correctly), the at most 3 + 3 unaligned end floats by loads; columns S..NTV-1
+// of the view are set to -inf when pad_neg_inf.  The caller commits, waits and syncs before use.
+__device__ __forceinline__ const float* stage_row_cg(float* B, const float* src, int S, int NTV, bool pad_neg_inf) {
+  const int a = (int)(((16u - ((unsigned)(uintptr_t)src & 15u)) & 15u) >> 2);  // floats before a 16-B boundary
+  float* P = B + ((4 - a) & 3);                                                 // P + a is 16-B aligned
+  const int nb = S > a ? (S - a) >> 2 : 0;
+  for (int j = threadIdx.x; j < nb; j += blockDim.x) cp_async16_cg(P + a + 4 * j, src + a + 4 * j);
+  const int head = a < S ? a : S;
+  for (int s = threadIdx.x; s < head; s += blockDim.x) P[s] = __ldcg(src + s);
+  for (int s = head + 4 * nb + threadIdx.x; s < S; s += blockDim.x) P[s] = __ldcg(src + s);
+  if (pad_neg_inf)
+    for (int s = S + threadIdx.x; s < NTV; s += blockDim.x) P[s] = neg_inf();
+  return P;
+}
+
 // Loads of rows that other CTAs of the SAME launch produce (the dataflow schedule) bypass L1:
 // L1 is not coherent across SMs, and a row's first and last cache lines are shared with its
 // neighbours.  Level launches keep the cached / asynchronous paths.
@@ -630,7 +649,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
   const int NT = blockDim.x;
   const int NTV = NT * VF;
   const int TB = 2 * NTV;  // floats per tour buffer
-  float* red = sm + 2 * TB;
+  float* red = sm + 8 * (NTV + 4);  // after the split staging slots (the tour buffers alias them)
   char* T0 = reinterpret_cast<char*>(sm);
   char* T1 = reinterpret_cast<char*>(sm + TB);
   const int tid = threadIdx.x;
@@ -651,94 +670,59 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
       x[k] = s < S ? leaf_seed(c, cb, item, leaf, s) : neg_inf();
     }
   } else {
-    // staging pairs (Pl, Pr) for split parity 0 / 1; padded columns read -inf
+    // Staging: per split the four child rows (Pi_l, Pi_r, Pibar_l, Pibar_r), double-buffered by
+    // split parity, each row a view at a 16-byte aligned position of a slot of NTV + 4 floats.
     float* stg = sm;
+    const int RS = NTV + 4;
+    unsigned ccol[VF];
+    float m[VF], acc[VF], kD[VF], kS[VF];
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
       const int s = tid + k * NT;
-      if (s >= S) {
-        stg[s] = neg_inf();
-        stg[NTV + s] = neg_inf();
-        stg[2 * NTV + s] = neg_inf();
-        stg[3 * NTV + s] = neg_inf();
-      }
-    }
-    unsigned ccol[VF];
-    float m[VF], acc[VF];
-#pragma unroll
-    for (int k = 0; k < VF; ++k) {
-      ccol[k] = __ldg(tb + tid + k * NT);
+      ccol[k] = __ldg(tb + s);
       m[k] = neg_inf();
       acc[k] = 0.f;
+      kD[k] = s < S ? __ldg(c.log_pD + pb + s) : 0.f;
+      kS[k] = s < S ? __ldg(c.log_pS + pb + s) : 0.f;
     }
-    if (!DF) {  // prefetch split i0
-      const float* pil = a.Pi_src + (size_t)a.sp.sl[i0] * S;
-      const float* pir = a.Pi_src + (size_t)a.sp.sr[i0] * S;
-#pragma unroll
-      for (int k = 0; k < VF; ++k) {
-        const int s = tid + k * NT;
-        if (s < S) {
-          cp_async4(stg + s, pil + s);
-          cp_async4(stg + NTV + s, pir + s);
-        }
-      }
+    const float *cPl, *cPr, *cBl, *cBr;
+    {
+      const long long l = a.sp.sl[i0], r = a.sp.sr[i0];
+      cPl = stage_row_cg(stg, a.Pi_src + (size_t)l * S, S, NTV, true);
+      cPr = stage_row_cg(stg + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
+      cBl = stage_row_cg(stg + 2 * RS, a.Pibar_src + (size_t)l * S, S, NTV, false);
+      cBr = stage_row_cg(stg + 3 * RS, a.Pibar_src + (size_t)r * S, S, NTV, false);
       cp_async_commit();
     }
     for (long long i = i0; i < i1; ++i) {
-      const int par = DF ? 0 : (int)((i - i0) & 1);
-      float* Pl = stg + par * 2 * NTV;
-      float* Pr = Pl + NTV;
-      if (DF) {
-        __syncthreads();  // the previous split's readers are done
-        const float* pil = a.Pi_src + (size_t)a.sp.sl[i] * S;
-        const float* pir = a.Pi_src + (size_t)a.sp.sr[i] * S;
-#pragma unroll
-        for (int k = 0; k < VF; ++k) {
-          const int s = tid + k * NT;
-          if (s < S) {
-            Pl[s] = __ldcg(pil + s);
-            Pr[s] = __ldcg(pir + s);
-          }
-        }
-      } else {
-        cp_async_wait_all();
-      }
-      __syncthreads();
-      if (!DF && i + 1 < i1) {
-        float* nl = stg + (par ^ 1) * 2 * NTV;
-        const float* pil = a.Pi_src + (size_t)a.sp.sl[i + 1] * S;
-        const float* pir = a.Pi_src + (size_t)a.sp.sr[i + 1] * S;
-#pragma unroll
-        for (int k = 0; k < VF; ++k) {
-          const int s = tid + k * NT;
-          if (s < S) {
-            cp_async4(nl + s, pil + s);
-            cp_async4(nl + NTV + s, pir + s);
-          }
-        }
+      const int par = (int)((i - i0) & 1);
+      cp_async_wait_all();
+      __syncthreads();  // split i staged; everyone is done with split i-1's slots
+      const float *nPl = nullptr, *nPr = nullptr, *nBl = nullptr, *nBr = nullptr;
+      if (i + 1 < i1) {
+        float* nb = stg + (par ^ 1) * 4 * RS;
+        const long long l = a.sp.sl[i + 1], r = a.sp.sr[i + 1];
+        nPl = stage_row_cg(nb, a.Pi_src + (size_t)l * S, S, NTV, true);
+        nPr = stage_row_cg(nb + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
+        nBl = stage_row_cg(nb + 2 * RS, a.Pibar_src + (size_t)l * S, S, NTV, false);
+        nBr = stage_row_cg(nb + 3 * RS, a.Pibar_src + (size_t)r * S, S, NTV, false);
         cp_async_commit();
       }
-      const long long l = a.sp.sl[i], r = a.sp.sr[i];
-      const float* pbl = a.Pibar_src + (size_t)l * S;
-      const float* pbr = a.Pibar_src + (size_t)r * S;
       const float lsp = a.sp.lsp[i];
 #pragma unroll
       for (int k = 0; k < VF; ++k) {
         const int s = tid + k * NT;
         if (s < S) {
-          const float ld = __ldg(c.log_pD + pb + s);
-          const float ls = __ldg(c.log_pS + pb + s);
-          const float vbr = ld_row<DF>(pbr + s), vbl = ld_row<DF>(pbl + s);
           const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
-          const float pl = Pl[s], pr = Pr[s];
+          const float pl = cPl[s], pr = cPr[s];
           // left-to-right sums, as the reference forms the terms (dts_fused.py:54-60): at log
           // magnitudes ~1e2 a different association moves the terms by an ulp (~1e-5)
-          const float lss = lsp + ls;
-          const float v0 = lsp + ld + pl + pr;
-          const float v1 = lsp + pl + vbr;
-          const float v2 = lsp + pr + vbl;
-          const float v3 = lss + Pl[ca] + Pr[cbb];
-          const float v4 = lss + Pr[ca] + Pl[cbb];
+          const float lss = lsp + kS[k];
+          const float v0 = lsp + kD[k] + pl + pr;
+          const float v1 = lsp + pl + cBr[s];
+          const float v2 = lsp + pr + cBl[s];
+          const float v3 = lss + cPl[ca] + cPr[cbb];
+          const float v4 = lss + cPr[ca] + cPl[cbb];
           const float mx = fmaxf(fmaxf(fmaxf(m[k], v0), fmaxf(v1, v2)), fmaxf(v3, v4));
           const float ms = safe_max(mx);
           acc[k] = fmaf(acc[k], ex2(m[k] - ms),
@@ -746,6 +730,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
           m[k] = mx;
         }
       }
+      cPl = nPl; cPr = nPr; cBl = nBl; cBr = nBr;
     }
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
@@ -760,10 +745,9 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
   const float Rd = safe_max(block_max(m0, red));  // scale of the initial row; syncs (staging done)
 
   // ---- linear-space iterations (see level_forward_kernel) ----
-  // per-column constants stay in L1 (shared by every row of the SM): (kA, kB) and (kC1, kC2) pairs
-  const float2* __restrict__ kab = reinterpret_cast<const float2*>(args.k4 + (size_t)(item * args.k4_rows));
+  const float4* __restrict__ k4 = args.k4 + (size_t)(item * args.k4_rows);
   unsigned ce[VF], tr[VF];
-  float z[VF], td[VF];
+  float z[VF], td[VF], kA[VF], kB[VF], kC1[VF], kC2[VF];
   float zmax_l = 0.f, zsum_l = 0.f;
 #pragma unroll
   for (int k = 0; k < VF; ++k) {
@@ -771,6 +755,8 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     const bool real = s < S;
     ce[k] = __ldg(tb + NTV + s);
     tr[k] = __ldg(tb + 2 * NTV + s);
+    const float4 kk = __ldg(k4 + s);  // zero on padded columns
+    kA[k] = kk.x; kB[k] = kk.y; kC1[k] = kk.z; kC2[k] = kk.w;
     z[k] = real ? ex2(x[k] - Rd) : 0.f;
     td[k] = is_leaf ? (s == leaf ? ex2(leafv - Rd) : 0.f) : z[k];
     sts_at(T0, tr[k] & 0xFFFFu) = z[k];
@@ -791,10 +777,8 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     }
     float part[VF];  // speciation terms z[c1] 2^sl1 + z[c2] 2^sl2, gathered before the scan
 #pragma unroll
-    for (int k = 0; k < VF; ++k) {
-      const float2 kc = __ldg(kab + 2 * (tid + k * NT) + 1);
-      part[k] = fmaf(lds_at(Tc, ce[k] & 0xFFFFu), kc.x, lds_at(Tc, ce[k] >> 16) * kc.y);
-    }
+    for (int k = 0; k < VF; ++k)
+      part[k] = fmaf(lds_at(Tc, ce[k] & 0xFFFFu), kC1[k], lds_at(Tc, ce[k] >> 16) * kC2[k]);
     float zmax = zmax_l, zsum = zsum_l;
     tour_scan_sw<VF>(reinterpret_cast<float*>(Tc), red, zmax, zsum);
     const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
@@ -806,10 +790,9 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     const bool resid = (it == last) && (a.residual != nullptr);
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
-      const float2 kk = __ldg(kab + 2 * (tid + k * NT));
       const float path = lds_at(Tc, tr[k] & 0xFFFFu) + z[k];
       const float D = fmaxf(zsum - path, 0.f);
-      const float lin = fmaf(D, kk.y, fmaf(z[k], kk.x, part[k]));
+      const float lin = fmaf(D, kB[k], fmaf(z[k], kA[k], part[k]));
       const float zn = fmaf(lin, inv, td[k] * fd);
       mincode = min(mincode, (unsigned)__float_as_int(zn) - 1u);
       if (resid && zn > 0.f && z[k] > 0.f) dres = fmaxf(dres, fabsf(lg2(zn) - lg2(z[k] * inv)));
@@ -917,7 +900,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
 }
 
 template <int VF>
-__global__ void __launch_bounds__(512, 2) level_forward_tour_kernel(Fwd4Args args) {
+__global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args args) {
   extern __shared__ __align__(16) float sm[];
   const int b = blockIdx.x;
   forward_tour_row<VF, false>(args, args.f.sp.rows[b], args.f.sp.split_ptr[b], args.f.sp.split_ptr[b + 1], sm);
@@ -997,7 +980,7 @@ __device__ __forceinline__ void flow_finish_row(const Flow& f, int row) {
 }
 
 template <int VF>
-__global__ void __launch_bounds__(512, 2) flow_forward_kernel(Fwd4Args args, Flow f) {
+__global__ void __launch_bounds__(512, 1) flow_forward_kernel(Fwd4Args args, Flow f) {
   extern __shared__ __align__(16) float sm[];
   __shared__ int slot;
   for (;;) {
@@ -2184,7 +2167,7 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
     a4.tb = tour_tables;
     a4.k4 = reinterpret_cast<const float4*>(tour_consts);
     a4.k4_rows = const_row_stride == 0 ? 0 : ntv4;
-    const size_t smem4 = (size_t)(4 * ntv4 + 96) * sizeof(float);
+    const size_t smem4 = (size_t)(8 * (ntv4 + 4) + 96) * sizeof(float);
 #define KB_LF4_CASE(V)                                                                                        \
   case V:                                                                                                     \
     if (smem4 > 48 * 1024 && cudaFuncSetAttribute((const void*)level_forward_tour_kernel<V>,                 \
@@ -2386,7 +2369,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
          row_split_ptr, C, max_polls, C};
   flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
-  const size_t smem = (size_t)(4 * ntv + 96) * sizeof(float);
+  const size_t smem = (size_t)(8 * (ntv + 4) + 96) * sizeof(float);
   int dev = 0, n_sm = 0, per_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
