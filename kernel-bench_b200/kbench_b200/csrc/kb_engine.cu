@@ -1593,6 +1593,70 @@ __global__ void __launch_bounds__(512, 1) flow_tangent2_kernel(TanArgs a, Flow f
 // backward
 // ------------------------------------------------------------------------------------------
 
+// Exclusive scan, in place, of buf[0 .. blockDim.x*CH) float2 entries (two independent sums),
+// thread t owning the consecutive entries [t*CH, (t+1)*CH); fused with the block sums of sa, sb
+// (returned to every thread).  Returns the two totals in ta, tb.  red >= 128 floats.  The caller
+// syncs before; two barriers inside, the second on exit.
+template <int CH>
+__device__ __forceinline__ void block_scan_pair_ch(float2* buf, float* red, float& sa, float& sb, float& ta,
+                                                   float& tb) {
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = (blockDim.x + 31) >> 5;
+  float2* base = buf + t * CH;
+  float2 v[CH];
+#pragma unroll
+  for (int j = 0; j < CH; ++j) v[j] = base[j];
+  float la = 0.f, lb = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    la += v[j].x;
+    lb += v[j].y;
+  }
+  float ia = la, ib = lb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, ia, o);
+    const float yb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ya;
+      ib += yb;
+    }
+  }
+  sa = warp_sum(sa);
+  sb = warp_sum(sb);
+  if (lane == 31) { red[wid] = ia; red[32 + wid] = ib; }
+  if (lane == 0) { red[64 + wid] = sa; red[96 + wid] = sb; }
+  __syncthreads();
+  float xa = lane < nw ? red[lane] : 0.f;
+  float xb = lane < nw ? red[32 + lane] : 0.f;
+  const float bsa = lane < nw ? red[64 + lane] : 0.f;
+  const float bsb = lane < nw ? red[96 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, xa, o);
+    const float yb = __shfl_up_sync(0xffffffffu, xb, o);
+    if (lane >= o) {
+      xa += ya;
+      xb += yb;
+    }
+  }
+  sa = warp_sum(bsa);
+  sb = warp_sum(bsb);
+  ta = __shfl_sync(0xffffffffu, xa, nw - 1);
+  tb = __shfl_sync(0xffffffffu, xb, nw - 1);
+  const float pa = __shfl_up_sync(0xffffffffu, xa, 1);
+  const float pb = __shfl_up_sync(0xffffffffu, xb, 1);
+  float ra = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : pa, wid) + ia - la;
+  float rb = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : pb, wid) + ib - lb;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const float2 x = v[j];
+    base[j] = make_float2(ra, rb);
+    ra += x.x;
+    rb += x.y;
+  }
+  __syncthreads();
+}
+
 struct BwdArgs {
   LevelConsts c;           // c.packed: padded [4, NTV] tables (invalid child/parent -> zero column NTV-1)
   SplitCSR sp;
@@ -1626,10 +1690,13 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a, Flow
   const int NT = blockDim.x;
   const int NTV = NT * VPT;
   float* P = sm;               // Pi row (log; -inf on padding), later speciation cotangents
-  float* T = sm + NTV;         // Neumann term / tour (with U) / staged child rows
-  float* U = sm + 2 * NTV;     // preorder scan buffer
-  float* ACC = sm + 3 * NTV;   // G_N rows of NTV fp32 column sums (this CTA)
-  float* red = ACC + G_N * NTV;
+  float* T = sm + NTV;         // Neumann term / tour (with U) / speciation cotangents
+  float* U = sm + 2 * NTV;     // preorder scan buffer (2 NTV: float2 pairs in the split phase)
+  float2* U2 = reinterpret_cast<float2*>(U);
+  float* ACC = sm + 4 * NTV;   // G_N rows of NTV fp32 column sums (this CTA)
+  float* SLb = ACC + G_N * NTV;  // staged child Pi rows of the current split (NTV + 4 each)
+  float* SRb = SLb + NTV + 4;
+  float* red = SRb + NTV + 4;
   unsigned cc[VPT], tr[VPT], pk[VPT], pa[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -1856,10 +1923,18 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a, Flow
     }
 
     // ---- splits: cotangents of the split reduction and the Pibar VJP trees ----
+    // Per split: the split's Pi cotangents (5 terms) and Pibar cotangents of both children, then
+    // both Pibar VJP trees at once (one scan of (left, right) pairs over the preorder numbering,
+    // fused with the side-activity sums), and one atomic add per child element.  The next split's
+    // child rows are fetched asynchronously while the current split's trees are scanned.
     if (has_splits) {
       float pip[VPT];
 #pragma unroll
       for (int k = 0; k < VPT; ++k) pip[k] = P[threadIdx.x + k * NT];
+      const float *cSL, *cSR;
+      cSL = stage_row_cg(SLb, a.Pi + (size_t)a.sp.sl[i0] * S, S, NTV, true);
+      cSR = stage_row_cg(SRb, a.Pi + (size_t)a.sp.sr[i0] * S, S, NTV, true);
+      cp_async_commit();
       for (long long i = i0; i < i1; ++i) {
         const long long l = a.sp.sl[i], r = a.sp.sr[i];
         const float lsp = a.sp.lsp[i];
@@ -1869,108 +1944,87 @@ __global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a, Flow
         const float* pbr = a.Pibar + (size_t)r * S;
         const float rml = a.row_max[l], rmr = a.row_max[r];
         const size_t mcl = (size_t)(c.item_idx[l] * c.crs), mcr = (size_t)(c.item_idx[r] * c.crs);
-        __syncthreads();
+        cp_async_wait_all();
+        __syncthreads();  // split i staged; the previous split's readers of P, T, U2 are done
+        float cl[VPT], cr[VPT];
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
           const int s = threadIdx.x + k * NT;
-          T[s] = s < S ? pil[s] : neg_inf();
-          U[s] = s < S ? pir[s] : neg_inf();
-        }
-        __syncthreads();
-        float cl[VPT], cr[VPT], v4r[VPT], udl[VPT], udr[VPT];
-        float sabs_l = 0.f, sabs_r = 0.f;
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          const int s = threadIdx.x + k * NT;
-          cl[k] = cr[k] = v4r[k] = udl[k] = udr[k] = 0.f;
-          float v3 = 0.f;
+          cl[k] = cr[k] = 0.f;
+          float v3 = 0.f, v4 = 0.f, udl = 0.f, udr = 0.f;
           if (s < S) {
-            const float pl = T[s], pr = U[s];
+            const float pl = cSL[s], pr = cSR[s];
             const float ld = c.log_pD[pb + s];
             const float ls = c.log_pS[pb + s];
             const unsigned ca = lo16(cc[k]), cbb = hi16(cc[k]);
             const float d0 = ld + pl + pr;
             const float d1 = pl + pbr[s];
             const float d2 = pr + pbl[s];
-            const float d3 = ls + T[ca] + U[cbb];
-            const float d4 = ls + U[ca] + T[cbb];
+            const float d3 = ls + cSL[ca] + cSR[cbb];
+            const float d4 = ls + cSR[ca] + cSL[cbb];
             const float ppar = pip[k];
             const bool pv = !is_neg_inf(ppar);
             const float vd0 = v[k] * (pv ? ex2(lsp + d0 - ppar) : 0.f);
             const float vd1 = v[k] * (pv ? ex2(lsp + d1 - ppar) : 0.f);
             const float vd2 = v[k] * (pv ? ex2(lsp + d2 - ppar) : 0.f);
             v3 = v[k] * (pv ? ex2(lsp + d3 - ppar) : 0.f);
-            v4r[k] = v[k] * (pv ? ex2(lsp + d4 - ppar) : 0.f);
+            v4 = v[k] * (pv ? ex2(lsp + d4 - ppar) : 0.f);
             ACC[G_PD * NTV + s] += vd0;
-            ACC[G_PS * NTV + s] += v3 + v4r[k];
+            ACC[G_PS * NTV + s] += v3 + v4;
             ACC[G_MT * NTV + s] += vd1 + vd2;
             cl[k] = vd0 + vd1;
             cr[k] = vd0 + vd2;
             const float bl = pbl[s], br = pbr[s];
-            udl[k] = is_neg_inf(bl) ? 0.f : vd2 * ex2(rml + c.mc[mcl + s] - bl);
-            udr[k] = is_neg_inf(br) ? 0.f : vd1 * ex2(rmr + c.mc[mcr + s] - br);
-            sabs_l += fabsf(udl[k]);
-            sabs_r += fabsf(udr[k]);
+            udl = is_neg_inf(bl) ? 0.f : vd2 * ex2(rml + c.mc[mcl + s] - bl);
+            udr = is_neg_inf(br) ? 0.f : vd1 * ex2(rmr + c.mc[mcr + s] - br);
           }
           P[s] = v3;  // P no longer holds Pi (pip registers do)
+          T[s] = v4;
+          U2[lo16(pk[k])] = make_float2(udl, udr);
         }
-        bool side_l = true, side_r = true;
-        if (a.side_thr_enabled) {
-          sabs_l = block_sum(sabs_l, red);
-          sabs_r = block_sum(sabs_r, red);
-          side_l = sabs_l > a.side_thr;
-          side_r = sabs_r > a.side_thr;
+        __syncthreads();  // P, T, U2 complete; the staged rows are no longer read
+        if (i + 1 < i1) {
+          cSL = stage_row_cg(SLb, a.Pi + (size_t)a.sp.sl[i + 1] * S, S, NTV, true);
+          cSR = stage_row_cg(SRb, a.Pi + (size_t)a.sp.sr[i + 1] * S, S, NTV, true);
+          cp_async_commit();
         }
-        __syncthreads();  // staged child rows no longer read
+        float sabs_l = 0.f, sabs_r = 0.f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          T[threadIdx.x + k * NT] = v4r[k];
-          U[lo16(pk[k])] = udl[k];
+        for (int k = 0; k < VPT; ++k) {  // the scatter wrote each column's pair at pre(s)
+          const float2 u = U2[lo16(pk[k])];
+          sabs_l += fabsf(u.x);
+          sabs_r += fabsf(u.y);
         }
-        __syncthreads();
+        float Al, Ar;
+        block_scan_pair_ch<VPT>(U2, red, sabs_l, sabs_r, Al, Ar);
+        const bool side_l = !a.side_thr_enabled || sabs_l > a.side_thr;
+        const bool side_r = !a.side_thr_enabled || sabs_r > a.side_thr;
         float* rl = a.acc + (size_t)l * S;
         float* rr = a.acc + (size_t)r * S;
         const float rmls = safe_max(rml), rmrs = safe_max(rmr);
-        {  // left side
-          const float A = block_exclusive_scan_ch<VPT>(U, red);
 #pragma unroll
-          for (int k = 0; k < VPT; ++k) {
-            const int x = threadIdx.x + k * NT;
-            if (x < S) {
-              const unsigned par = lo16(pa[k]);
-              const float st = hi16(pa[k]) ? P[par] : T[par];
-              float tl = 0.f;
-              if (side_l) {
-                float w = pil[x];
-                if (c.use_col) w += c.col[x];
-                tl = ex2(w - rmls) * (A - (U[hi16(pk[k])] - U[lo16(pk[k])]));
-              }
-              ACC[G_COL * NTV + x] += tl;
-              atomicAdd(rl + x, cl[k] + st + tl);
+        for (int k = 0; k < VPT; ++k) {
+          const int x = threadIdx.x + k * NT;
+          if (x < S) {
+            const unsigned par = lo16(pa[k]);
+            const bool first = hi16(pa[k]) != 0;
+            const float stl = first ? P[par] : T[par];
+            const float str = first ? T[par] : P[par];
+            const float2 ue = U2[hi16(pk[k])], ub = U2[lo16(pk[k])];
+            float tl = 0.f, trr = 0.f;
+            if (side_l) {
+              float w = pil[x];
+              if (c.use_col) w += c.col[x];
+              tl = ex2(w - rmls) * (Al - (ue.x - ub.x));
             }
-          }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = udr[k];
-        __syncthreads();
-        {  // right side
-          const float A = block_exclusive_scan_ch<VPT>(U, red);
-#pragma unroll
-          for (int k = 0; k < VPT; ++k) {
-            const int x = threadIdx.x + k * NT;
-            if (x < S) {
-              const unsigned par = lo16(pa[k]);
-              const float st = hi16(pa[k]) ? T[par] : P[par];
-              float tr_ = 0.f;
-              if (side_r) {
-                float w = pir[x];
-                if (c.use_col) w += c.col[x];
-                tr_ = ex2(w - rmrs) * (A - (U[hi16(pk[k])] - U[lo16(pk[k])]));
-              }
-              ACC[G_COL * NTV + x] += tr_;
-              atomicAdd(rr + x, cr[k] + st + tr_);
+            if (side_r) {
+              float w = pir[x];
+              if (c.use_col) w += c.col[x];
+              trr = ex2(w - rmrs) * (Ar - (ue.y - ub.y));
             }
+            ACC[G_COL * NTV + x] += tl + trr;
+            atomicAdd(rl + x, cl[k] + stl + tl);
+            atomicAdd(rr + x, cr[k] + str + trr);
           }
         }
       }
@@ -2226,7 +2280,7 @@ extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, in
   int bd;
   const int vpt = engine_width(S, bd);
   const int ntv = bd * vpt;
-  const size_t smem = (size_t)((3 + G_N) * ntv + 128) * sizeof(float);
+  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = n_rows < n_slots ? n_rows : n_slots;
   cudaStream_t st = (cudaStream_t)stream;
   const Flow nof{};
@@ -2426,7 +2480,7 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   int bd;
   const int vpt = engine_width(S, bd);
   const int ntv = bd * vpt;
-  const size_t smem = (size_t)((3 + G_N) * ntv + 128) * sizeof(float);
+  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = C < n_slots ? C : n_slots;  // persistent CTAs, one fp64 slot each
 #define KB_FB_CASE(V)                                                                                      \
   case V:                                                                                                  \
