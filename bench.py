@@ -156,6 +156,19 @@ def algorithmic_bytes(plan, S):
     return fwd, bwd
 
 
+# DRAM bytes per row of the dataflow kernels at S = 4095, from one ncu capture on the config-3
+# species tree with a 12,709-row family (profiles/flow_kernels_dram_traffic.md); rows are
+# independent units, so a full-family launch moves ~C times these.
+TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782593280 + 542440704) / 12709,
+                               "kb_flow_backward": (1968742400 + 787051264) / 12709}
+
+
+def launch_traffic(name, C, S):
+    """Measured-and-scaled DRAM bytes of one launch of ``name`` (None where not measured)."""
+    per_row = TRAFFIC_BYTES_PER_ROW_S4095.get(name)
+    return None if per_row is None or S != 4095 else round(per_row * C)
+
+
 def kernel_bytes(name, per, fwd_b, bwd_b):
     """Algorithmic bytes of the launches ``per`` [(level, ms)] of one engine kernel: a level launch
     covers its level, a dataflow launch (kb_flow_*) the whole sweep."""
@@ -623,7 +636,9 @@ def main():
         roofline = {
             "bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
             "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-            "traffic": None,
+            "traffic": launch_traffic(dominant, C, S),
+            "traffic_note": "dram__bytes_read+write per launch, scaled by rows from an ncu capture "
+                            "(profiles/flow_kernels_dram_traffic.md)",
             "algorithmic_bytes_per_launch": alg_bytes / n_launch,
             "avg_launch_ms": k_ms / n_launch,
             "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items() if v > 0},

@@ -280,6 +280,10 @@ int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl,
                      int use_col_weights, const long long* item_idx, const int* leaf_state,
                      const unsigned* packed_padded, int S, void* stream);
 
+/* Number of backward CTAs that are resident at once on this device for S columns (SMs x CTAs
+ * per SM): the slot count to give kb_level_backward / kb_flow_backward (host only). */
+int kb_backward_ctas(int S, int* n_ctas);
+
 /* Fixed-order sum of kb_level_backward's fp64 slots -> out8 [8,S] fp32: the cotangents of
  * log_pD, log_pS, max_coupling, E, Ebar, E_s1, E_s2 and col_log_probs (in that order). */
 int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S, float* out8, void* stream);

@@ -2109,6 +2109,17 @@ int engine_width(int S, int& bd) {
   return v;
 }
 
+// Threads and columns per thread of the backward kernel: the engine's padded width NTV with
+// (where the row allows) 4 columns per thread, so narrow rows leave room for several CTAs per SM.
+int bwd_width(int S, int& bd) {
+  int b0;
+  const int ntv = engine_width(S, b0) * b0;
+  bd = ntv / 4;
+  if (bd < 32) bd = 32;
+  if (bd > 1024) bd = 1024;
+  return ntv / bd;
+}
+
 // Padded width, threads and columns per thread of the forward tour kernel (mirrors
 // kbench_b200/tree.py tour_layout): NTV = smallest power of two > S (>= 64); 0 when NTV > 4096.
 int tour_layout(int S, int& nt, int& vf) {
@@ -2278,7 +2289,7 @@ extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, in
   a.side_thr = side_threshold; a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms;
   a.n_rows = n_rows;
   int bd;
-  const int vpt = engine_width(S, bd);
+  const int vpt = bwd_width(S, bd);
   const int ntv = bd * vpt;
   const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = n_rows < n_slots ? n_rows : n_slots;
@@ -2478,7 +2489,7 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
   int bd;
-  const int vpt = engine_width(S, bd);
+  const int vpt = bwd_width(S, bd);
   const int ntv = bd * vpt;
   const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = C < n_slots ? C : n_slots;  // persistent CTAs, one fp64 slot each
@@ -2554,4 +2565,26 @@ extern "C" int kb_flow_tangent(int C, const long long* row_split_ptr, const long
   }
 #undef KB_FT_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_backward_ctas(int S, int* n_ctas) {
+  if (S <= 0 || S > KB_MAX_S || n_ctas == nullptr) return KB_ERR_ARG;
+  int bd;
+  const int vpt = bwd_width(S, bd);
+  const int ntv = bd * vpt;
+  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
+  int dev = 0, n_sm = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KB_ERR_LAUNCH;
+  const void* fn = vpt == 1 ? (const void*)level_backward_kernel<1, true>
+                 : vpt == 2 ? (const void*)level_backward_kernel<2, true>
+                 : vpt == 4 ? (const void*)level_backward_kernel<4, true>
+                            : (const void*)level_backward_kernel<8, true>;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+    return KB_ERR_LAUNCH;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, bd, smem) != cudaSuccess || per_sm < 1)
+    return KB_ERR_LAUNCH;
+  *n_ctas = n_sm * per_sm;
+  return KB_OK;
 }

@@ -342,8 +342,24 @@ def _flow_scratch(static, C, dev) -> dict:
 def new_grad_slots(static, dev) -> torch.Tensor:
     """Zeroed fp64 per-CTA accumulators ``[n_slots, 8, NTV]`` of the backward's column sums
     (rows: pD, pS, mt, E, Ebar, E_s1, E_s2, col)."""
-    bd, vpt = tree.engine_width(int(static.state_helpers["S"]))
-    return torch.zeros((_sm_count(dev), 8, bd * vpt), device=dev, dtype=torch.float64)
+    S = int(static.state_helpers["S"])
+    bd, vpt = tree.engine_width(S)
+    return torch.zeros((_backward_ctas(S, dev), 8, bd * vpt), device=dev, dtype=torch.float64)
+
+
+_BWD_CTAS: dict = {}
+
+
+def _backward_ctas(S, dev) -> int:
+    """Resident backward CTAs on ``dev`` for S columns (one fp64 slot each)."""
+    import ctypes
+    key = (S, torch.device(dev).index)
+    if key not in _BWD_CTAS:
+        with torch.cuda.device(dev):
+            n = ctypes.c_int(0)
+            _lib.call("kb_backward_ctas", S, ctypes.byref(n))
+            _BWD_CTAS[key] = int(n.value)
+    return _BWD_CTAS[key]
 
 
 def grad_accumulators_from(E, S, acc8) -> glue.GradAccumulators:
