@@ -2131,30 +2131,6 @@ int tour_layout(int S, int& nt, int& vf) {
   return ntv;
 }
 
-// Up to 1024 threads per row (4 columns per thread at S = 4095).
-int vpt_pick_wide(int S, int& bd) {
-  bd = 1024;
-  if (S <= 1024) bd = ((S + 31) / 32) * 32;
-  if (bd < 32) bd = 32;
-  const int v = (S + bd - 1) / bd;
-  if (v <= 1) return 1;
-  if (v <= 2) return 2;
-  if (v <= 4) return 4;
-  return 8;
-}
-
-int vpt_pick(int S, int& bd) {
-  bd = 512;
-  if (S <= 512) bd = ((S + 31) / 32) * 32;
-  if (bd < 32) bd = 32;
-  const int v = (S + bd - 1) / bd;
-  if (v <= 1) return 1;
-  if (v <= 2) return 2;
-  if (v <= 4) return 4;
-  if (v <= 8) return 8;
-  return 16;
-}
-
 LevelConsts make_lc(const float* mc, const float* dl, const float* ebar, const float* e, const float* sl1,
                     const float* sl2, const float* leaf_logp, const float* linA, const float* linB,
                     const float* linC1, const float* linC2, const float* log_pD, const float* log_pS,

@@ -145,7 +145,11 @@ def _sm_count(dev) -> int:
 
 
 def supported(static) -> bool:
-    return bool(static.statewise) and not bool(static.itemwise)
+    """The fused engine's layouts: one shared item row (statewise, not itemwise) and rows of at
+    most 4,095 columns (the tour kernels' 4,096-column padded width); anything else runs on the
+    call-by-call driver of ``glue.py``."""
+    S = int(static.state_helpers["S"])
+    return bool(static.statewise) and not bool(static.itemwise) and tree.tour_layout(S) is not None
 
 
 class _Topo:
