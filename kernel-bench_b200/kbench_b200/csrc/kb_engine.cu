@@ -1683,7 +1683,7 @@ enum { G_PD = 0, G_PS, G_MT, G_E, G_EBAR, G_ES1, G_ES2, G_COL, G_N };
 // DF = the dataflow schedule (one persistent launch; f.par_ptr / par_idx then list each row's
 // distinct CHILD rows, released when the row is done; a row is ready once all its parents ran).
 template <int VPT, bool DF>
-__global__ void __launch_bounds__(1024, 1) level_backward_kernel(BwdArgs a, Flow f) {
+__global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_kernel(BwdArgs a, Flow f) {
   extern __shared__ float sm[];
   const LevelConsts& c = a.c;
   const int S = c.S;
@@ -2110,11 +2110,15 @@ int engine_width(int S, int& bd) {
 }
 
 // Threads and columns per thread of the backward kernel: the engine's padded width NTV with
-// (where the row allows) 4 columns per thread, so narrow rows leave room for several CTAs per SM.
+// (where the row allows) KB_BWD_COLS columns per thread, so narrow rows leave room for several
+// CTAs per SM.
+#ifndef KB_BWD_COLS
+#define KB_BWD_COLS 4
+#endif
 int bwd_width(int S, int& bd) {
   int b0;
   const int ntv = engine_width(S, b0) * b0;
-  bd = ntv / 4;
+  bd = ntv / KB_BWD_COLS;
   if (bd < 32) bd = 32;
   if (bd > 1024) bd = 1024;
   return ntv / bd;
