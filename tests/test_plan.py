@@ -1,0 +1,49 @@
+"""The dataflow dependency arrays of the engine plan (host side, no GPU): simulating the device
+queue on the CPU must release every row exactly once, in an order that respects the splits, for
+the forward (children before parents) and the backward (parents before children)."""
+
+import numpy as np
+import pytest
+
+from kbench_b200 import engine, gen, runtime
+
+
+def _simulate(dep, ready, ptr, idx):
+    dep = dep.copy()
+    order = list(ready)
+    i = 0
+    while i < len(order):
+        r = order[i]
+        i += 1
+        for j in range(ptr[r], ptr[r + 1]):
+            c = idx[j]
+            dep[c] -= 1
+            assert dep[c] >= 0
+            if dep[c] == 0:
+                order.append(c)
+    return np.asarray(order), dep
+
+
+@pytest.mark.parametrize("config,seed", [(1, 1000), (2, 2000)])
+def test_dataflow_arrays_release_every_row_in_dependency_order(config, seed):
+    cap = gen.generate(config, seed=seed)
+    static = runtime.make_static(cap, "cpu")
+    plan = engine.build_plan(static)
+    C = int(cap["meta"]["C"])
+    rsp = plan.row_split_ptr.numpy()
+    sl, sr = plan.sl_r.numpy(), plan.sr_r.numpy()
+    fwd, dep = _simulate(plan.dep0.numpy(), plan.ready0.numpy(), plan.par_ptr.numpy(), plan.par_idx.numpy())
+    assert len(fwd) == C and (dep == 0).all() and len(set(fwd.tolist())) == C
+    pos = np.empty(C, np.int64)
+    pos[fwd] = np.arange(C)
+    for p in range(C):
+        for n in range(rsp[p], rsp[p + 1]):
+            assert pos[sl[n]] < pos[p] and pos[sr[n]] < pos[p]
+    bwd, dep = _simulate(plan.dep_b.numpy(), plan.ready_b.numpy(), plan.child_ptr.numpy(), plan.child_idx.numpy())
+    assert len(bwd) == C and (dep == 0).all()
+    pos[bwd] = np.arange(C)
+    for p in range(C):
+        for n in range(rsp[p], rsp[p + 1]):
+            assert pos[p] < pos[sl[n]] and pos[p] < pos[sr[n]]
+    roots = cap["static"]["wave_layout"]["root_row_ids"].numpy()
+    assert set(plan.ready_b.numpy().tolist()) == set(roots.tolist())
