@@ -78,6 +78,39 @@ int kb_e_step_vjp(const float* E, const float* E_new, const float* E_s1, const f
                   float* grad_pS, float* grad_pD, float* grad_pL, float* grad_mc, float* grad_col, int S, int G,
                   int use_col_weights, void* stream);
 
+/* Replaces the E-adjoint solve and the E-step parameter VJP of _implicit_grad.py:373-475 (the
+ * BiCGSTAB of :28-94 with one e_step VJP per matvec) for ONE shared row, in one launch:
+ *   q  = g_E + d/dE[n_fam * log2(1 - mean 2^E)] + VJP_E(E_s1, E_s2, Ebar cotangents),
+ *   solve (I - J_E^T) w = q with the reference's stopping and breakdown rules,
+ *   grad_params [5,S] = cotangents of (log_pS, log_pD, log_pL, max_coupling, col_log_probs) from
+ *   the E step at w with Ebar cotangent g_Ebar (the caller adds the direct accumulators).
+ * work: KB_EADJ_WORK_VECTORS * S floats of device scratch.  status [2] = (0 converged / 1 not,
+ * iterations); rel_out [1] = last relative residual.  All arrays are [S] (row 0). */
+#define KB_EADJ_WORK_VECTORS 17
+int kb_e_adjoint_solve(const float* E, const float* log_pS, const float* log_pD, const float* log_pL,
+                       const float* max_coupling, const float* col_log_probs, const int* node_parent,
+                       const int* node_child1, const int* node_child2, const int* jumps, int K,
+                       const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1, const int* lv_c2,
+                       const float* g_E, const float* g_Ebar, const float* g_E_s1, const float* g_E_s2, double n_fam,
+                       int max_iter, double tol, double breakdown_tol, float* work, float* w_out,
+                       float* grad_params, int* status, float* rel_out, int S, int use_col_weights, void* stream);
+
+/* ---- parameter extraction (kbench/core/parameters/extract_parameters.py) ---------------- */
+
+/* Replaces col_valid_log_normalizer (extract_parameters.py:41-65): norm_out[s] =
+ * -log2(max(1 - mass[s], FLT_MIN)) where 1 - mass[s] > 0, else -inf, mass[s] = sum of
+ * 2^col_log_probs over the first max_ancestor_depth nodes of s's root path (self first, summed in
+ * that order).  One launch; S <= KB_MAX_S. */
+int kb_col_normalizer(const float* col_log_probs, const int* node_parent, int max_ancestor_depth, int S,
+                      float* norm_out, void* stream);
+
+/* VJP of kb_col_normalizer: grad_col_log_probs [S] (overwritten) from the cotangent g_norm [S].
+ * The compact levels (internal nodes, deepest first) give the subtree sums; max_ancestor_depth
+ * must cover every root path (as the static's does). */
+int kb_col_normalizer_vjp(const float* col_log_probs, const int* node_parent, int max_ancestor_depth,
+                          const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1,
+                          const int* lv_c2, const float* g_norm, float* grad_col_log_probs, int S, void* stream);
+
 /* ---- split reduction (kbench/core/kernels/dts_fused.py) ------------------------------- */
 
 /* Replaces compute_dts_forward (dts_fused.py:171-231). out [W,S] must be pre-filled with -inf

@@ -346,6 +346,37 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
     return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
 
 
+DEVICE_E_ADJOINT = True  # one shared E row: the whole solve in one launch (kb_e_adjoint_solve)
+
+
+def _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo):
+    """:func:`e_adjoint_and_theta_vjp` for one shared E row: the right-hand side, the BiCGSTAB
+    solve and the E step's parameter VJP run in ONE kernel (``kb_e_adjoint_solve``); what is left
+    here is the VJP of the parameter extraction, with the same terms as the general path."""
+    from .kernels.e_step import _as_item_state_ad, e_adjoint_solve
+    so = static.solver_options
+    sh = static.state_helpers
+    S = int(sh["S"])
+    wE, gp = e_adjoint_solve(saved["E"], saved["log_pS"], saved["log_pD"], saved["log_pL"],
+                             saved["max_coupling"], saved["col_log_probs"], *topo, g.E, g.Ebar, g.E_s1, g.E_s2,
+                             n_fam=n_fam, max_iter=so.bicgstab_max_iter, tol=so.bicgstab_tol,
+                             breakdown_tol=so.bicgstab_breakdown_tol, use_col_weights=use_col_weights)
+    static._last_e_adjoint = wE
+    theta_req = theta.detach().requires_grad_(True)
+    col_req = col_weights.detach().requires_grad_(True)
+    with torch.enable_grad():
+        pS, pD, pL, mt, clp = extract_parameters_weighted_cols(theta_req, col_req, sh, statewise=static.statewise,
+                                                               itemwise=static.itemwise,
+                                                               uniform_fast=not use_col_weights)
+        loss = ((as_item_param(pS, 1, S) * g.pS).sum() + (as_item_param(pD, 1, S) * g.pD).sum()
+                + (mt * g.mt.reshape(mt.shape)).sum() + (clp * g.col).sum()
+                + (_as_item_state_ad(pS, S, 1) * gp[0:1]).sum() + (_as_item_state_ad(pD, S, 1) * gp[1:2]).sum()
+                + (_as_item_state_ad(pL, S, 1) * gp[2:3]).sum() + (_as_item_state_ad(mt, S, 1) * gp[3:4]).sum()
+                + (clp.contiguous().reshape(-1) * gp[4]).sum())
+        grad_theta, grad_col = torch.autograd.grad(loss, (theta_req, col_req))
+    return grad_theta, grad_col
+
+
 def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col_weights):
     """The accumulated cotangents are kept on ``static._last_grad_acc`` for inspection.
 
@@ -356,6 +387,8 @@ def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col
     static._last_grad_acc = g
     topo = (sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]))
     E_star = saved["E"]
+    if DEVICE_E_ADJOINT and E_star.shape[0] == 1 and E_star.is_cuda:
+        return _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo)
     E_req = E_star.detach().requires_grad_(True)
     with torch.enable_grad():
         E_from_E, Es1_from_E, Es2_from_E, Ebar_from_E = e_step_triton_autograd(
@@ -378,6 +411,7 @@ def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col
 
     wE = bicgstab(AG, q, max_iter=so.bicgstab_max_iter, tol=so.bicgstab_tol,
                   breakdown_tol=so.bicgstab_breakdown_tol).view(shape)
+    static._last_e_adjoint = wE
     theta_req = theta.detach().requires_grad_(True)
     col_req = col_weights.detach().requires_grad_(True)
     with torch.enable_grad():

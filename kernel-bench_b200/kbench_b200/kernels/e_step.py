@@ -121,3 +121,53 @@ def e_fixed_point_triton(E0, log_pS, log_pD, log_pL, max_coupling, col_log_probs
               _lib.stream_handle(E0.device))
     e_fixed_point_triton.last_iters = iters
     return E_out, E_s1, E_s2, Ebar
+
+
+KB_EADJ_WORK_VECTORS = 17  # include/kb_solver.h
+
+
+def e_adjoint_solve(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
+                    node_child2, max_ancestor_depth, g_E, g_Ebar, g_E_s1, g_E_s2, *, n_fam, max_iter=500,
+                    tol=1e-7, breakdown_tol=1e-30, use_col_weights=True):
+    """The E adjoint of ONE shared row (reference ``_implicit_grad.py:373-475``) in one launch:
+    ``q = g_E + d/dE[n_fam log2(1 - mean 2^E)] + VJP(g_E_s1, g_E_s2, g_Ebar)``, BiCGSTAB on
+    ``(I - J_E^T) w = q`` with the stopping and breakdown rules of ``_implicit_grad.py:28-94``,
+    then the E step's parameter cotangents at ``w``.
+
+    Returns ``(w [1,S], grad_params [5,S])`` -- the cotangents of ``(log_pS, log_pD, log_pL,
+    max_coupling, col_log_probs)`` through the E step (the Ebar cotangent ``g_Ebar`` included).
+    Raises ``RuntimeError`` (the reference's message) when the solve does not converge."""
+    max_iter, tol, breakdown_tol = int(max_iter), float(tol), float(breakdown_tol)
+    if max_iter < 1:
+        raise ValueError("max_iter must be at least 1")
+    if tol <= 0.0:
+        raise ValueError("tol must be positive")
+    if breakdown_tol <= 0.0:
+        raise ValueError("breakdown_tol must be positive")
+    require_cuda_f32("e_adjoint_solve", E)
+    S = int(E.shape[-1])
+    if E.numel() != S:
+        raise ValueError("e_adjoint_solve takes one shared row")
+    E = f32(E.reshape(1, S))
+    tt = tree.tables(node_parent, node_child1, node_child2, max_ancestor_depth)
+    pS, pD, pL, mc = (rows_of(t, 1, S) for t in (log_pS, log_pD, log_pL, max_coupling))
+    col = f32(col_log_probs.reshape(-1))
+    gs = [f32(g.reshape(1, S)) for g in (g_E, g_Ebar, g_E_s1, g_E_s2)]
+    dev = E.device
+    work = torch.empty((KB_EADJ_WORK_VECTORS, S), dtype=torch.float32, device=dev)
+    w = torch.empty((1, S), dtype=torch.float32, device=dev)
+    grad_params = torch.empty((5, S), dtype=torch.float32, device=dev)
+    status = torch.zeros((2,), dtype=torch.int32, device=dev)
+    rel = torch.zeros((1,), dtype=torch.float32, device=dev)
+    _lib.call("kb_e_adjoint_solve", E.data_ptr(), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(), mc.data_ptr(),
+              col.data_ptr(), tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
+              tt.jumps.data_ptr(), tt.K, tt.lv_ptr.data_ptr(), tt.n_levels, tt.lv_par.data_ptr(),
+              tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(), *[g.data_ptr() for g in gs], float(n_fam), max_iter,
+              tol, breakdown_tol, work.data_ptr(), w.data_ptr(), grad_params.data_ptr(), status.data_ptr(),
+              rel.data_ptr(), S, int(bool(use_col_weights)), _lib.stream_handle(dev))
+    code, iters = status.tolist()
+    e_adjoint_solve.last_iters = iters
+    if code != 0:
+        raise RuntimeError(f"E-adjoint BiCGSTAB solve failed after {iters} iterations "
+                           f"(relative residual {float(rel.item()):.3e})")
+    return w, grad_params

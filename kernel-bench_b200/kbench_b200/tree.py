@@ -232,6 +232,23 @@ def tables(node_parent, node_child1, node_child2, max_ancestor_depth, *, compact
     return tt
 
 
+def children_from_parent(node_parent):
+    """(node_child1, node_child2) of a binary tree given by its parent array: the smaller and the
+    larger child index of each internal node, ``S`` (no child) for leaves."""
+    par = node_parent.detach().to("cpu", torch.int64)
+    S = int(par.numel())
+    c1 = torch.full((S,), S, dtype=torch.int64)
+    c2 = torch.full((S,), S, dtype=torch.int64)
+    for s in range(S):
+        p = int(par[s])
+        if 0 <= p < S:
+            if int(c1[p]) == S:
+                c1[p] = s
+            else:
+                c2[p] = s
+    return c1.to(node_parent.device), c2.to(node_parent.device)
+
+
 def derive_levels(node_parent, node_child1, node_child2):
     """Compact levels (internal nodes grouped by depth, deepest level first) from the parent
     and child arrays, for callers that did not pass the precomputed ones."""
