@@ -933,11 +933,19 @@ struct Flow {
   int n_items;             // C * groups
 };
 
-// Claims the next queue slot and waits (bounded) until it holds a row.  Returns the row, -1 when
-// every row has been taken, -2 on a timeout (error recorded).  Called by all threads.
-__device__ __forceinline__ int flow_next_row(const Flow& f, int* shared_slot) {
+// Per-CTA state of the dataflow loop (shared memory; thread 0 sets next = -1 before the loop).
+struct FlowSlot {
+  int row;   // the claimed item, broadcast to the CTA
+  int next;  // queue ticket taken ahead by flow_finish_row, -1 = none
+};
+
+// Claims the next queue slot (the ticket taken ahead, if any) and waits (bounded) until it holds
+// a row.  Returns the row, -1 when every row has been taken, -2 on a timeout (error recorded).
+// Called by all threads.
+__device__ __forceinline__ int flow_next_row(const Flow& f, FlowSlot* st) {
   if (threadIdx.x == 0) {
-    const unsigned idx = atomicAdd(f.head, 1u);
+    const unsigned idx = st->next >= 0 ? (unsigned)st->next : atomicAdd(f.head, 1u);
+    st->next = -1;
     int row = -1;
     if (idx < (unsigned)f.n_items) {
       const volatile int* q = f.queue + idx;
@@ -954,40 +962,46 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, int* shared_slot) {
       }
       __threadfence();  // the row's children, written before it was queued, are visible
     }
-    *shared_slot = row;
+    st->row = row;
   }
   __syncthreads();
-  const int row = *shared_slot;
+  const int row = st->row;
   __syncthreads();
   return row;
 }
 
-// After a row's outputs are written by the whole CTA: release the rows that wait on it.
-__device__ __forceinline__ void flow_finish_row(const Flow& f, int row) {
+// After a row's outputs are written by the whole CTA: release the rows that wait on it (one lane
+// of warp 0 per dependent row) while thread 32 takes the CTA's next queue ticket.
+__device__ __forceinline__ void flow_finish_row(const Flow& f, int row, FlowSlot* st) {
   __threadfence();  // every thread's outputs (stores and atomics) are device-visible ...
-  __syncthreads();  // ... before thread 0 releases the dependent rows
-  if (threadIdx.x == 0) {
+  __syncthreads();  // ... before warp 0 releases the dependent rows
+  if (threadIdx.x < 32) {
     const int grp = row / f.C;
     const int r = row - grp * f.C;
-    for (long long j = f.par_ptr[r]; j < f.par_ptr[r + 1]; ++j) {
+    for (long long j = f.par_ptr[r] + threadIdx.x; j < f.par_ptr[r + 1]; j += 32) {
       const int p = grp * f.C + f.par_idx[j];
       if (atomicSub(f.remaining + p, 1) == 1) {
         const unsigned slot = atomicAdd(f.tail, 1u);
         atomicExch(f.queue + slot, p);
       }
     }
+  } else if (threadIdx.x == 32) {
+    const unsigned idx = atomicAdd(f.head, 1u);
+    st->next = idx < (unsigned)f.n_items ? (int)idx : f.n_items;  // >= n_items: nothing left
   }
+  __syncthreads();  // next is visible to thread 0
 }
 
 template <int VF>
 __global__ void __launch_bounds__(512, 1) flow_forward_kernel(Fwd4Args args, Flow f) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ int slot;
+  __shared__ FlowSlot fs;
+  if (threadIdx.x == 0) fs.next = -1;
   for (;;) {
-    const int row = flow_next_row(f, &slot);
+    const int row = flow_next_row(f, &fs);
     if (row < 0) break;
     forward_tour_row<VF, true>(args, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], sm);
-    flow_finish_row(f, row);
+    flow_finish_row(f, row, &fs);
   }
 }
 
@@ -1579,13 +1593,14 @@ __global__ void __launch_bounds__(512, 1) level_tangent2_kernel(TanArgs a) {
 template <int VF>
 __global__ void __launch_bounds__(512, 1) flow_tangent2_kernel(TanArgs a, Flow f) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ int slot;
+  __shared__ FlowSlot fs;
+  if (threadIdx.x == 0) fs.next = -1;
   for (;;) {
-    const int itm = flow_next_row(f, &slot);
+    const int itm = flow_next_row(f, &fs);
     if (itm < 0) break;
     const int pair = itm / f.C, row = itm - pair * f.C;
     tangent_pair_row<VF, true>(a, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], 2 * pair, sm);
-    flow_finish_row(f, itm);
+    flow_finish_row(f, itm, &fs);
   }
 }
 
@@ -1708,13 +1723,14 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
 #pragma unroll
     for (int j = 0; j < G_N; ++j) ACC[j * NTV + s] = 0.f;
   }
-  __shared__ int flow_slot;
+  __shared__ FlowSlot fs;
+  if (threadIdx.x == 0) fs.next = -1;
   int b = blockIdx.x;
   int since_flush = 0;  // DF: rows accumulated in the fp32 shared sums since the last fp64 flush
   for (;;) {
     long long row, i0, i1;
     if (DF) {
-      const int r = flow_next_row(f, &flow_slot);
+      const int r = flow_next_row(f, &fs);
       if (r < 0) break;
       row = r;
       i0 = f.row_split_ptr[r];
@@ -1746,7 +1762,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     amax = block_max(amax, red);
     const bool active = a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold);
     if (!active) {
-      if (DF) flow_finish_row(f, (int)row);
+      if (DF) flow_finish_row(f, (int)row, &fs);
       continue;
     }
 
@@ -2030,7 +2046,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       }
     }
     if (DF) {
-      flow_finish_row(f, (int)row);
+      flow_finish_row(f, (int)row, &fs);
       // A persistent CTA runs hundreds of rows: keep the fp32 partial sums short (as a level launch
       // does) by moving them into the fp64 slot every few rows.  Own columns only: no barrier.
       if (++since_flush == KB_FLOW_FLUSH_ROWS) {
