@@ -95,6 +95,59 @@ int kb_e_adjoint_solve(const float* E, const float* log_pS, const float* log_pD,
                        int max_iter, double tol, double breakdown_tol, float* work, float* w_out,
                        float* grad_params, int* status, float* rel_out, int S, int use_col_weights, void* stream);
 
+/* ---- exact-Hessian HVP: second-order contractions (newton/hvp_exact.py) ---------------- */
+
+/* Replaces wave_backward_so (kbench/core/kernels/wave_so.py:213-250, kernel :37-210): for wave
+ * rows w < W (global row ws + w), at the FIXED adjoint v [W,S], the tangent along (dPi, dPibar and
+ * the d-constants) of the self-loop J^T v (d_out [W,S], plus the rows ws.. of d_rhs [C,S] when
+ * d_rhs != NULL) and of the parameter buckets (d_aw [6,W,S]: aw0, aw1, aw2, aw345, aw3, aw4).
+ * Constants at item * const_row_stride + s (item = item_idx[ws + w]); leaf_state [C] (NULL = no
+ * leaf term) with leaf_logp / dleaf_logp at item * S + s; dts_r / d_dts [W,S] both or neither.
+ * jumps [K,S] (ancestor doubling) and the compact levels give the path and subtree sums. */
+int kb_wave_backward_so(const float* Pi, const float* dPi, const float* Pibar, const float* dPibar, const float* v,
+                        long long ws, int W, const float* pibar_row_max, const float* mc, const float* DL,
+                        const float* dDL, const float* Ebar, const float* dEbar, const float* E, const float* dE,
+                        const float* SL1, const float* dSL1, const float* SL2, const float* dSL2,
+                        long long const_row_stride, const float* col_log_probs, int use_col_weights,
+                        const int* node_parent, const int* node_child1, const int* node_child2, const int* jumps,
+                        int K, const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1,
+                        const int* lv_c2, const int* leaf_state, const float* leaf_logp, const float* dleaf_logp,
+                        const long long* item_idx, const float* dts_r, const float* d_dts, const float* d_rhs,
+                        float* d_out, float* d_aw, int S, void* stream);
+
+/* Replaces dts_backward_so (kbench/core/kernels/dts_so.py:233-303, kernels :24-230): for the
+ * wave's N splits (children sl / sr, parent ws + reduce_idx, split log-probabilities, NULL =
+ * zeros) at the FIXED adjoint v [W,S]: the tangents of the split cotangents, added with atomics
+ * into d_rhs [C,S] and d_grad_pD / d_grad_pS / d_grad_mt (rows item * S), and of both Pibar VJP
+ * trees, added into d_rhs (child rows) and d_grad_col [S].  Rates at item * param_row_stride + s
+ * (item = item_idx[item_offset + reduce_idx]), mt / dmt at item * mt_row_stride + s.  ud / dud
+ * [2N,S] are scratch. */
+int kb_dts_backward_so(const float* Pi, const float* dPi, const float* Pibar, const float* dPibar, const float* v,
+                       long long ws, const long long* sl, const long long* sr, const long long* reduce_idx,
+                       const float* log_split_probs, int N, long long item_offset, const long long* item_idx,
+                       const float* log_pD, const float* log_pS, const float* dlog_pD, const float* dlog_pS,
+                       long long param_row_stride, const float* mt, const float* dmt, long long mt_row_stride,
+                       const float* pibar_row_max, const float* col_log_probs, int use_col_weights,
+                       const int* node_child1, const int* node_child2, const long long* lv_ptr, int n_levels,
+                       const int* lv_par, const int* lv_c1, const int* lv_c2, float* ud, float* dud, float* d_rhs,
+                       float* d_grad_pD, float* d_grad_pS, float* d_grad_mt, float* d_grad_col, int S,
+                       void* stream);
+
+/* Replaces e_step_backward_so (kbench/core/kernels/e_step_so.py:188-220, kernels :23-185): the
+ * tangent of the E-step VJP outputs at FIXED cotangents (g_new, g_ebar) [G,S] along (dE,
+ * dE_new, dE_s1, dE_s2, dEbar, dlog_pS, dlog_pD, dlog_pL [G,S], dcol [S] or NULL).  Outputs
+ * [G,S] (d_grad_col [S], overwritten: sum over rows). */
+int kb_e_step_backward_so(const float* E, const float* E_new, const float* E_s1, const float* E_s2,
+                          const float* Ebar, const float* log_pS, const float* log_pD, const float* log_pL,
+                          const float* col_log_probs, const int* node_parent, const int* node_child1,
+                          const int* node_child2, const int* jumps, int K, const long long* lv_ptr, int n_levels,
+                          const int* lv_par, const int* lv_c1, const int* lv_c2, const float* g_new,
+                          const float* g_ebar, const float* dE, const float* dE_new, const float* dE_s1,
+                          const float* dE_s2, const float* dEbar, const float* dlog_pS, const float* dlog_pD,
+                          const float* dlog_pL, const float* dcol, float* d_grad_E, float* d_grad_pS,
+                          float* d_grad_pD, float* d_grad_pL, float* d_grad_mc, float* d_grad_col, int S, int G,
+                          int use_col_weights, void* stream);
+
 /* ---- parameter extraction (kbench/core/parameters/extract_parameters.py) ---------------- */
 
 /* Replaces col_valid_log_normalizer (extract_parameters.py:41-65): norm_out[s] =

@@ -241,7 +241,7 @@ def root_rhs(Pi, root_ids):
 
 
 @torch.no_grad()
-def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumulation=False):
+def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumulation=False, cache=None):
     """Reference ``_implicit_grad.py:98-370`` followed by :func:`e_adjoint_and_theta_vjp`.
 
     ``exact_accumulation=False`` reproduces the reference's accumulation exactly: every wave's
@@ -250,7 +250,13 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
     contributions are many orders of magnitude smaller, so fp32 swamping loses ~1e-3 of the
     split sums.  ``exact_accumulation=True`` runs the same kernels but starts each wave's fp32
     partial sums from zero and adds them into fp64 totals (the accuracy the fused engine gets
-    from its fp64 accumulators)."""
+    from its fp64 accumulators).
+
+    ``cache`` (a dict) receives the point cache of the exact-Hessian HVP (``newton/ggn.py:152-162``,
+    ``newton/hvp_exact.py:37-45``): ``waves`` -- per wave in the order processed (reverse wave
+    order) ``ws, W, v`` (adjoint rows, zero on inactive rows), ``dts_r, active_mask, has_splits,
+    has_leaf_term, meta`` --, ``accum`` (the column cotangent accumulators) and ``wE`` (the
+    E-side adjoint)."""
     so = static.solver_options
     wl, sh = static.wave_layout, static.state_helpers
     Pi, Pibar = saved["pi_wave"], saved["pibar_wave"]
@@ -315,6 +321,11 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
                 flush()
         if v_out is not None:
             v_out[ws:ws + W][active] = v_k[active]
+        if cache is not None:
+            row_on = active.reshape(W, -1).any(dim=1)
+            cache.setdefault("waves", []).append(dict(
+                ws=ws, W=W, v=torch.where(row_on[:, None], v_k, torch.zeros_like(v_k)), dts_r=dts_r,
+                active_mask=active, has_splits=has_splits, has_leaf_term=not has_splits, meta=meta))
         if has_splits:
             n_split = int(meta["sl"].numel())
             split_blocks = [(0, n_split)] if chunk is None else [(a, min(a + chunk, n_split))
@@ -343,7 +354,11 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
             getattr(g, n)[0] = g_total[n].float()
         g.col.copy_(g_total["col"].float())
     static._last_acc = acc
-    return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
+    out = e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
+    if cache is not None:
+        cache["accum"] = g
+        cache["wE"] = static._last_e_adjoint
+    return out
 
 
 DEVICE_E_ADJOINT = True  # one shared E row: the whole solve in one launch (kb_e_adjoint_solve)

@@ -702,7 +702,7 @@ def backward(static: dict, theta, col_weights, saved: dict, acc_dtype=F32):
                                    acc["mt"], acc["col"], n_fam=n_fam)
 
 
-def backward_accumulators(static: dict, saved: dict, acc_dtype=F32) -> dict:
+def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list | None = None) -> dict:
     """The reverse wave loop of ``kbench/api/_implicit_grad.py:98-370`` alone: the fp32 column
     accumulators ``pD, pS, mt, E, Ebar, E_s1, E_s2, col`` (``:144-158``) that the E adjoint and
     theta VJP consume.
@@ -710,7 +710,11 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32) -> dict:
     ``acc_dtype=np.float64`` keeps every per-wave / per-split fp32 partial as the reference
     computes it but adds them into float64 running sums: the accumulation-exact evaluation of the
     same algorithm (the reference's fp32 running sums lose low-order bits of small contributions
-    once the sums have grown)."""
+    once the sums have grown).
+
+    ``cache`` (a list) receives one dict per wave in the order processed (reverse wave order):
+    ``ws, W, v`` (the adjoint rows, zero on inactive rows), ``dts_r, active, has_splits, meta``
+    -- the point cache of the exact-Hessian HVP (``newton/ggn.py:152-162``)."""
     sh = static["state_helpers"]
     wl = static["wave_layout"]
     so = static["solver_options"]
@@ -748,6 +752,9 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32) -> dict:
             neumann_terms=int(so["neumann_terms"]),
             leaf_state=None if has_splits else leaf_state_all[ws:ws + W],
             leaf_logp=pS, active=act, grad_col=g_col)
+        if cache is not None:
+            cache.append(dict(ws=ws, W=W, v=np.where(act[:, None], v_k, F32(0.0)).astype(F32), dts_r=dts_r,
+                              active=act, has_splits=has_splits, meta=meta))
         g_pD += aw0.sum(0, dtype=F32); g_pS += aw345.sum(0, dtype=F32)
         g_E += (aw0 + aw2).sum(0, dtype=F32); g_Ebar += aw1.sum(0, dtype=F32)
         g_Es1 += aw4.sum(0, dtype=F32); g_Es2 += aw3.sum(0, dtype=F32)
@@ -764,7 +771,7 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32) -> dict:
 
 
 def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree: Tree, g_E, g_Ebar, g_Es1,
-                            g_Es2, g_pD, g_pS, g_mt, g_col, *, n_fam):
+                            g_Es2, g_pD, g_pS, g_mt, g_col, *, n_fam, out: dict | None = None):
     """``kbench/api/_implicit_grad.py:373-475``: solve ``(I - J_E^T) wE = q_E`` by BiCGSTAB with
     E-step VJPs as the matvec, then the theta/column-weight VJP."""
     so = static["solver_options"]
@@ -794,6 +801,8 @@ def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree: Tree, g_E, 
     wE = bicgstab(AG, q, max_iter=so.get("bicgstab_max_iter", 500),
                   tol=so.get("bicgstab_tol", 1e-7),
                   breakdown_tol=so.get("bicgstab_breakdown_tol", 1e-30))
+    if out is not None:
+        out["wE"] = wE
     # theta VJP: param_loss + E-step at E_star with cotangents (wE on E_new, g_Ebar on Ebar)
     _, q_pS, q_pD, q_pL, q_mt, q_col = vjp_E(wE, zeros, zeros, g_Ebar)
     grad_theta, grad_col = extract_parameters_vjp(

@@ -24,7 +24,13 @@ self-loop with ``self_iters = pi_iters``), evaluated at the fixture's saved forw
 along two seeded directions ``v ~ N(0,1)`` of theta's shape (seed 5000 + k); saved as
 ``tangent/<case>.npz``.
 
-Usage:  python tests/golden/make_golden.py --reference <path-to-reference-checkout> [--tangent]
+HVP fixtures (``--hvp``): for each forward fixture, the reference's analytic exact-Hessian HVP
+``newton/hvp_exact.py`` ``make_exact_hvp`` (its own ``kbench/core/kernels/{wave_so,dts_so,
+e_step_so}.py`` second-order kernels over the pristine first-order ones) at the fixture's saved
+forward intermediates along the same two seeded directions, with the driver's debug tangents
+(``d_g*`` accumulators, the E-side rhs ``dq_E`` and solve ``dwE``); saved as ``hvp/<case>.npz``.
+
+Usage:  python tests/golden/make_golden.py --reference <path-to-reference-checkout> [--tangent | --hvp]
 """
 
 from __future__ import annotations
@@ -150,16 +156,54 @@ def run_tangent_case(runtime, name):
     print(f"[tangent {name}] S={S} directions={TANGENT_DIRECTIONS} {time.time() - t0:.1f}s")
 
 
+HVP_DIRECTIONS = 2
+HVP_DEBUG_KEYS = ("d_gE", "d_gpD", "d_gpS", "d_gmc", "d_gEbar", "d_gEs1", "d_gEs2", "dq_E", "dwE")
+
+
+def run_hvp_case(runtime, name):
+    """The reference's analytic exact-Hessian HVP (``newton/hvp_exact.py`` ``make_exact_hvp``:
+    point cache from the production backward, tangent forward with ``self_iters = pi_iters``,
+    tangent-adjoint sweep with ``wave_so`` / ``dts_so`` / ``e_step_so``, smooth parameter head),
+    at the fixture's saved forward intermediates, along the tangent fixtures' directions."""
+    from kbench_b200.problem_io import unflatten_case
+    from newton.hvp_exact import make_exact_hvp
+    cap, out = unflatten_case(np.load(HERE / f"{name}.npz"))
+    cap = gen.to_torch(cap)
+    static = runtime.make_static(cap, "cpu")
+    theta = cap["inputs"]["theta"]
+    cw = cap["inputs"]["col_weights"]
+    S = int(theta.shape[0])
+    sv = {k: torch.from_numpy(np.asarray(v)) for k, v in out.items() if k not in ("loss", "grad_theta", "grad_col")}
+    arrays = {}
+    t0 = time.time()
+    dbg: dict = {}
+    hvp = make_exact_hvp(static, theta, cw, sv, debug_out=dbg)
+    for k in range(HVP_DIRECTIONS):
+        u = torch.from_numpy(tangent_direction(S, k)).reshape(-1)
+        dbg.clear()
+        hu = hvp(u)
+        arrays[f"u{k}"] = u.numpy()
+        arrays[f"hu{k}"] = hu.detach().numpy()
+        for key in HVP_DEBUG_KEYS:
+            arrays[f"{key}{k}"] = dbg[key].reshape(-1).numpy()
+    (HERE / "hvp").mkdir(exist_ok=True)
+    np.savez_compressed(HERE / "hvp" / f"{name}.npz", **arrays)
+    print(f"[hvp {name}] S={S} directions={HVP_DIRECTIONS} {time.time() - t0:.1f}s")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--cases", default=",".join(CASES))
     ap.add_argument("--tangent", action="store_true", help="tangent fixtures from the forward fixtures")
+    ap.add_argument("--hvp", action="store_true", help="exact-Hessian HVP fixtures from the forward fixtures")
     args = ap.parse_args()
     torch.set_num_threads(1)
     runtime = install_pristine(args.reference.resolve())
     for name in args.cases.split(","):
-        if args.tangent:
+        if args.hvp:
+            run_hvp_case(runtime, name)
+        elif args.tangent:
             run_tangent_case(runtime, name)
         else:
             cfg, seed, ov = CASES[name]
