@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--families", type=int, default=None, help="config 4: families in the whole batch")
     ap.add_argument("--chunk", type=int, default=128, help="config 4: families per chunk on a GPU")
     ap.add_argument("--directions", type=int, default=32, help="config 5: tangent directions per pass")
+    ap.add_argument("--hvp", action="store_true",
+                    help="exact-Hessian HVPs/s (newton/hvp_exact.py) on the --hvp-config family")
+    ap.add_argument("--hvp-config", type=int, default=2, help="--hvp: the problem config (default 2, S=511)")
     return ap.parse_args()
 
 
@@ -202,6 +205,136 @@ def run_cpu_oracle_sample(full_rows, seed, n_genes=512, species_leaves=2048):
     # per-row work is the same (same S, same iteration counts): scale to the full family
     solve_s = dt * full_rows / rows
     return 1.0 / solve_s, dt, rows
+
+
+HVP_BYTES_PER_ROW_ELEM = 13 * 4
+
+
+def hvp_oracle_sample(cfg, seed, n_genes):
+    """Time one oracle HVP (point cache excluded) on a small family of config ``cfg``'s species
+    tree; returns (seconds per HVP, rows of the sample)."""
+    import numpy as np
+    from kbench_b200 import gen
+    from oracle import kb_oracle as O
+    from oracle import kb_oracle_hvp as OH
+    c = gen.CONFIGS[cfg]
+    case = gen.ProblemConfig("hvp_sample", c.n_species, n_genes, 2, max(4, n_genes // 3), 0,
+                             solver_options=dict(c.solver_options))
+    cap = gen.generate(case, seed=seed, as_torch=False)
+    st = dict(cap["static"])
+    st["solver_options"] = cap["meta"]["solver_options"]
+    theta, cw = cap["inputs"]["theta"], cap["inputs"]["col_weights"]
+    _, saved = O.forward(st, theta, cw)
+    cache = OH.point_cache(st, theta, cw, saved)
+    u = np.random.default_rng(seed).standard_normal(theta.size).astype(np.float32)
+    t0 = time.perf_counter()
+    OH.hvp(st, theta, cw, saved, u, cache=cache)
+    return time.perf_counter() - t0, int(cap["meta"]["C"])
+
+
+def hvp_arm(args, world, rank, local):
+    """--hvp: analytic exact-Hessian HVPs (forward over reverse) at a fixed point of the
+    --hvp-config family, as a Newton-CG inner loop runs them (point cache built once, untimed);
+    replicas on N>1."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from kbench_b200 import _lib, gen, hvp, runtime
+
+    cfg = int(args.hvp_config)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    cap = gen.generate(cfg, seed=1000 * cfg + rank)
+    S, C = int(cap["meta"]["S"]), int(cap["meta"]["C"])
+    static = runtime.make_static(cap, dev)
+    theta = cap["inputs"]["theta"].to(dev)
+    cw = cap["inputs"]["col_weights"].to(dev)
+    _, sv = runtime.run_forward(static, theta, cw)
+    torch.cuda.synchronize()
+    c0 = time.perf_counter()
+    f = hvp.make_exact_hvp(static, theta, cw, sv)
+    torch.cuda.synchronize()
+    cache_ms = (time.perf_counter() - c0) * 1e3
+    U = torch.from_numpy(np.random.default_rng(7).standard_normal((4, 3 * S)).astype(np.float32)).to(dev)
+    for i in range(args.warmup):
+        f(U[i % 4])
+    torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = sum(_lib.LAUNCHES.values())
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        f(U[i % 4])
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    launches = sum(_lib.LAUNCHES.values()) - launches0
+    ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    # symmetry of the operator (u1 . H u0 = u0 . H u1 up to the solves' truncation)
+    h0, h1 = f(U[0]).double(), f(U[1]).double()
+    asym = abs(float(U[1].double() @ h0) - float(U[0].double() @ h1)) / float(
+        h0.norm() * U[1].double().norm() + h1.norm() * U[0].double().norm())
+    # end to end: the direction from pinned host memory, H u back
+    u_host = U.cpu().pin_memory()
+    out_host = torch.empty((3 * S,), dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for i in range(args.steps):
+        out_host.copy_(f(u_host[i % 4].to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        float(out_host[0])
+    x1.record()
+    torch.cuda.synchronize()
+    x_t = torch.tensor([x0.elapsed_time(x1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(x_t, op=dist.ReduceOp.MAX)
+    e_ms = float(x_t.item())
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        alg = HVP_BYTES_PER_ROW_ELEM * C * S
+        achieved = alg / (ms * 1e-3) / 1e9
+        cpu = None
+        if not args.no_cpu_baseline:
+            dt, rows = hvp_oracle_sample(cfg, seed=77, n_genes=24)
+            per = dt * C / rows
+            cpu = {"value": round(1.0 / per, 6), "unit": "HVPs/s", "cores": 1, "kind": "port",
+                   "sample": f"numpy oracle HVP of a {rows}-row family on the config-{cfg} species tree (S={S}), "
+                             f"{dt:.1f} s, extrapolated per row to C={C}"}
+        line = {
+            "metric": f"exact-Hessian HVPs/sec (newton/hvp_exact.py, config {cfg}: S={S}, C={C})",
+            "value": round(world * 1000.0 / ms, 4), "unit": "HVPs/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator of the benchmark's config text)",
+            "config": {"workload": f"config{cfg} HVP at a fixed point: tangent forward + tangent-adjoint sweep over "
+                                   f"{int(cap['meta']['n_waves'])} waves + E side + head; point cache "
+                                   f"{cache_ms:.0f} ms once, untimed", "parallelism": f"dp{world} (replicas)",
+                       "l2": "state arrays re-read every HVP; no flush"},
+            "point_cache_ms": round(cache_ms, 1), "symmetry_rel": asym,
+            "roofline": {"bound": "hbm", "kernel": "whole HVP (per-wave launches)", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5),
+                         "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                         "algorithmic_bytes_per_launch": alg},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * 1000.0 / e_ms, 4), "unit": "HVPs/s", "h2d_bytes_per_step": 3 * S * 4,
+                    "d2h_bytes_per_step": 3 * S * 4},
+            "gpu_launches": int(launches), "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def reference_arm(args, world, rank):
@@ -520,6 +653,9 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
+    if args.hvp:
+        hvp_arm(args, world, rank, local)
+        return
     if args.config == 4:
         batch_arm(args, world, rank, local)
         return

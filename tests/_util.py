@@ -70,3 +70,23 @@ def assert_close_rows(name, got, ref, rtol=RTOL, atol=ATOL):
         i = np.unravel_index(int(np.argmax(d / tol)), d.shape)
         raise AssertionError(f"{name}: {int(bad.sum())} elements out of tolerance; worst |d|={d[i]:.3e} "
                              f"ref={ref[i]:.6e} row scale={float(scale[i[:-1]][0]):.3e}")
+
+
+def assert_close_vec(name, got, ref, rtol=RTOL, atol=ATOL):
+    """Vectors that are signed accumulations over every wave (the HVP's tangent cotangents and
+    H u): |got - ref| <= atol + rtol * max|ref| per element, and ||got - ref|| <= rtol ||ref||.
+    An element that is a near-cancelling sum of many terms carries the absolute error of the
+    terms, so its bound is set by the vector's scale, not by its own size."""
+    got = np.asarray(got, dtype=np.float64).reshape(-1)
+    ref = np.asarray(ref, dtype=np.float64).reshape(-1)
+    assert got.shape == ref.shape, f"{name}: shape {got.shape} vs {ref.shape}"
+    assert not np.isnan(got).any(), f"{name}: NaN in result"
+    scale = float(np.abs(ref).max()) if ref.size else 0.0
+    d = np.abs(got - ref)
+    tol = atol + rtol * scale
+    if (d > tol).any():
+        i = int(np.argmax(d))
+        raise AssertionError(f"{name}: {int((d > tol).sum())} elements out of tolerance; worst |d|={d[i]:.3e} "
+                             f"ref={ref[i]:.6e} (tol {tol:.3e}, scale {scale:.3e})")
+    nr = float(np.linalg.norm(ref))
+    assert float(np.linalg.norm(got - ref)) <= rtol * max(nr, 1e-30) + atol, f"{name}: norm-wise error"

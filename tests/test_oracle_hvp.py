@@ -1,11 +1,13 @@
 """The CPU exact-Hessian HVP oracle against the reference's own ``newton/hvp_exact.py``
 ``make_exact_hvp`` run by tests/golden/make_golden.py --hvp (its second-order kernels under
-``TRITON_INTERPRET=1``), and the symmetry a Hessian-vector product must have."""
+``TRITON_INTERPRET=1``), and the symmetry a Hessian-vector product must have.  The compared
+vectors are signed accumulations over every wave: ``assert_close_vec`` (rel 1e-4 of the vector's
+scale per element, and norm-wise)."""
 
 import numpy as np
 import pytest
 
-from _util import GOLDEN, assert_close, load_golden, oracle_static
+from _util import GOLDEN, assert_close_vec, load_golden, oracle_static
 from oracle import kb_oracle_hvp as OH
 
 NAMES = sorted(p.stem for p in (GOLDEN / "hvp").glob("*.npz"))
@@ -37,8 +39,8 @@ def test_oracle_hvp_matches_reference(name):
         dbg: dict = {}
         hu = OH.hvp(st, theta, cw, saved, hv[f"u{k}"], cache=cache, debug_out=dbg)
         for key in DEBUG:
-            assert_close(f"{key}[{k}]", dbg[key].reshape(-1), hv[f"{key}{k}"])
-        assert_close(f"Hu[{k}]", hu, hv[f"hu{k}"])
+            assert_close_vec(f"{key}[{k}]", dbg[key].reshape(-1), hv[f"{key}{k}"])
+        assert_close_vec(f"Hu[{k}]", hu, hv[f"hu{k}"])
         k += 1
     assert k >= 1
 
