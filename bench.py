@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--hvp", action="store_true",
                     help="exact-Hessian HVPs/s (newton/hvp_exact.py) on the --hvp-config family")
     ap.add_argument("--hvp-config", type=int, default=2, help="--hvp: the problem config (default 2, S=511)")
+    ap.add_argument("--cuda-profiler-range", action="store_true",
+                    help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
 
 
@@ -266,11 +268,15 @@ def hvp_arm(args, world, rank, local):
     if sampler:
         sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.cuda_profiler_range:
+        torch.cuda.profiler.start()
     e0.record()
     for i in range(args.steps):
         f(U[i % 4])
     e1.record()
     torch.cuda.synchronize()
+    if args.cuda_profiler_range:
+        torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop() if sampler else None

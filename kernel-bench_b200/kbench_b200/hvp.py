@@ -27,7 +27,7 @@ from .kernels.wave_backward import (dts_cross_backward_accum_fused, uniform_cros
                                     wave_backward_uniform_fused)
 from .kernels.wave_so import wave_backward_so
 from .params import as_item_param, as_item_state, extract_parameters_weighted_cols
-from .tangent import jvp_root_scores
+from .tangent import jvp_root_scores, tangent_wave_cache
 
 LN2 = math.log(2.0)
 
@@ -73,6 +73,7 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
     if cache is None:
         _, _, cache = build_point_cache(static, theta, col_weights, sv)
     acc, wE = cache["accum"], cache["wE"].reshape(E_star.shape)
+    tcache = tangent_wave_cache(static, sv)  # u-independent: primal split reductions, split CSRs
     cst = _wave_constants(sv, S, G)
     prm, col = sv["pibar_row_max"], sv["col_log_probs"]
     item = lambda t: as_item_state(t, S, G)  # noqa: E731
@@ -125,7 +126,8 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
     def hvp(u_vec):
         u = u_vec.reshape(S, 3).to(theta.dtype)
         with torch.no_grad():
-            t_root, full = jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters)
+            t_root, full = jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters,
+                                           wave_cache=tcache)
             dc = full["dcst"]
             dPi, dPibar = full["dPi"], full["dPibar"]
             dE, dEbar_e, dE_s1, dE_s2 = full["dE"], full["dEbar"], full["dE_s1"], full["dE_s2"]
@@ -147,7 +149,8 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
                     d_dts = compute_dts_tangent(
                         sv["pi_wave"], sv["pibar_wave"], dPi, dPibar, meta["sl"], meta["sr"], c1, c2, W,
                         meta["reduce_idx"], cst["pd_param"], cst["ps_param"], dc["dpd_param"], dc["dps_param"],
-                        dts_r, item_idx, log_split_probs=meta.get("log_split_probs"), item_offset=ws)
+                        dts_r, item_idx, log_split_probs=meta.get("log_split_probs"), item_offset=ws,
+                        csr=tcache[ws]["csr"])
                 has_leaf = wave["has_leaf_term"]
                 # (a) second-order contraction at the fixed v_k, the wave's d_rhs folded in: the seed
                 d_Av, *c_aw = wave_backward_so(
@@ -164,14 +167,15 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
                     node_parent=parent, max_ancestor_depth=mad, pibar_row_max=prm, item_idx=item_idx,
                     item_indexed_consts=True, **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
                     self_loop_solver=so.self_loop_solver)
-                aw = [c + l for c, l in zip(c_aw, l_aw)]  # aw0, aw1, aw2, aw345, aw3, aw4
-                d_gpD[0] += aw[0].sum(dim=0)
-                d_gpS[0] += aw[3].sum(dim=0)
-                d_gE[0] += (aw[0] + aw[2]).sum(dim=0)
-                d_gEbar[0] += aw[1].sum(dim=0)
-                d_gEs1[0] += aw[5].sum(dim=0)
-                d_gEs2[0] += aw[4].sum(dim=0)
-                d_gmc[0] += aw[2].sum(dim=0)
+                # column sums of aw0, aw1, aw2, aw345, aw3, aw4 (contraction + solve parts) in one pass
+                aw = (torch.stack(c_aw) + torch.stack(l_aw)).sum(dim=1)
+                d_gpD[0] += aw[0]
+                d_gpS[0] += aw[3]
+                d_gE[0] += aw[0] + aw[2]
+                d_gEbar[0] += aw[1]
+                d_gEs1[0] += aw[5]
+                d_gEs2[0] += aw[4]
+                d_gmc[0] += aw[2]
                 if dts_r is not None:
                     gl, gr, side, _, _ = dts_cross_backward_accum_fused(
                         sv["pi_wave"], sv["pibar_wave"], dv, ws, meta["sl"], meta["sr"], meta["reduce_idx"],

@@ -8,13 +8,27 @@ from .. import _lib
 from ._common import f32, i32, i64, require_cuda_f32, state_rows
 
 
+def parent_csr(reduce_idx, W):
+    """(order, ptr): the splits of each of the W parent rows, in split order, as a CSR over
+    ``reduce_idx`` -- the fixed summation order of :func:`compute_dts_tangent`.  Depends only on the
+    wave layout, so callers that run many tangents can build it once and pass it as ``csr``."""
+    N = int(reduce_idx.numel())
+    red = i64(reduce_idx.reshape(N))
+    order = torch.sort(red, stable=True).indices.contiguous()
+    counts = torch.bincount(red, minlength=int(W))
+    ptr = torch.zeros((int(W) + 1,), device=red.device, dtype=torch.int64)
+    torch.cumsum(counts, 0, out=ptr[1:])
+    return order, ptr
+
+
 def compute_dts_tangent(Pi, Pibar, dPi, dPibar, lefts, rights, node_child1, node_child2, W, reduce_idx,
                         log_pD_vec, log_pS_vec, dlog_pD_vec, dlog_pS_vec, dts_r, item_idx, *, log_split_probs=None,
                         n_eq1=None, eq1_reduce_idx=None, ge2_ptr=None, ge2_parent_ids=None, ge2_max_fanout=None,
-                        item_offset=0):
+                        item_offset=0, csr=None):
     """Reference ``dts_tangent.py:99-122``: returns a new ``d_dts`` [W,S].  Each parent row sums its
     splits in a fixed order (the eq1 / ge2 layout arguments are accepted for signature
-    compatibility; the full ``reduce_idx`` map is used, as the reference's kernel does)."""
+    compatibility; the full ``reduce_idx`` map is used, as the reference's kernel does).  ``csr``:
+    :func:`parent_csr` of this wave, built once by the caller (else here)."""
     require_cuda_f32("compute_dts_tangent", Pi, Pibar, dPi, dPibar, dts_r)
     N = int(lefts.shape[0])
     S = int(Pi.shape[1])
@@ -22,11 +36,7 @@ def compute_dts_tangent(Pi, Pibar, dPi, dPibar, lefts, rights, node_child1, node
     out = torch.zeros((W, S), device=Pi.device, dtype=Pi.dtype)
     if N == 0 or W == 0:
         return out
-    red = i64(reduce_idx.reshape(N))
-    order = torch.sort(red, stable=True).indices.contiguous()
-    counts = torch.bincount(red, minlength=W)
-    ptr = torch.zeros((W + 1,), device=Pi.device, dtype=torch.int64)
-    torch.cumsum(counts, 0, out=ptr[1:])
+    order, ptr = parent_csr(reduce_idx, W) if csr is None else csr
     lsp = None if log_split_probs is None else f32(log_split_probs.reshape(N))
     pD, prs = state_rows(log_pD_vec, S)
     pS, _ = state_rows(log_pS_vec, S)

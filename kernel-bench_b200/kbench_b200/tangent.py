@@ -24,7 +24,7 @@ import torch
 from . import _lib, engine, tree
 from .kernels._common import f32, i32, i64
 from .kernels.dts_fused import compute_dts_forward
-from .kernels.dts_tangent import compute_dts_tangent
+from .kernels.dts_tangent import compute_dts_tangent, parent_csr
 from .kernels.e_step_tangent import e_tangent_fixed_point
 from .kernels.wave_tangent import compute_wave_step_tangent, compute_wave_step_tangent_selfloop
 from .params import as_item_param, as_item_state
@@ -86,14 +86,39 @@ def tangent_constants(static, theta, v, sv, S, e_tol, raw_out=None):
 
 
 @torch.no_grad()
+def tangent_wave_cache(static, sv) -> dict:
+    """The direction-independent part of :func:`jvp_root_scores`' wave loop, for callers that run
+    many tangents at one point (the exact-Hessian HVP): per wave with splits, the primal split
+    reduction ``dts_r`` and the split CSR of the tangent reduction (keyed by the wave's start row)."""
+    sh, wl = static.state_helpers, static.wave_layout
+    S = int(sh["S"])
+    base = _base_constants(sv, S)
+    out = {}
+    for meta in wl["wave_metas"]:
+        if "sl" not in meta:
+            continue
+        ws, W = int(meta["start"]), int(meta["W"])
+        dts_r = compute_dts_forward(sv["pi_wave"], sv["pibar_wave"], meta["sl"], meta["sr"], sh["node_child1"],
+                                    sh["node_child2"], W, meta["reduce_idx"], base["pd_param"], base["ps_param"],
+                                    item_idx=static.rate_item_idx, log_split_probs=meta.get("log_split_probs"),
+                                    n_eq1=meta.get("n_eq1"), eq1_reduce_idx=meta.get("eq1_reduce_idx"),
+                                    ge2_ptr=meta.get("ge2_ptr"), ge2_parent_ids=meta.get("ge2_parent_ids"),
+                                    ge2_max_fanout=meta.get("ge2_max_fanout"), item_offset=ws)
+        out[ws] = {"dts_r": dts_r, "csr": parent_csr(meta["reduce_idx"], W)}
+    return out
+
+
+@torch.no_grad()
 def jvp_root_scores(static, theta, v, sv, *, self_tol=None, self_max_iter=200, e_tol=None, self_iters=None,
-                    return_full=False):
+                    return_full=False, wave_cache=None):
     """``forward_tangent.py:105-215`` driven through the drop-in wrappers (one direction):
     returns ``d(Pi_root)/dtheta . v`` [n_roots, S] (and, with ``return_full``, a dict with
     ``dPi``, ``dPibar``, the tangent constants and the raw parameter / E tangents).
 
     ``self_iters`` runs the fused fixed-count self-loop (the tangent config's setting); ``None``
-    iterates each wave's self-loop to ``self_tol`` as the reference's adaptive path does."""
+    iterates each wave's self-loop to ``self_tol`` as the reference's adaptive path does.
+    ``wave_cache``: :func:`tangent_wave_cache` at the same point (skips recomputing the primal
+    split reductions)."""
     sh, wl = static.state_helpers, static.wave_layout
     S = int(sh["S"])
     if self_tol is None:
@@ -129,11 +154,16 @@ def jvp_root_scores(static, theta, v, sv, *, self_tol=None, self_max_iter=200, e
                       eq1_reduce_idx=meta.get("eq1_reduce_idx"), ge2_ptr=meta.get("ge2_ptr"),
                       ge2_parent_ids=meta.get("ge2_parent_ids"), ge2_max_fanout=meta.get("ge2_max_fanout"),
                       item_offset=ws)
-            dts_r = compute_dts_forward(pi, pibar, meta["sl"], meta["sr"], c1, c2, W, meta["reduce_idx"],
-                                        base["pd_param"], base["ps_param"], item_idx=item_idx, **kw)
+            wc = None if wave_cache is None else wave_cache[ws]
+            if wc is None:
+                dts_r = compute_dts_forward(pi, pibar, meta["sl"], meta["sr"], c1, c2, W, meta["reduce_idx"],
+                                            base["pd_param"], base["ps_param"], item_idx=item_idx, **kw)
+            else:
+                dts_r = wc["dts_r"]
             d_dts = compute_dts_tangent(pi, pibar, dpi, dpibar, meta["sl"], meta["sr"], c1, c2, W,
                                         meta["reduce_idx"], base["pd_param"], base["ps_param"], dc["dpd_param"],
-                                        dc["dps_param"], dts_r, item_idx, **kw)
+                                        dc["dps_param"], dts_r, item_idx, csr=None if wc is None else wc["csr"],
+                                        **kw)
         else:
             dts_r = d_dts = None
         if self_iters is not None:
