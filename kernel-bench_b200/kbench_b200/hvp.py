@@ -18,10 +18,11 @@ import math
 
 import torch
 
+from . import _lib
 from .glue import implicit_grad, logsumexp2, _safe_exp2_ratio
 from .kernels.dts_so import dts_backward_so
 from .kernels.dts_tangent import compute_dts_tangent
-from .kernels.e_step import e_adjoint_solve, e_step_triton_autograd
+from .kernels.e_step import _launch_e_step_forward_2d, e_adjoint_check, e_adjoint_solve, e_step_vjp
 from .kernels.e_step_so import e_step_backward_so
 from .kernels.wave_backward import (dts_cross_backward_accum_fused, uniform_cross_pibar_vjp_tree_from_ud_fused,
                                     wave_backward_uniform_fused)
@@ -50,10 +51,23 @@ def _wave_constants(sv, S, G):
             "pd_param": as_item_param(sv["log_pD"], G, S), "ps_param": as_item_param(sv["log_pS"], G, S)}
 
 
-def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None, tangent_self_iters=None):
+def _closed_form_head(theta, S, G):
+    """The smooth head has a closed form for statewise theta ``[S,3]`` and one item row: the
+    parameters are ``log2softmax([0, theta_s])`` (plus theta-free shifts), whose derivative in the
+    logits is ``I - 1 p^T`` and second derivative ``-ln2 (diag p - p p^T)`` (``p = softmax2``)."""
+    return G == 1 and theta.ndim == 2 and tuple(theta.shape) == (S, 3)
+
+
+def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None, tangent_self_iters=None,
+                   graph=False):
     """``hvp_exact.py:64-375``: returns ``hvp(u_vec) -> H u`` (flat ``[3S]``) at ``theta``.  The
     tangent self-loop runs ``tangent_self_iters`` fixed iterations (default ``pi_iters``, the
-    primal forward's truncation)."""
+    primal forward's truncation).
+
+    ``graph=True`` captures one HVP into a CUDA graph on the first call and replays it for every
+    direction (the HVP is otherwise bound by host dispatch: thousands of small launches); every
+    call then costs one copy of ``u``, one replay and one read of the E-solve status word.  It needs
+    the closed-form head (statewise theta, one item row) and no ``debug_out``."""
     so = static.solver_options
     if tangent_self_iters is None:
         tangent_self_iters = int(so.pi_iters) if getattr(so, "pi_iters", None) else 16
@@ -80,156 +94,192 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
     pS_m, pD_m, pL_m = item(sv["log_pS"]), item(sv["log_pD"]), item(sv["log_pL"])
     mc_m = item(sv["max_coupling"].squeeze(-1))
     topo = (parent, c1, c2, mad)
+    closed = _closed_form_head(theta, S, G)
+    if graph and (not closed or debug_out is not None):
+        raise ValueError("make_exact_hvp(graph=True) needs statewise theta [S,3], one item row, no debug_out")
 
-    # the E step at (E*, parameters) as an autograd graph: the linear-in-cotangent VJPs
-    E_req = E_star.detach().requires_grad_(True)
-    with torch.enable_grad():
-        _, Es1_g, Es2_g, Ebar_g = e_step_triton_autograd(E_req, sv["log_pS"], sv["log_pD"], sv["log_pL"],
-                                                          sv["max_coupling"], col, *topo, use_col_weights=False)
+    # the E step at (E*, parameters), once: its VJPs are linear in the cotangents
+    E_fwd = _launch_e_step_forward_2d(E_star.contiguous(), pS_m, pD_m, pL_m, mc_m, col, *topo, use_col_weights=False)
 
-    def aux_T(g_s1, g_s2, g_ebar):
-        with torch.enable_grad():
-            (out,) = torch.autograd.grad((Es1_g, Es2_g, Ebar_g), E_req, grad_outputs=(g_s1, g_s2, g_ebar),
-                                         retain_graph=True)
-        return out
-
-    def e_bwd_params(g_new, g_ebar):
-        """Cotangents of (log_pS, log_pD, log_pL, max_coupling, col_log_probs) through the E step."""
-        with torch.enable_grad():
-            req = [t.detach().requires_grad_(True) for t in (pS_m, pD_m, pL_m, mc_m, col)]
-            En, _, _, Eb = e_step_triton_autograd(E_star.detach(), *req, *topo, use_col_weights=False)
-            outs = torch.autograd.grad((En, Eb), req, grad_outputs=(g_new, g_ebar), allow_unused=True)
-        return tuple(torch.zeros_like(r) if o is None else o for o, r in zip(outs, req))
+    def vjp_E(g_new, g_s1, g_s2, g_ebar):
+        """(grad_E, grad_pS, grad_pD, grad_pL, grad_mc, grad_col) of the E step at E*."""
+        return e_step_vjp(E_star, *E_fwd, pS_m, pD_m, pL_m, col, *topo, g_new, g_s1, g_s2, g_ebar,
+                          use_col_weights=False)
 
     norm = (1 - torch.exp2(E_star).mean(dim=-1, keepdim=True)).clamp_min(torch.finfo(E_star.dtype).tiny)
     fam_factor = 1.0 if G == n_fam else float(n_fam)
 
-    # u-independent: the primal parameter cotangents and the smooth head's first-order graph
-    base_p = e_bwd_params(wE, acc.Ebar)
+    # u-independent: the primal parameter cotangents of the smooth head
+    base_p = vjp_E(wE, None, None, acc.Ebar)[1:]
     cot_pS = acc.pS + as_item_param(base_p[0], G, S)
     cot_pD = acc.pD + as_item_param(base_p[1], G, S)
     cot_pL = base_p[2]
     cot_mc = acc.mt + base_p[3]
     cot_col = acc.col + base_p[4]
-    theta_req = theta.detach().requires_grad_(True)
-    col_req = col_weights.detach().requires_grad_(True)
-    with torch.enable_grad():
-        pS_h, pD_h, pL_h, mt_h, col_h = extract_parameters_weighted_cols(
-            theta_req, col_req, sh, statewise=static.statewise, itemwise=static.itemwise, uniform_fast=True)
-        pS_hp, pD_hp = as_item_param(pS_h, G, S), as_item_param(pD_h, G, S)
-        pL_hi = as_item_state(pL_h, S, G)
-        mt_hi = as_item_state(mt_h.squeeze(-1) if mt_h.ndim == pS_h.ndim + 1 else mt_h, S, G)
-        phi1 = ((pS_hp * cot_pS).sum() + (pD_hp * cot_pD).sum() + (pL_hi * cot_pL).sum() + (mt_hi * cot_mc).sum()
-                + (col_h * cot_col).sum())
-        (g1,) = torch.autograd.grad(phi1, theta_req, create_graph=True)
+    if closed:
+        lg = torch.cat([torch.zeros((S, 1), device=theta.device, dtype=torch.float32), theta.float()], dim=1)
+        p_ev = torch.softmax(lg * LN2, dim=1)[:, 1:]                     # softmax2 of the theta events
+        c_sum = (cot_pS.reshape(S) + cot_pD.reshape(S) + cot_pL.reshape(S) + cot_mc.reshape(S))[:, None]
+    else:
+        theta_req = theta.detach().requires_grad_(True)
+        col_req = col_weights.detach().requires_grad_(True)
+        with torch.enable_grad():
+            pS_h, pD_h, pL_h, mt_h, col_h = extract_parameters_weighted_cols(
+                theta_req, col_req, sh, statewise=static.statewise, itemwise=static.itemwise, uniform_fast=True)
+            pS_hp, pD_hp = as_item_param(pS_h, G, S), as_item_param(pD_h, G, S)
+            pL_hi = as_item_state(pL_h, S, G)
+            mt_hi = as_item_state(mt_h.squeeze(-1) if mt_h.ndim == pS_h.ndim + 1 else mt_h, S, G)
+            phi1 = ((pS_hp * cot_pS).sum() + (pD_hp * cot_pD).sum() + (pL_hi * cot_pL).sum()
+                    + (mt_hi * cot_mc).sum() + (col_h * cot_col).sum())
+            (g1,) = torch.autograd.grad(phi1, theta_req, create_graph=True)
 
-    def hvp(u_vec):
-        u = u_vec.reshape(S, 3).to(theta.dtype)
-        with torch.no_grad():
-            t_root, full = jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters,
-                                           wave_cache=tcache)
-            dc = full["dcst"]
-            dPi, dPibar = full["dPi"], full["dPibar"]
-            dE, dEbar_e, dE_s1, dE_s2 = full["dE"], full["dEbar"], full["dE_s1"], full["dE_s2"]
-            dpS_m, dpD_m, dpL_m = item(full["dlog_pS"]), item(full["dlog_pD"]), item(full["dlog_pL"])
-            # tangent of the loss seed -softmax2(Pi_root) on the root rows
-            root_Pi = sv["pi_wave"].index_select(0, root_ids)
-            q = _safe_exp2_ratio(root_Pi, logsumexp2(root_Pi, dim=-1, keepdim=True))
-            d_rhs = torch.zeros((C, S), device=theta.device, dtype=torch.float32)
-            d_rhs.index_copy_(0, root_ids, (-LN2 * q * (t_root - (q * t_root).sum(dim=-1, keepdim=True))).float())
-            d_gpD, d_gpS = torch.zeros_like(acc.pD), torch.zeros_like(acc.pS)
-            d_gE, d_gEbar, d_gEs1, d_gEs2 = (torch.zeros_like(E_star) for _ in range(4))
-            d_gmc = torch.zeros_like(acc.mt)
-            d_gcol = torch.zeros((S,), device=theta.device, dtype=torch.float32)
-            for wave in cache["waves"]:  # reverse wave order
-                ws, W, meta = wave["ws"], wave["W"], wave["meta"]
-                v_k, dts_r, active = wave["v"], wave["dts_r"], wave["active_mask"]
-                d_dts = None
-                if dts_r is not None:
-                    d_dts = compute_dts_tangent(
-                        sv["pi_wave"], sv["pibar_wave"], dPi, dPibar, meta["sl"], meta["sr"], c1, c2, W,
-                        meta["reduce_idx"], cst["pd_param"], cst["ps_param"], dc["dpd_param"], dc["dps_param"],
-                        dts_r, item_idx, log_split_probs=meta.get("log_split_probs"), item_offset=ws,
-                        csr=tcache[ws]["csr"])
-                has_leaf = wave["has_leaf_term"]
-                # (a) second-order contraction at the fixed v_k, the wave's d_rhs folded in: the seed
-                d_Av, *c_aw = wave_backward_so(
-                    sv["pi_wave"], dPi, sv["pibar_wave"], dPibar, v_k, ws, W, S, prm, cst["mc"], cst["dl"],
-                    dc["dDL"], cst["ebar"], dc["dEbar"], cst["e"], dc["dE"], cst["sl1"], dc["dSL1"], cst["sl2"],
-                    dc["dSL2"], col, c1, c2, parent, mad, dts_r, d_dts, leaf_state_idx=leaf_state,
-                    leaf_logp=cst["leaf"], dleaf_logp=dc["dleaf"], item_idx=item_idx, has_leaf_term=has_leaf,
-                    use_col_weights=False, d_rhs=d_rhs)
-                # (b) the tangent adjoint: the same solve and mask, seeded with it
-                dv, *l_aw = wave_backward_uniform_fused(
-                    sv["pi_wave"], sv["pibar_wave"], ws, W, S, dts_r, d_Av, cst["mc"], cst["dl"], cst["ebar"],
-                    cst["e"], cst["sl1"], cst["sl2"], col, c1, c2, None, neumann_terms=int(so.neumann_terms),
-                    leaf_state_idx=leaf_state, leaf_logp=cst["leaf"], has_leaf_term=has_leaf, active_mask=active,
-                    node_parent=parent, max_ancestor_depth=mad, pibar_row_max=prm, item_idx=item_idx,
-                    item_indexed_consts=True, **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
-                    self_loop_solver=so.self_loop_solver)
-                # column sums of aw0, aw1, aw2, aw345, aw3, aw4 (contraction + solve parts) in one pass
-                aw = (torch.stack(c_aw) + torch.stack(l_aw)).sum(dim=1)
-                d_gpD[0] += aw[0]
-                d_gpS[0] += aw[3]
-                d_gE[0] += aw[0] + aw[2]
-                d_gEbar[0] += aw[1]
-                d_gEs1[0] += aw[5]
-                d_gEs2[0] += aw[4]
-                d_gmc[0] += aw[2]
-                if dts_r is not None:
-                    gl, gr, side, _, _ = dts_cross_backward_accum_fused(
-                        sv["pi_wave"], sv["pibar_wave"], dv, ws, meta["sl"], meta["sr"], meta["reduce_idx"],
-                        meta["log_split_probs"], cst["pd_param"], cst["ps_param"], c1, c2, d_rhs, S,
-                        active_mask=active, merge_s_term=True, grad_log_pD=d_gpD, grad_log_pS=d_gpS, grad_mt=d_gmc,
-                        accum_param_reductions=True, accum_mt_reduction=True, output_pibar_ud=True,
-                        output_pibar_side_active=True, pibar_side_threshold=so.pibar_side_threshold,
-                        mt_squeezed=cst["mc"], pibar_row_max=prm, skip_inactive_pibar_output_zero=True,
-                        item_idx=item_idx)
-                    uniform_cross_pibar_vjp_tree_from_ud_fused(
-                        sv["pi_wave"], col, gl, gr, meta["sl"], meta["sr"], d_rhs, S, active_mask=active,
-                        reduce_idx=meta["reduce_idx"], pibar_row_max=prm, skip_zero_sides=True, side_active=side,
-                        **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
-                        side_active_threshold=so.pibar_side_threshold)
-                    dts_backward_so(sv["pi_wave"], dPi, sv["pibar_wave"], dPibar, v_k, ws, meta, S,
-                                    cst["pd_param"], cst["ps_param"], dc["dpd_param"], dc["dps_param"], cst["mc"],
-                                    dc["dMC"], col, c1, c2, parent, mad, prm, item_idx, d_rhs, d_gpD, d_gpS,
-                                    d_gmc, d_gcol, **lv, use_col_weights=False)
-            del dPi, dPibar
-            full.clear()
-            # ---- E side ----
-            x_args = (E_star.contiguous(), E_star.contiguous(), sv["E_s1"], sv["E_s2"], sv["Ebar"], pS_m, pD_m, pL_m,
-                      col.contiguous(), *topo)
-            dx = (dE, dE, dE_s1, dE_s2, dEbar_e, dpS_m, dpD_m, dpL_m, None)
-            zero = torch.zeros_like(E_star)
-            aux_lin = aux_T(d_gEs1, d_gEs2, d_gEbar)
-            so_aux = e_step_backward_so(*x_args, zero, acc.E_s1, acc.E_s2, acc.Ebar, *dx, use_col_weights=False)
-            e2E = torch.exp2(E_star)
-            dnorm = -LN2 * (e2E * dE).mean(dim=-1, keepdim=True)
-            dg_norm = fam_factor * (-LN2 * e2E * dE / (S * norm) + e2E * dnorm / (S * norm * norm))
-            dq_E = d_gE + aux_lin + so_aux[0] + dg_norm
-            so_w = e_step_backward_so(*x_args, wE, zero, zero, zero, *dx, use_col_weights=False)
-            rhs_E = dq_E + so_w[0]
-            zs = torch.zeros((S,), device=theta.device, dtype=torch.float32)
-            dwE, _ = e_adjoint_solve(E_star, sv["log_pS"], sv["log_pD"], sv["log_pL"], sv["max_coupling"], col,
-                                     *topo, rhs_E.reshape(-1), zs, zs, zs, n_fam=0.0,
-                                     max_iter=so.bicgstab_max_iter, tol=float(so.bicgstab_tol),
-                                     breakdown_tol=so.bicgstab_breakdown_tol, use_col_weights=False)
-            dwE = dwE.reshape(E_star.shape)
-            if debug_out is not None:
-                debug_out.update(d_gE=d_gE.clone(), d_gpD=d_gpD.clone(), d_gpS=d_gpS.clone(), d_gmc=d_gmc.clone(),
-                                 d_gEbar=d_gEbar.clone(), d_gEs1=d_gEs1.clone(), d_gEs2=d_gEs2.clone(),
-                                 dq_E=dq_E.clone(), dwE=dwE.clone())
-            lin_p = e_bwd_params(dwE, d_gEbar)
-            so_p = e_step_backward_so(*x_args, wE, zero, zero, acc.Ebar, *dx, use_col_weights=False)
-            d_cot_pS = d_gpS + as_item_param(lin_p[0] + so_p[1], G, S)
-            d_cot_pD = d_gpD + as_item_param(lin_p[1] + so_p[2], G, S)
-            d_cot_pL = lin_p[2] + so_p[3]
-            d_cot_mc = d_gmc + lin_p[3] + so_p[4]
-            d_cot_col = d_gcol + lin_p[4] + so_p[5]
+    @torch.no_grad()
+    def body(u_vec):
+        """One HVP without host synchronisation: returns (H u, E-solve status, residual)."""
+        u = u_vec.reshape(S, 3).to(torch.float32)
+        t_root, full = jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters,
+                                       wave_cache=tcache)
+        dc = full["dcst"]
+        dPi, dPibar = full["dPi"], full["dPibar"]
+        dE, dEbar_e, dE_s1, dE_s2 = full["dE"], full["dEbar"], full["dE_s1"], full["dE_s2"]
+        dpS_m, dpD_m, dpL_m = item(full["dlog_pS"]), item(full["dlog_pD"]), item(full["dlog_pL"])
+        # tangent of the loss seed -softmax2(Pi_root) on the root rows
+        root_Pi = sv["pi_wave"].index_select(0, root_ids)
+        q = _safe_exp2_ratio(root_Pi, logsumexp2(root_Pi, dim=-1, keepdim=True))
+        d_rhs = torch.zeros((C, S), device=theta.device, dtype=torch.float32)
+        d_rhs.index_copy_(0, root_ids, (-LN2 * q * (t_root - (q * t_root).sum(dim=-1, keepdim=True))).float())
+        d_gpD, d_gpS = torch.zeros_like(acc.pD), torch.zeros_like(acc.pS)
+        d_gE, d_gEbar, d_gEs1, d_gEs2 = (torch.zeros_like(E_star) for _ in range(4))
+        d_gmc = torch.zeros_like(acc.mt)
+        d_gcol = torch.zeros((S,), device=theta.device, dtype=torch.float32)
+        for wave in cache["waves"]:  # reverse wave order
+            ws, W, meta = wave["ws"], wave["W"], wave["meta"]
+            v_k, dts_r, active = wave["v"], wave["dts_r"], wave["active_mask"]
+            d_dts = None
+            if dts_r is not None:
+                d_dts = compute_dts_tangent(
+                    sv["pi_wave"], sv["pibar_wave"], dPi, dPibar, meta["sl"], meta["sr"], c1, c2, W,
+                    meta["reduce_idx"], cst["pd_param"], cst["ps_param"], dc["dpd_param"], dc["dps_param"],
+                    dts_r, item_idx, log_split_probs=meta.get("log_split_probs"), item_offset=ws,
+                    csr=tcache[ws]["csr"])
+            has_leaf = wave["has_leaf_term"]
+            # (a) second-order contraction at the fixed v_k, the wave's d_rhs folded in: the seed
+            d_Av, *c_aw = wave_backward_so(
+                sv["pi_wave"], dPi, sv["pibar_wave"], dPibar, v_k, ws, W, S, prm, cst["mc"], cst["dl"],
+                dc["dDL"], cst["ebar"], dc["dEbar"], cst["e"], dc["dE"], cst["sl1"], dc["dSL1"], cst["sl2"],
+                dc["dSL2"], col, c1, c2, parent, mad, dts_r, d_dts, leaf_state_idx=leaf_state,
+                leaf_logp=cst["leaf"], dleaf_logp=dc["dleaf"], item_idx=item_idx, has_leaf_term=has_leaf,
+                use_col_weights=False, d_rhs=d_rhs)
+            # (b) the tangent adjoint: the same solve and mask, seeded with it
+            dv, *l_aw = wave_backward_uniform_fused(
+                sv["pi_wave"], sv["pibar_wave"], ws, W, S, dts_r, d_Av, cst["mc"], cst["dl"], cst["ebar"],
+                cst["e"], cst["sl1"], cst["sl2"], col, c1, c2, None, neumann_terms=int(so.neumann_terms),
+                leaf_state_idx=leaf_state, leaf_logp=cst["leaf"], has_leaf_term=has_leaf, active_mask=active,
+                node_parent=parent, max_ancestor_depth=mad, pibar_row_max=prm, item_idx=item_idx,
+                item_indexed_consts=True, **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
+                self_loop_solver=so.self_loop_solver)
+            # column sums of aw0, aw1, aw2, aw345, aw3, aw4 (contraction + solve parts) in one pass
+            aw = (torch.stack(c_aw) + torch.stack(l_aw)).sum(dim=1)
+            d_gpD[0] += aw[0]
+            d_gpS[0] += aw[3]
+            d_gE[0] += aw[0] + aw[2]
+            d_gEbar[0] += aw[1]
+            d_gEs1[0] += aw[5]
+            d_gEs2[0] += aw[4]
+            d_gmc[0] += aw[2]
+            if dts_r is not None:
+                gl, gr, side, _, _ = dts_cross_backward_accum_fused(
+                    sv["pi_wave"], sv["pibar_wave"], dv, ws, meta["sl"], meta["sr"], meta["reduce_idx"],
+                    meta["log_split_probs"], cst["pd_param"], cst["ps_param"], c1, c2, d_rhs, S,
+                    active_mask=active, merge_s_term=True, grad_log_pD=d_gpD, grad_log_pS=d_gpS, grad_mt=d_gmc,
+                    accum_param_reductions=True, accum_mt_reduction=True, output_pibar_ud=True,
+                    output_pibar_side_active=True, pibar_side_threshold=so.pibar_side_threshold,
+                    mt_squeezed=cst["mc"], pibar_row_max=prm, skip_inactive_pibar_output_zero=True,
+                    item_idx=item_idx)
+                uniform_cross_pibar_vjp_tree_from_ud_fused(
+                    sv["pi_wave"], col, gl, gr, meta["sl"], meta["sr"], d_rhs, S, active_mask=active,
+                    reduce_idx=meta["reduce_idx"], pibar_row_max=prm, skip_zero_sides=True, side_active=side,
+                    **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
+                    side_active_threshold=so.pibar_side_threshold)
+                dts_backward_so(sv["pi_wave"], dPi, sv["pibar_wave"], dPibar, v_k, ws, meta, S,
+                                cst["pd_param"], cst["ps_param"], dc["dpd_param"], dc["dps_param"], cst["mc"],
+                                dc["dMC"], col, c1, c2, parent, mad, prm, item_idx, d_rhs, d_gpD, d_gpS,
+                                d_gmc, d_gcol, **lv, use_col_weights=False)
+        del dPi, dPibar
+        full.clear()
+        # ---- E side ----
+        x_args = (E_star.contiguous(), E_star.contiguous(), sv["E_s1"], sv["E_s2"], sv["Ebar"], pS_m, pD_m, pL_m,
+                  col.contiguous(), *topo)
+        dx = (dE, dE, dE_s1, dE_s2, dEbar_e, dpS_m, dpD_m, dpL_m, None)
+        zero = torch.zeros_like(E_star)
+        aux_lin = vjp_E(None, d_gEs1, d_gEs2, d_gEbar)[0]
+        so_aux = e_step_backward_so(*x_args, zero, acc.E_s1, acc.E_s2, acc.Ebar, *dx, use_col_weights=False)
+        e2E = torch.exp2(E_star)
+        dnorm = -LN2 * (e2E * dE).mean(dim=-1, keepdim=True)
+        dg_norm = fam_factor * (-LN2 * e2E * dE / (S * norm) + e2E * dnorm / (S * norm * norm))
+        dq_E = d_gE + aux_lin + so_aux[0] + dg_norm
+        so_w = e_step_backward_so(*x_args, wE, zero, zero, zero, *dx, use_col_weights=False)
+        rhs_E = dq_E + so_w[0]
+        zs = torch.zeros((S,), device=theta.device, dtype=torch.float32)
+        dwE, _, status, rel = e_adjoint_solve(
+            E_star, sv["log_pS"], sv["log_pD"], sv["log_pL"], sv["max_coupling"], col, *topo, rhs_E.reshape(-1),
+            zs, zs, zs, n_fam=0.0, max_iter=so.bicgstab_max_iter, tol=float(so.bicgstab_tol),
+            breakdown_tol=so.bicgstab_breakdown_tol, use_col_weights=False, check=False)
+        dwE = dwE.reshape(E_star.shape)
+        if debug_out is not None:
+            debug_out.update(d_gE=d_gE.clone(), d_gpD=d_gpD.clone(), d_gpS=d_gpS.clone(), d_gmc=d_gmc.clone(),
+                             d_gEbar=d_gEbar.clone(), d_gEs1=d_gEs1.clone(), d_gEs2=d_gEs2.clone(),
+                             dq_E=dq_E.clone(), dwE=dwE.clone())
+        lin_p = vjp_E(dwE, None, None, d_gEbar)[1:]
+        so_p = e_step_backward_so(*x_args, wE, zero, zero, acc.Ebar, *dx, use_col_weights=False)
+        d_cot_pS = d_gpS + as_item_param(lin_p[0] + so_p[1], G, S)
+        d_cot_pD = d_gpD + as_item_param(lin_p[1] + so_p[2], G, S)
+        d_cot_pL = lin_p[2] + so_p[3]
+        d_cot_mc = d_gmc + lin_p[3] + so_p[4]
+        d_cot_col = d_gcol + lin_p[4] + so_p[5]
+        if closed:
+            # head: H_phi1 u (primal cotangents) + J^T d_cot (tangent cotangents), theta rows only
+            g = torch.stack([d_cot_pS.reshape(S), d_cot_pD.reshape(S), d_cot_pL.reshape(S), d_cot_mc.reshape(S)],
+                            dim=1)
+            lin = g[:, 1:] - p_ev * g.sum(dim=1, keepdim=True)
+            pu = p_ev * u
+            head = -LN2 * c_sum * (pu - p_ev * pu.sum(dim=1, keepdim=True))
+            return (lin + head).reshape(-1), status, rel
         with torch.enable_grad():
             phi2 = ((pS_hp * d_cot_pS).sum() + (pD_hp * d_cot_pD).sum() + (pL_hi * d_cot_pL).sum()
                     + (mt_hi * d_cot_mc).sum() + (col_h * d_cot_col).sum())
             (out,) = torch.autograd.grad((g1 * u).sum() + phi2, theta_req, retain_graph=True)
-        return out.reshape(-1)
+        return out.reshape(-1), status, rel
 
-    return hvp
+    if not graph:
+        def hvp(u_vec):
+            out, status, rel = body(u_vec)
+            e_adjoint_check(status, rel)
+            return out
+        return hvp
+
+    state: dict = {}
+
+    def hvp_graph(u_vec):
+        if "graph" not in state:
+            u_static = torch.zeros((3 * S,), device=theta.device, dtype=torch.float32)
+            u_static.copy_(u_vec.reshape(-1))
+            side = torch.cuda.Stream(device=theta.device)
+            side.wait_stream(torch.cuda.current_stream(theta.device))
+            with torch.cuda.stream(side):  # warm every lazy allocation and table outside the capture
+                for _ in range(2):
+                    body(u_static)
+            torch.cuda.current_stream(theta.device).wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            n0 = sum(_lib.LAUNCHES.values())
+            with torch.cuda.graph(g):
+                out, status, rel = body(u_static)
+            n_kernels = sum(_lib.LAUNCHES.values()) - n0  # this library's kernels in one replay
+            state.update(graph=g, u=u_static, out=out, status=status, rel=rel, n=n_kernels)
+        state["u"].copy_(u_vec.reshape(-1))
+        state["graph"].replay()
+        _lib.LAUNCHES["hvp graph replay"] = _lib.LAUNCHES.get("hvp graph replay", 0) + state["n"]
+        e_adjoint_check(state["status"], state["rel"])
+        return state["out"].clone()
+
+    return hvp_graph

@@ -57,21 +57,32 @@ class _TritonEStep2D(torch.autograd.Function):
     def backward(ctx, grad_E_new, grad_E_s1_out, grad_E_s2_out, grad_Ebar_out):
         (E, E_new, E_s1, E_s2, Ebar, log_pS_mat, log_pD_mat, log_pL_mat, col_log_probs, node_parent,
          node_child1, node_child2) = ctx.saved_tensors
-        G, S = int(E.shape[0]), int(E.shape[1])
-        tt = tree.tables(node_parent, node_child1, node_child2, ctx.max_ancestor_depth)
-        gs = [None if g is None else f32(g) for g in (grad_E_new, grad_E_s1_out, grad_E_s2_out, grad_Ebar_out)]
-        grad_E, grad_pS, grad_pD, grad_pL, grad_mc = (torch.empty_like(E) for _ in range(5))
-        grad_col = torch.empty_like(col_log_probs)
-        pS, pD, pL = (rows_of(t, G, S) for t in (log_pS_mat, log_pD_mat, log_pL_mat))
-        _lib.call("kb_e_step_vjp", E.data_ptr(), E_new.data_ptr(), E_s1.data_ptr(), E_s2.data_ptr(),
-                  Ebar.data_ptr(), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(),
-                  f32(col_log_probs).data_ptr(), tt.parent.data_ptr(), tt.child1.data_ptr(),
-                  tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K, tt.lv_ptr.data_ptr(), tt.n_levels,
-                  tt.lv_par.data_ptr(), tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(),
-                  *[_lib.ptr(g) for g in gs], grad_E.data_ptr(), grad_pS.data_ptr(), grad_pD.data_ptr(),
-                  grad_pL.data_ptr(), grad_mc.data_ptr(), grad_col.data_ptr(), S, G,
-                  int(ctx.use_col_weights), _lib.stream_handle(E.device))
-        return (grad_E, grad_pS, grad_pD, grad_pL, grad_mc, grad_col, None, None, None, None, None)
+        grads = e_step_vjp(E, E_new, E_s1, E_s2, Ebar, log_pS_mat, log_pD_mat, log_pL_mat, col_log_probs,
+                           node_parent, node_child1, node_child2, ctx.max_ancestor_depth, grad_E_new,
+                           grad_E_s1_out, grad_E_s2_out, grad_Ebar_out, use_col_weights=ctx.use_col_weights)
+        return (*grads, None, None, None, None, None)
+
+
+def e_step_vjp(E, E_new, E_s1, E_s2, Ebar, log_pS, log_pD, log_pL, col_log_probs, node_parent, node_child1,
+               node_child2, max_ancestor_depth, g_new, g_s1, g_s2, g_ebar, *, use_col_weights=True):
+    """The VJP of one E application (``_TritonEStep2D.backward``, reference ``e_step.py:325-409``)
+    at saved forward values, as one call: returns (grad_E, grad_pS, grad_pD, grad_pL, grad_mc,
+    grad_col); ``g_*`` may be None (zero cotangent)."""
+    E = f32(E)
+    G, S = int(E.shape[0]), int(E.shape[1])
+    tt = tree.tables(node_parent, node_child1, node_child2, int(max_ancestor_depth))
+    gs = [None if g is None else f32(g) for g in (g_new, g_s1, g_s2, g_ebar)]
+    grad_E, grad_pS, grad_pD, grad_pL, grad_mc = (torch.empty_like(E) for _ in range(5))
+    grad_col = torch.empty_like(col_log_probs)
+    pS, pD, pL = (rows_of(t, G, S) for t in (log_pS, log_pD, log_pL))
+    _lib.call("kb_e_step_vjp", E.data_ptr(), f32(E_new).data_ptr(), f32(E_s1).data_ptr(), f32(E_s2).data_ptr(),
+              f32(Ebar).data_ptr(), pS.data_ptr(), pD.data_ptr(), pL.data_ptr(), f32(col_log_probs).data_ptr(),
+              tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K,
+              tt.lv_ptr.data_ptr(), tt.n_levels, tt.lv_par.data_ptr(), tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(),
+              *[_lib.ptr(g) for g in gs], grad_E.data_ptr(), grad_pS.data_ptr(), grad_pD.data_ptr(),
+              grad_pL.data_ptr(), grad_mc.data_ptr(), grad_col.data_ptr(), S, G, int(bool(use_col_weights)),
+              _lib.stream_handle(E.device))
+    return grad_E, grad_pS, grad_pD, grad_pL, grad_mc, grad_col
 
 
 def e_step_triton_autograd(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
@@ -128,7 +139,7 @@ KB_EADJ_WORK_VECTORS = 17  # include/kb_solver.h
 
 def e_adjoint_solve(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node_parent, node_child1,
                     node_child2, max_ancestor_depth, g_E, g_Ebar, g_E_s1, g_E_s2, *, n_fam, max_iter=500,
-                    tol=1e-7, breakdown_tol=1e-30, use_col_weights=True):
+                    tol=1e-7, breakdown_tol=1e-30, use_col_weights=True, check=True):
     """The E adjoint of ONE shared row (reference ``_implicit_grad.py:373-475``) in one launch:
     ``q = g_E + d/dE[n_fam log2(1 - mean 2^E)] + VJP(g_E_s1, g_E_s2, g_Ebar)``, BiCGSTAB on
     ``(I - J_E^T) w = q`` with the stopping and breakdown rules of ``_implicit_grad.py:28-94``,
@@ -136,7 +147,9 @@ def e_adjoint_solve(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node
 
     Returns ``(w [1,S], grad_params [5,S])`` -- the cotangents of ``(log_pS, log_pD, log_pL,
     max_coupling, col_log_probs)`` through the E step (the Ebar cotangent ``g_Ebar`` included).
-    Raises ``RuntimeError`` (the reference's message) when the solve does not converge."""
+    Raises ``RuntimeError`` (the reference's message) when the solve does not converge.  With
+    ``check=False`` nothing is read back (no host synchronisation, e.g. inside a CUDA graph): returns
+    ``(w, grad_params, status [2] int32, rel [1])`` and :func:`e_adjoint_check` raises later."""
     max_iter, tol, breakdown_tol = int(max_iter), float(tol), float(breakdown_tol)
     if max_iter < 1:
         raise ValueError("max_iter must be at least 1")
@@ -165,9 +178,17 @@ def e_adjoint_solve(E, log_pS, log_pD, log_pL, max_coupling, col_log_probs, node
               tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(), *[g.data_ptr() for g in gs], float(n_fam), max_iter,
               tol, breakdown_tol, work.data_ptr(), w.data_ptr(), grad_params.data_ptr(), status.data_ptr(),
               rel.data_ptr(), S, int(bool(use_col_weights)), _lib.stream_handle(dev))
+    if not check:
+        return w, grad_params, status, rel
+    e_adjoint_check(status, rel)
+    return w, grad_params
+
+
+def e_adjoint_check(status, rel):
+    """Raise the reference's ``RuntimeError`` when a :func:`e_adjoint_solve` did not converge
+    (reads its status words: one host synchronisation)."""
     code, iters = status.tolist()
     e_adjoint_solve.last_iters = iters
     if code != 0:
         raise RuntimeError(f"E-adjoint BiCGSTAB solve failed after {iters} iterations "
                            f"(relative residual {float(rel.item()):.3e})")
-    return w, grad_params

@@ -140,3 +140,19 @@ def test_second_order_kernels_vs_oracle(name, cuda):
                                row(raw["dEbar"]), row(raw["dlog_pS"]), row(raw["dlog_pD"]), row(raw["dlog_pL"]), None)
     for nm, g, r in zip(("d_grad_E", "d_grad_pS", "d_grad_pD", "d_grad_pL", "d_grad_mc", "d_grad_col"), got_e, ref_e):
         close_vec(f"e_step_so {nm}", g.cpu().numpy(), r)
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_hvp_cuda_graph_replays_match(name, cuda):
+    """graph=True: one HVP captured into a CUDA graph and replayed per direction gives the same H u
+    as the eager driver, for each direction in turn (the captured input buffer is refreshed)."""
+    from kbench_b200.hvp import make_exact_hvp
+    cap, out = load_golden(name)
+    hv = dict(np.load(GOLDEN / "hvp" / f"{name}.npz"))
+    static, theta, cw, sv = _gpu_problem(cap, out, cuda)
+    eager = make_exact_hvp(static, theta, cw, sv)
+    graphed = make_exact_hvp(static, theta, cw, sv, graph=True)
+    for k in (0, 1, 0):
+        u = torch.from_numpy(hv[f"u{k}"]).to(cuda)
+        close_vec(f"graph Hu[{k}]", graphed(u).cpu().numpy(), eager(u).cpu().numpy())
+        close_vec(f"graph Hu[{k}] vs reference", graphed(u).cpu().numpy(), hv[f"hu{k}"])
