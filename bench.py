@@ -345,9 +345,39 @@ def hvp_arm(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def reference_hvp_arm(args, world):
+    """--impl reference --hvp: the oracle port of ``newton/hvp_exact.py`` on the host cores (one
+    HVP per step on a bounded sample of the --hvp-config family, extrapolated per row)."""
+    from kbench_b200 import gen
+    cfg = int(args.hvp_config)
+    full = gen.generate(cfg, as_torch=False)["meta"]
+    C, S = int(full["C"]), int(full["S"])
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt, rows = hvp_oracle_sample(cfg, seed=77, n_genes=24)
+        if i >= args.warmup:
+            times.append(dt * C / rows)
+    step_s = statistics.median(times)
+    value = 1.0 / step_s
+    sample = (f"numpy oracle HVP of a {rows}-row family on the config-{cfg} species tree (S={S}), "
+              f"extrapolated per row to C={C}")
+    print(json.dumps({
+        "metric": f"exact-Hessian HVPs/sec (newton/hvp_exact.py, config {cfg}: S={S}, C={C})", "value": value,
+        "unit": "HVPs/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded generator)", "impl": "reference",
+        "config": {"workload": f"config{cfg} HVP, CPU sample", "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": "HVPs/s", "cores": 1, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "HVPs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def reference_arm(args, world, rank):
     """--impl reference: the oracle port of the reference algorithm on the host cores."""
     if rank != 0:
+        return
+    if args.hvp:
+        reference_hvp_arm(args, world)
         return
     from kbench_b200 import gen
     batched = args.config == 4
