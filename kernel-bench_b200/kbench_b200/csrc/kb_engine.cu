@@ -685,27 +685,33 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
       kD[k] = s < S ? __ldg(c.log_pD + pb + s) : 0.f;
       kS[k] = s < S ? __ldg(c.log_pS + pb + s) : 0.f;
     }
-    const float *cPl, *cPr, *cBl, *cBr;
+    // Pi rows are staged (the speciation terms gather them at the children's columns); Pibar rows
+    // are only read at the own column and come straight from global memory
+    const float *cPl, *cPr;
     {
       const long long l = a.sp.sl[i0], r = a.sp.sr[i0];
       cPl = stage_row_cg(stg, a.Pi_src + (size_t)l * S, S, NTV, true);
       cPr = stage_row_cg(stg + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
-      cBl = stage_row_cg(stg + 2 * RS, a.Pibar_src + (size_t)l * S, S, NTV, false);
-      cBr = stage_row_cg(stg + 3 * RS, a.Pibar_src + (size_t)r * S, S, NTV, false);
       cp_async_commit();
     }
     for (long long i = i0; i < i1; ++i) {
       const int par = (int)((i - i0) & 1);
+      const long long li = a.sp.sl[i], ri = a.sp.sr[i];
+      float bl[VF], br[VF];  // issued before the wait: their latency overlaps it
+#pragma unroll
+      for (int k = 0; k < VF; ++k) {
+        const int s = tid + k * NT;
+        bl[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)li * S + s) : 0.f;
+        br[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)ri * S + s) : 0.f;
+      }
       cp_async_wait_all();
       __syncthreads();  // split i staged; everyone is done with split i-1's slots
-      const float *nPl = nullptr, *nPr = nullptr, *nBl = nullptr, *nBr = nullptr;
+      const float *nPl = nullptr, *nPr = nullptr;
       if (i + 1 < i1) {
         float* nb = stg + (par ^ 1) * 4 * RS;
         const long long l = a.sp.sl[i + 1], r = a.sp.sr[i + 1];
         nPl = stage_row_cg(nb, a.Pi_src + (size_t)l * S, S, NTV, true);
         nPr = stage_row_cg(nb + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
-        nBl = stage_row_cg(nb + 2 * RS, a.Pibar_src + (size_t)l * S, S, NTV, false);
-        nBr = stage_row_cg(nb + 3 * RS, a.Pibar_src + (size_t)r * S, S, NTV, false);
         cp_async_commit();
       }
       const float lsp = a.sp.lsp[i];
@@ -719,8 +725,8 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
           // magnitudes ~1e2 a different association moves the terms by an ulp (~1e-5)
           const float lss = lsp + kS[k];
           const float v0 = lsp + kD[k] + pl + pr;
-          const float v1 = lsp + pl + cBr[s];
-          const float v2 = lsp + pr + cBl[s];
+          const float v1 = lsp + pl + br[k];
+          const float v2 = lsp + pr + bl[k];
           const float v3 = lss + cPl[ca] + cPr[cbb];
           const float v4 = lss + cPr[ca] + cPl[cbb];
           const float mx = fmaxf(fmaxf(fmaxf(m[k], v0), fmaxf(v1, v2)), fmaxf(v3, v4));
@@ -730,7 +736,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
           m[k] = mx;
         }
       }
-      cPl = nPl; cPr = nPr; cBl = nBl; cBr = nBr;
+      cPl = nPl; cPr = nPr;
     }
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
