@@ -627,6 +627,83 @@ __device__ __forceinline__ const float* stage_row_cg(float* B, const float* src,
   return P;
 }
 
+// ---- bulk (TMA) row copies into shared memory, completion counted on an mbarrier ----
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Split staging of the dataflow forward: the aligned middle of each child Pi row arrives by one
+// bulk copy (issued by thread 0, counted on the buffer's mbarrier), the unaligned ends and the
+// padding by plain loads.  Every thread tracks the parity of each buffer's next completion.
+struct BulkStage {
+  unsigned long long* bar;  // [2] mbarriers (one per staging buffer), shared memory
+  unsigned phase;           // bit b: parity of bar[b]'s next completion
+  int* error;               // set when a wait gives up
+  long long max_polls;
+};
+
+// Stage rows s0 and s1 (S floats each) into slots B0 / B1 (NTV + 4 floats each), -inf padding to
+// NTV; returns the aligned views.  Called by all threads after the slots' previous readers are
+// done (a barrier); completion: bulk_wait on the same mbarrier, then a barrier.
+__device__ __forceinline__ void stage_rows_bulk(float* B0, const float* s0, float* B1, const float* s1, int S,
+                                                int NTV, unsigned long long* bar, const float** v0,
+                                                const float** v1) {
+  const int a0 = (int)(((16u - ((unsigned)(uintptr_t)s0 & 15u)) & 15u) >> 2);
+  const int a1 = (int)(((16u - ((unsigned)(uintptr_t)s1 & 15u)) & 15u) >> 2);
+  float* P0 = B0 + ((4 - a0) & 3);
+  float* P1 = B1 + ((4 - a1) & 3);
+  const int nb0 = S > a0 ? (S - a0) >> 2 : 0, nb1 = S > a1 ? (S - a1) >> 2 : 0;
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slots' previous readers
+    mbar_arrive_expect_tx(bar, (unsigned)(16 * (nb0 + nb1)));
+    if (nb0) bulk_copy_g2s(P0 + a0, s0 + a0, (unsigned)(16 * nb0), bar);
+    if (nb1) bulk_copy_g2s(P1 + a1, s1 + a1, (unsigned)(16 * nb1), bar);
+  }
+  const int h0 = a0 < S ? a0 : S, h1 = a1 < S ? a1 : S;
+  for (int s = threadIdx.x; s < h0; s += blockDim.x) P0[s] = __ldcg(s0 + s);
+  for (int s = threadIdx.x; s < h1; s += blockDim.x) P1[s] = __ldcg(s1 + s);
+  for (int s = h0 + 4 * nb0 + threadIdx.x; s < S; s += blockDim.x) P0[s] = __ldcg(s0 + s);
+  for (int s = h1 + 4 * nb1 + threadIdx.x; s < S; s += blockDim.x) P1[s] = __ldcg(s1 + s);
+  for (int s = S + threadIdx.x; s < NTV; s += blockDim.x) {
+    P0[s] = neg_inf();
+    P1[s] = neg_inf();
+  }
+  *v0 = P0;
+  *v1 = P1;
+}
+
+__device__ __forceinline__ void bulk_wait(BulkStage& bs, int b) {
+  const unsigned parity = (bs.phase >> b) & 1u;
+  long long polls = 0;
+  while (!mbar_try_wait(bs.bar + b, parity)) {
+    if (++polls > bs.max_polls) {  // cannot happen with valid copies; results flagged invalid
+      if (bs.error) atomicExch(bs.error, 1);
+      break;
+    }
+  }
+  bs.phase ^= 1u << b;
+}
+
 // Loads of rows that other CTAs of the SAME launch produce (the dataflow schedule) bypass L1:
 // L1 is not coherent across SMs, and a row's first and last cache lines are shared with its
 // neighbours.  Level launches keep the cached / asynchronous paths.
@@ -641,7 +718,7 @@ __device__ __forceinline__ float ld_row(const float* p) {
 // Splits [i0, i1) of the split arrays; sm: the CTA's dynamic shared memory.
 template <int VF, bool DF>
 __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long row, long long i0, long long i1,
-                                                 float* sm) {
+                                                 float* sm, BulkStage* bs = nullptr) {
   const FwdArgs& a = args.f;
   const LevelConsts& c = a.c;
   const unsigned* __restrict__ tb = args.tb;
@@ -688,11 +765,17 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     // Pi rows are staged (the speciation terms gather them at the children's columns); Pibar rows
     // are only read at the own column and come straight from global memory
     const float *cPl, *cPr;
+    const bool bulk = DF && bs != nullptr;
     {
       const long long l = a.sp.sl[i0], r = a.sp.sr[i0];
-      cPl = stage_row_cg(stg, a.Pi_src + (size_t)l * S, S, NTV, true);
-      cPr = stage_row_cg(stg + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
-      cp_async_commit();
+      if (bulk) {
+        stage_rows_bulk(stg, a.Pi_src + (size_t)l * S, stg + RS, a.Pi_src + (size_t)r * S, S, NTV, bs->bar, &cPl,
+                        &cPr);
+      } else {
+        cPl = stage_row_cg(stg, a.Pi_src + (size_t)l * S, S, NTV, true);
+        cPr = stage_row_cg(stg + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
+        cp_async_commit();
+      }
     }
     for (long long i = i0; i < i1; ++i) {
       const int par = (int)((i - i0) & 1);
@@ -704,15 +787,21 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
         bl[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)li * S + s) : 0.f;
         br[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)ri * S + s) : 0.f;
       }
-      cp_async_wait_all();
+      if (bulk) bulk_wait(*bs, par);
+      else cp_async_wait_all();
       __syncthreads();  // split i staged; everyone is done with split i-1's slots
       const float *nPl = nullptr, *nPr = nullptr;
       if (i + 1 < i1) {
         float* nb = stg + (par ^ 1) * 4 * RS;
         const long long l = a.sp.sl[i + 1], r = a.sp.sr[i + 1];
-        nPl = stage_row_cg(nb, a.Pi_src + (size_t)l * S, S, NTV, true);
-        nPr = stage_row_cg(nb + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
-        cp_async_commit();
+        if (bulk) {
+          stage_rows_bulk(nb, a.Pi_src + (size_t)l * S, nb + RS, a.Pi_src + (size_t)r * S, S, NTV,
+                          bs->bar + (par ^ 1), &nPl, &nPr);
+        } else {
+          nPl = stage_row_cg(nb, a.Pi_src + (size_t)l * S, S, NTV, true);
+          nPr = stage_row_cg(nb + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
+          cp_async_commit();
+        }
       }
       const float lsp = a.sp.lsp[i];
 #pragma unroll
@@ -1002,11 +1091,19 @@ template <int VF>
 __global__ void __launch_bounds__(512, 1) flow_forward_kernel(Fwd4Args args, Flow f) {
   extern __shared__ __align__(16) float sm[];
   __shared__ FlowSlot fs;
-  if (threadIdx.x == 0) fs.next = -1;
+  __shared__ __align__(8) unsigned long long bars[2];
+  if (threadIdx.x == 0) {
+    fs.next = -1;
+    mbar_init(bars, 1);
+    mbar_init(bars + 1, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  BulkStage bs{bars, 0u, f.error, f.max_polls};
   for (;;) {
     const int row = flow_next_row(f, &fs);
     if (row < 0) break;
-    forward_tour_row<VF, true>(args, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], sm);
+    forward_tour_row<VF, true>(args, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], sm, &bs);
     flow_finish_row(f, row, &fs);
   }
 }
