@@ -662,19 +662,22 @@ struct BulkStage {
   long long max_polls;
 };
 
-// Stage rows s0 and s1 (S floats each) into slots B0 / B1 (NTV + 4 floats each), -inf padding to
-// NTV; returns the aligned views.  Called by all threads after the slots' previous readers are
-// done (a barrier); completion: bulk_wait on the same mbarrier, then a barrier.
+// Stage rows s0 and s1 (S floats each) into slots B0 / B1 (NTV + 4 floats each), padded with
+// `pad` up to NTV; returns the aligned views.  Called by all threads after the slots' previous
+// readers are done (a barrier); one arrival on `bar` (with the copies' byte count) per call;
+// completion: bulk_wait on the same mbarrier, then a barrier.
 __device__ __forceinline__ void stage_rows_bulk(float* B0, const float* s0, float* B1, const float* s1, int S,
                                                 int NTV, unsigned long long* bar, const float** v0,
-                                                const float** v1) {
+                                                const float** v1, float pad = neg_inf()) {
   const int a0 = (int)(((16u - ((unsigned)(uintptr_t)s0 & 15u)) & 15u) >> 2);
   const int a1 = (int)(((16u - ((unsigned)(uintptr_t)s1 & 15u)) & 15u) >> 2);
   float* P0 = B0 + ((4 - a0) & 3);
   float* P1 = B1 + ((4 - a1) & 3);
   const int nb0 = S > a0 ? (S - a0) >> 2 : 0, nb1 = S > a1 ? (S - a1) >> 2 : 0;
   if (threadIdx.x == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slots' previous readers
+    // generic-proxy accesses before -> this thread's bulk copies: the slots' previous readers, and
+    // the child rows other CTAs wrote (made visible to this thread by the queue's acquire)
+    asm volatile("fence.proxy.async;" ::: "memory");
     mbar_arrive_expect_tx(bar, (unsigned)(16 * (nb0 + nb1)));
     if (nb0) bulk_copy_g2s(P0 + a0, s0 + a0, (unsigned)(16 * nb0), bar);
     if (nb1) bulk_copy_g2s(P1 + a1, s1 + a1, (unsigned)(16 * nb1), bar);
@@ -685,8 +688,8 @@ __device__ __forceinline__ void stage_rows_bulk(float* B0, const float* s0, floa
   for (int s = h0 + 4 * nb0 + threadIdx.x; s < S; s += blockDim.x) P0[s] = __ldcg(s0 + s);
   for (int s = h1 + 4 * nb1 + threadIdx.x; s < S; s += blockDim.x) P1[s] = __ldcg(s1 + s);
   for (int s = S + threadIdx.x; s < NTV; s += blockDim.x) {
-    P0[s] = neg_inf();
-    P1[s] = neg_inf();
+    P0[s] = pad;
+    P1[s] = pad;
   }
   *v0 = P0;
   *v1 = P1;
@@ -1444,7 +1447,7 @@ __device__ __forceinline__ float2& pair_at(float2* base, unsigned off) {
 // level_tangent_kernel.
 template <int VF, bool DF>
 __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row, long long i0, long long i1, int d0,
-                                                 float* sm) {
+                                                 float* sm, BulkStage* bs = nullptr) {
   const unsigned* __restrict__ tb = a.tb;
   const unsigned* __restrict__ tp = a.tb2;
   const int S = a.S;
@@ -1561,17 +1564,30 @@ __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row
       const long long l = a.sp.sl[i], rr = a.sp.sr[i];
       const float lsp = a.sp.lsp[i];
       __syncthreads();
+      const float *vPl = Pl, *vPr = Pr, *vQla = Qla, *vQra = Qra, *vQlb = Qlb, *vQrb = Qrb;
+      if (bs) {
+        // bulk copies of the six child rows (three arrivals on the split barrier); the tangent
+        // rows are written by other CTAs of this launch, which a bulk copy reads through L2
+        const size_t ol = (size_t)l * S, orr = (size_t)rr * S;
+        const int RS = NTV + 4;
+        float* b = sm;
+        stage_rows_bulk(b, a.Pi + ol, b + RS, a.Pi + orr, S, NTV, bs->bar, &vPl, &vPr);
+        stage_rows_bulk(b + 2 * RS, dPa + ol, b + 3 * RS, dPa + orr, S, NTV, bs->bar, &vQla, &vQra, 0.f);
+        stage_rows_bulk(b + 4 * RS, dPb + ol, b + 5 * RS, dPb + orr, S, NTV, bs->bar, &vQlb, &vQrb, 0.f);
+        bulk_wait(*bs, 0);
+      } else {
 #pragma unroll
-      for (int k = 0; k < VF; ++k) {
-        const int s = tid + k * NT;
-        const bool real = s < S;
-        const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
-        Pl[s] = real ? a.Pi[ol] : neg_inf();
-        Pr[s] = real ? a.Pi[orr] : neg_inf();
-        Qla[s] = real ? (DF ? __ldcg(dPa + ol) : dPa[ol]) : 0.f;  // DF: children written in this launch
-        Qra[s] = real ? (DF ? __ldcg(dPa + orr) : dPa[orr]) : 0.f;
-        Qlb[s] = real ? (DF ? __ldcg(dPb + ol) : dPb[ol]) : 0.f;
-        Qrb[s] = real ? (DF ? __ldcg(dPb + orr) : dPb[orr]) : 0.f;
+        for (int k = 0; k < VF; ++k) {
+          const int s = tid + k * NT;
+          const bool real = s < S;
+          const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
+          Pl[s] = real ? a.Pi[ol] : neg_inf();
+          Pr[s] = real ? a.Pi[orr] : neg_inf();
+          Qla[s] = real ? (DF ? __ldcg(dPa + ol) : dPa[ol]) : 0.f;  // DF: children written in this launch
+          Qra[s] = real ? (DF ? __ldcg(dPa + orr) : dPa[orr]) : 0.f;
+          Qlb[s] = real ? (DF ? __ldcg(dPb + ol) : dPb[ol]) : 0.f;
+          Qrb[s] = real ? (DF ? __ldcg(dPb + orr) : dPb[orr]) : 0.f;
+        }
       }
       __syncthreads();
 #pragma unroll
@@ -1581,21 +1597,21 @@ __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row
         if (!is_neg_inf(dts)) {
           const unsigned ca = ccol[k] & 0xFFFFu, cbb = ccol[k] >> 16;
           const float ld = __ldg(a.log_pD + pb + s), ls = __ldg(a.log_pS + pb + s);
-          const float pl = Pl[s], pr = Pr[s];
+          const float pl = vPl[s], pr = vPr[s];
           const float w0 = ex2(lsp + ld + pl + pr - dts);
           const float w1 = ex2(lsp + pl + a.Pibar[(size_t)rr * S + s] - dts);
           const float w2 = ex2(lsp + pr + a.Pibar[(size_t)l * S + s] - dts);
-          const float w3 = ex2(lsp + ls + Pl[ca] + Pr[cbb] - dts);
-          const float w4 = ex2(lsp + ls + Pr[ca] + Pl[cbb] - dts);
+          const float w3 = ex2(lsp + ls + vPl[ca] + vPr[cbb] - dts);
+          const float w4 = ex2(lsp + ls + vPr[ca] + vPl[cbb] - dts);
           const size_t ol = (size_t)l * S + s, orr = (size_t)rr * S + s;
           const float bar_a = DF ? __ldcg(dBa + orr) : dBa[orr], bal_a = DF ? __ldcg(dBa + ol) : dBa[ol];
           const float bar_b = DF ? __ldcg(dBb + orr) : dBb[orr], bal_b = DF ? __ldcg(dBb + ol) : dBb[ol];
-          const float xa = w0 * (a.dpD[tofa + pb + s] + Qla[s] + Qra[s]) + w1 * (Qla[s] + bar_a) +
-                           w2 * (Qra[s] + bal_a) + w3 * (a.dpS[tofa + pb + s] + Qla[ca] + Qra[cbb]) +
-                           w4 * (a.dpS[tofa + pb + s] + Qra[ca] + Qla[cbb]);
-          const float xb = w0 * (a.dpD[tofb + pb + s] + Qlb[s] + Qrb[s]) + w1 * (Qlb[s] + bar_b) +
-                           w2 * (Qrb[s] + bal_b) + w3 * (a.dpS[tofb + pb + s] + Qlb[ca] + Qrb[cbb]) +
-                           w4 * (a.dpS[tofb + pb + s] + Qrb[ca] + Qlb[cbb]);
+          const float xa = w0 * (a.dpD[tofa + pb + s] + vQla[s] + vQra[s]) + w1 * (vQla[s] + bar_a) +
+                           w2 * (vQra[s] + bal_a) + w3 * (a.dpS[tofa + pb + s] + vQla[ca] + vQra[cbb]) +
+                           w4 * (a.dpS[tofa + pb + s] + vQra[ca] + vQla[cbb]);
+          const float xb = w0 * (a.dpD[tofb + pb + s] + vQlb[s] + vQrb[s]) + w1 * (vQlb[s] + bar_b) +
+                           w2 * (vQrb[s] + bal_b) + w3 * (a.dpS[tofb + pb + s] + vQlb[ca] + vQrb[cbb]) +
+                           w4 * (a.dpS[tofb + pb + s] + vQrb[ca] + vQlb[cbb]);
           ca_[k] = fmaf(cD[k], xa, ca_[k]);
           cb_[k] = fmaf(cD[k], xb, cb_[k]);
         }
@@ -1697,12 +1713,19 @@ template <int VF>
 __global__ void __launch_bounds__(512, 1) flow_tangent2_kernel(TanArgs a, Flow f) {
   extern __shared__ __align__(16) float sm[];
   __shared__ FlowSlot fs;
-  if (threadIdx.x == 0) fs.next = -1;
+  __shared__ __align__(8) unsigned long long bar;  // the split staging's bulk copies (3 arrivals)
+  if (threadIdx.x == 0) {
+    fs.next = -1;
+    mbar_init(&bar, 3);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  BulkStage bs{&bar, 0u, f.error, f.max_polls};
   for (;;) {
     const int itm = flow_next_row(f, &fs);
     if (itm < 0) break;
     const int pair = itm / f.C, row = itm - pair * f.C;
-    tangent_pair_row<VF, true>(a, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], 2 * pair, sm);
+    tangent_pair_row<VF, true>(a, row, f.row_split_ptr[row], f.row_split_ptr[row + 1], 2 * pair, sm, &bs);
     flow_finish_row(f, itm, &fs);
   }
 }
