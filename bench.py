@@ -36,7 +36,6 @@ import csv
 import datetime
 import io
 import json
-import math
 import os
 import statistics
 import subprocess

@@ -5,7 +5,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib, tree
-from ._common import f32, i32, i64, require_cuda_f32, state_rows
+from ._common import f32, i64, require_cuda_f32, state_rows
 
 
 def _inplace(name, t):

@@ -10,7 +10,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib, tree
-from ._common import f32, i32, require_cuda_f32, rows_of
+from ._common import f32, require_cuda_f32, rows_of
 
 
 def _as_item_state(t, S, G):
