@@ -60,3 +60,26 @@ def test_oracle_hvp_is_symmetric(name):
     a, b = float(u1 @ h0), float(u0 @ h1)
     scale = np.linalg.norm(h0) * np.linalg.norm(u1) + np.linalg.norm(h1) * np.linalg.norm(u0)
     assert abs(a - b) <= 1e-4 * scale, (a, b, scale)
+
+
+def test_head_second_order_term_matches_finite_differences():
+    """The closed-form smooth-head Hessian (the GPU driver uses the same formula) against central
+    differences of the extraction's VJP at fixed cotangents."""
+    from oracle import kb_oracle as O
+    cap, st, _ = _case(NAMES[0])
+    tree = O.Tree(st["state_helpers"])
+    S = tree.S
+    rng = np.random.default_rng(3)
+    theta = rng.standard_normal((S, 3))
+    u = rng.standard_normal((S, 3))
+    cot = [rng.standard_normal(S).astype(np.float32) for _ in range(4)]
+    cw = np.zeros(S, np.float32)
+    eps = 1e-3
+
+    def jt(th):
+        g, _ = O.extract_parameters_vjp(th, cw, tree, *cot, np.zeros(S, np.float32), uniform_fast=True)
+        return g.astype(np.float64)
+
+    fd = (jt(theta + eps * u) - jt(theta - eps * u)) / (2 * eps)
+    h = OH.head_hvp(theta, u, cot)
+    assert np.abs(h - fd).max() <= 1e-3 * max(np.abs(fd).max(), 1e-6)
