@@ -54,13 +54,18 @@ def test_hvp_vs_reference_golden(name, cuda):
     assert k >= 1
 
 
-WIDE = gen.ProblemConfig("hvp511", 256, 16, 3, 6, 0, solver_options=dict(gen.CONFIGS[2].solver_options))
+WIDE = {
+    "S511": gen.ProblemConfig("hvp511", 256, 16, 3, 6, 0, solver_options=dict(gen.CONFIGS[2].solver_options)),
+    "S4095": gen.ProblemConfig("hvp4095", 2048, 16, 3, 6, 0, solver_options=dict(gen.CONFIGS[3].solver_options)),
+}
 
 
-def test_hvp_wide_vs_oracle(cuda):
-    """S = 511 (the config-2 species tree width) on a small family, GPU against the oracle."""
+@pytest.mark.parametrize("name", sorted(WIDE))
+def test_hvp_wide_vs_oracle(name, cuda):
+    """The config-2 and config-3 species tree widths on a small family, GPU against the oracle at
+    the oracle's forward state."""
     from kbench_b200.hvp import make_exact_hvp
-    cap = gen.generate(WIDE, seed=515, as_torch=False)
+    cap = gen.generate(WIDE[name], seed=515, as_torch=False)
     st = oracle_static(cap)
     theta, cw = cap["inputs"]["theta"], cap["inputs"]["col_weights"]
     _, saved = O.forward(st, theta, cw)
