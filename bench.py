@@ -173,6 +173,23 @@ def launch_traffic(name, C, S):
     return None if per_row is None or S != 4095 else round(per_row * C)
 
 
+def algorithmic_mufu(C, S, n_splits, pi_iters):
+    """MUFU (ex2 / lg2 / rcp) operations the reference's math performs per pass (its own counting:
+    per element per wave-step call 7 ex2 + 2 lg2 + 1 more pair on the final iteration, per
+    split-element 5 ex2 + 1 lg2 in the forward; per element 14 in the backward's precompute and per
+    split-element 6 + 7 in its dts recompute and cross terms plus 1 per side-element of the Pibar
+    trees).  This kernel replaces most of them by FMAs (linear-space iterations), so the rate below
+    is the reference-equivalent SFU rate, reported beside the HBM fraction."""
+    fwd = C * S * (10 * (pi_iters - 1) + 2) + 6 * n_splits * S
+    bwd = 14 * C * S + 13 * n_splits * S + 2 * n_splits * S
+    return fwd, bwd
+
+
+def mufu_peak_tops(sm_mhz):
+    """Nominal SFU peak: 148 SMs x 16 MUFU results per clock x the sampled max SM clock."""
+    return 148 * 16 * float(sm_mhz) * 1e6 / 1e12
+
+
 def kernel_bytes(name, per, fwd_b, bwd_b):
     """Algorithmic bytes of the launches ``per`` [(level, ms)] of one engine kernel: a level launch
     covers its level, a dataflow launch (kb_flow_*) the whole sweep."""
@@ -816,6 +833,23 @@ def main():
             "avg_launch_ms": k_ms / n_launch,
             "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items() if v > 0},
         }
+        # both candidate bounds per kernel: HBM (algorithmic bytes) and SFU (reference MUFU ops)
+        mf, mb = algorithmic_mufu(C, S, int(plan.n_splits), int(static.solver_options.pi_iters))
+        smx = (clocks or {}).get("sm_max_mhz") or 1965.0
+        mpk = mufu_peak_tops(smx)
+        per_kernel = {}
+        for name, kms in k_tot.items():
+            if kms <= 0 or not name.startswith("kb_flow_"):
+                continue
+            fwd_k = "forward" in name
+            kb = sum((fwd_b if fwd_k else bwd_b).values())
+            ops = mf if fwd_k else mb
+            per_kernel[name] = {"ms": round(kms, 3), "hbm_gbs": round(kb / (kms * 1e-3) / 1e9, 1),
+                                "hbm_frac": round(kb / (kms * 1e-3) / 1e9 / peak, 4),
+                                "sfu_equiv_tops": round(ops / (kms * 1e-3) / 1e12, 3),
+                                "sfu_frac": round(ops / (kms * 1e-3) / 1e12 / mpk, 4)}
+        roofline["per_kernel"] = per_kernel
+        roofline["sfu_peak"] = {"tops": round(mpk, 3), "source": f"nominal: 148 SMs x 16/clk x {smx:.0f} MHz"}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             sps, dt, rows = run_cpu_oracle_sample(C, seed=3000)

@@ -675,9 +675,10 @@ __device__ __forceinline__ void stage_rows_bulk(float* B0, const float* s0, floa
   float* P1 = B1 + ((4 - a1) & 3);
   const int nb0 = S > a0 ? (S - a0) >> 2 : 0, nb1 = S > a1 ? (S - a1) >> 2 : 0;
   if (threadIdx.x == 0) {
-    // generic-proxy accesses before -> this thread's bulk copies: the slots' previous readers, and
-    // the child rows other CTAs wrote (made visible to this thread by the queue's acquire)
-    asm volatile("fence.proxy.async;" ::: "memory");
+    // generic-proxy writes -> this thread's bulk copies: the child rows other CTAs wrote (made
+    // visible to this thread by the queue's acquire).  The slots' previous readers finished before
+    // the caller's barrier, which orders them before any write to the slots.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     mbar_arrive_expect_tx(bar, (unsigned)(16 * (nb0 + nb1)));
     if (nb0) bulk_copy_g2s(P0 + a0, s0 + a0, (unsigned)(16 * nb0), bar);
     if (nb1) bulk_copy_g2s(P1 + a1, s1 + a1, (unsigned)(16 * nb1), bar);
