@@ -1056,7 +1056,7 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, FlowSlot* st) {
           row = -2;
           break;
         }
-        __nanosleep(32);
+        __nanosleep(128);
         row = *q;
       }
       __threadfence();  // the row's children, written before it was queued, are visible
