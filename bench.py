@@ -67,6 +67,10 @@ def parse_args():
     ap.add_argument("--hvp", action="store_true",
                     help="exact-Hessian HVPs/s (newton/hvp_exact.py) on the --hvp-config family")
     ap.add_argument("--hvp-config", type=int, default=2, help="--hvp: the problem config (default 2, S=511)")
+    ap.add_argument("--traffic-case", action="store_true",
+                    help="two forward + backward passes of a reduced config-3 family (the config-3 species tree, "
+                         "2,048 genes: ~12.7k rows, 208 MB per [C,S] buffer), the case the DRAM-traffic capture "
+                         "is taken on")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
@@ -226,6 +230,26 @@ def run_cpu_oracle_sample(full_rows, seed, n_genes=512, species_leaves=2048):
 
 
 HVP_BYTES_PER_ROW_ELEM = 13 * 4
+
+
+def traffic_case(args):
+    """--traffic-case: the reduced config-3 family that the DRAM-traffic ncu capture runs on (a full
+    config-3 launch is too large to capture).  Rows are independent units, so per-row traffic
+    scales to the full family."""
+    import torch
+    from kbench_b200 import engine, gen, runtime
+    cfg = gen.ProblemConfig("traffic", gen.CONFIGS[3].n_species, 2048, 32, 682, 0,
+                            solver_options=dict(gen.CONFIGS[3].solver_options))
+    cap = gen.generate(cfg, seed=3000)
+    static = runtime.make_static(cap, "cuda")
+    theta, cw = cap["inputs"]["theta"].cuda(), cap["inputs"]["col_weights"].cuda()
+    engine.build_plan(static)
+    for _ in range(2):
+        loss, saved = runtime.run_forward(static, theta, cw)
+        runtime.run_backward(static, theta, cw, saved)
+    torch.cuda.synchronize()
+    print(json.dumps({"traffic_case": True, "C": int(cap["meta"]["C"]), "S": int(cap["meta"]["S"]),
+                      "loss": float(loss)}), flush=True)
 
 
 def hvp_oracle_sample(cfg, seed, n_genes):
@@ -707,6 +731,9 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
+    if args.traffic_case:
+        traffic_case(args)
+        return
     if args.hvp:
         hvp_arm(args, world, rank, local)
         return
