@@ -167,8 +167,8 @@ def algorithmic_bytes(plan, S):
 # DRAM bytes per row of the dataflow kernels at S = 4095, from one ncu capture on the config-3
 # species tree with a 12,709-row family (profiles/flow_kernels_dram_traffic.md); rows are
 # independent units, so a full-family launch moves ~C times these.
-TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782593280 + 542440704) / 12709,
-                               "kb_flow_backward": (1968742400 + 787051264) / 12709}
+TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782290944 + 542546688) / 12709,
+                               "kb_flow_backward": (1977673728 + 786529536) / 12709}
 
 
 def launch_traffic(name, C, S):
