@@ -165,8 +165,8 @@ def algorithmic_bytes(plan, S):
 
 
 # DRAM bytes per row of the dataflow kernels at S = 4095, from one ncu capture on the config-3
-# species tree with a 12,709-row family (profiles/flow_kernels_dram_traffic.md); rows are
-# independent units, so a full-family launch moves ~C times these.
+# species tree with a 12,709-row family (the capture runs ``bench.py --traffic-case``); rows
+# are independent units, so a full-family launch moves ~C times these.
 TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782290944 + 542546688) / 12709,
                                "kb_flow_backward": (1977673728 + 786529536) / 12709}
 
@@ -855,7 +855,7 @@ def main():
             "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
             "traffic": launch_traffic(dominant, C, S),
             "traffic_note": "dram__bytes_read+write per launch, scaled by rows from an ncu capture "
-                            "(profiles/flow_kernels_dram_traffic.md)",
+                            "of bench.py --traffic-case (12,709 rows, same species tree)",
             "algorithmic_bytes_per_launch": alg_bytes / n_launch,
             "avg_launch_ms": k_ms / n_launch,
             "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items() if v > 0},
