@@ -68,20 +68,6 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   float r = (lane < nw) ? scratch[lane] : 0.0f;
   return warp_sum(r);
 }
-// Max and sum in one pass (returns both); scratch >= 64 floats.
-__device__ __forceinline__ void block_max_sum(float& m, float& s, float* scratch) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nw = (blockDim.x + 31) >> 5;
-  m = warp_max(m);
-  s = warp_sum(s);
-  __syncthreads();
-  if (lane == 0) { scratch[wid] = m; scratch[32 + wid] = s; }
-  __syncthreads();
-  float mm = (lane < nw) ? scratch[lane] : neg_inf();
-  float ss = (lane < nw) ? scratch[32 + lane] : 0.0f;
-  m = warp_max(mm);
-  s = warp_sum(ss);
-}
 
 // Ancestor-or-self path sum by pointer doubling over precomputed jump tables:
 // after round r, buf[s] holds the sum over the first 2^(r+1) nodes of s's root path.
@@ -122,99 +108,6 @@ __device__ __forceinline__ void subtree_sums_levels(float* buf, const long long*
     __syncthreads();
   }
 }
-
-}  // namespace kb
-
-namespace kb {
-
-// In-place exclusive prefix sums of two shared buffers a[0..n), b[0..n) (each thread owns a
-// contiguous chunk); returns the totals.  tmp must hold 64 floats.  Syncs on entry and exit.
-__device__ __forceinline__ void block_exclusive_scan2(float* a, float* b, int n, float* tmp, float& tot_a,
-                                                      float& tot_b) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int lane = tid & 31, wid = tid >> 5, nw = (nt + 31) >> 5;
-  const int ch = (n + nt - 1) / nt;
-  const int b0 = min(tid * ch, n), b1 = min(b0 + ch, n);
-  __syncthreads();
-  float la = 0.f, lb = 0.f;
-  for (int i = b0; i < b1; ++i) { la += a[i]; lb += b[i]; }
-  float ia = la, ib = lb;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float ya = __shfl_up_sync(0xffffffffu, ia, o);
-    const float yb = __shfl_up_sync(0xffffffffu, ib, o);
-    if (lane >= o) { ia += ya; ib += yb; }
-  }
-  if (lane == 31) { tmp[wid] = ia; tmp[32 + wid] = ib; }
-  __syncthreads();
-  if (wid == 0) {
-    float ta = lane < nw ? tmp[lane] : 0.f;
-    float tb = lane < nw ? tmp[32 + lane] : 0.f;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float ya = __shfl_up_sync(0xffffffffu, ta, o);
-      const float yb = __shfl_up_sync(0xffffffffu, tb, o);
-      if (lane >= o) { ta += ya; tb += yb; }
-    }
-    tmp[lane] = ta;
-    tmp[32 + lane] = tb;
-  }
-  __syncthreads();
-  float ra = (wid > 0 ? tmp[wid - 1] : 0.f) + ia - la;
-  float rb = (wid > 0 ? tmp[32 + wid - 1] : 0.f) + ib - lb;
-  tot_a = tmp[nw - 1];
-  tot_b = tmp[32 + nw - 1];
-  for (int i = b0; i < b1; ++i) {
-    const float va = a[i], vb = b[i];
-    a[i] = ra;
-    b[i] = rb;
-    ra += va;
-    rb += vb;
-  }
-  __syncthreads();
-}
-
-// Single-buffer variant.
-__device__ __forceinline__ float block_exclusive_scan(float* a, int n, float* tmp) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int lane = tid & 31, wid = tid >> 5, nw = (nt + 31) >> 5;
-  const int ch = (n + nt - 1) / nt;
-  const int b0 = min(tid * ch, n), b1 = min(b0 + ch, n);
-  __syncthreads();
-  float la = 0.f;
-  for (int i = b0; i < b1; ++i) la += a[i];
-  float ia = la;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float ya = __shfl_up_sync(0xffffffffu, ia, o);
-    if (lane >= o) ia += ya;
-  }
-  if (lane == 31) tmp[wid] = ia;
-  __syncthreads();
-  if (wid == 0) {
-    float ta = lane < nw ? tmp[lane] : 0.f;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float ya = __shfl_up_sync(0xffffffffu, ta, o);
-      if (lane >= o) ta += ya;
-    }
-    tmp[lane] = ta;
-  }
-  __syncthreads();
-  float ra = (wid > 0 ? tmp[wid - 1] : 0.f) + ia - la;
-  const float tot = tmp[nw - 1];
-  for (int i = b0; i < b1; ++i) {
-    const float va = a[i];
-    a[i] = ra;
-    ra += va;
-  }
-  __syncthreads();
-  return tot;
-}
-
-}  // namespace kb
-
-namespace kb {
 
 // Exclusive prefix sums in place over buf[0 .. blockDim.x*CH) (the caller zero-pads the tail);
 // thread t owns the contiguous chunk [t*CH, (t+1)*CH).  Returns the total.  tmp >= 32 floats.
@@ -277,27 +170,6 @@ __device__ __forceinline__ float block_exclusive_scan_ch(float* buf, float* tmp)
   __syncthreads();
   return total;
 }
-
-// Block max / min-of-positives / sum in one reduction; tmp >= 96 floats.  Two barriers.
-__device__ __forceinline__ void block_max_minpos_sum(float& mx, float& mn, float& sm, float* tmp) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  mx = warp_max(mx);
-  mn = -warp_max(-mn);
-  sm = warp_sum(sm);
-  __syncthreads();
-  if (lane == 0) { tmp[wid] = mx; tmp[32 + wid] = mn; tmp[64 + wid] = sm; }
-  __syncthreads();
-  const float a1 = lane < nw ? tmp[lane] : 0.f;
-  const float a2 = lane < nw ? tmp[32 + lane] : 3.0e38f;
-  const float a3 = lane < nw ? tmp[64 + lane] : 0.f;
-  mx = warp_max(a1);
-  mn = -warp_max(-a2);
-  sm = warp_sum(a3);
-}
-
-}  // namespace kb
-
-namespace kb {
 
 // Exclusive scan of buf[0 .. blockDim.x*CH) fused with a block max and sum of one value per
 // thread (mx, sm, returned block-wide).  tmp >= 96 floats.  Two barriers (after the per-warp
