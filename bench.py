@@ -816,9 +816,21 @@ def main():
     fwd_ms, bwd_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
 
     # ---- end-to-end through the public API with host buffers ----
+    del loss, saved  # the split pass's saved state: e2e steps reuse the same cached blocks
     th_host = theta.detach().cpu().pin_memory()
     cw_host = cw.detach().cpu().pin_memory()
     out_host = torch.empty((n_grad,), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        th_d = th_host.to(dev, non_blocking=True)
+        cw_d = cw_host.to(dev, non_blocking=True)
+        loss, gt, gc = step(th_d, cw_d)
+        res = torch.cat([loss.reshape(1).float(), gt.reshape(-1).float(), gc.reshape(-1).float()])
+        out_host.copy_(res, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(out_host[0])
+
+    e2e_step()  # untimed: first use of the pinned buffers on this path
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -826,13 +838,7 @@ def main():
     e_end = torch.cuda.Event(enable_timing=True)
     e_start.record()
     for _ in range(args.steps):
-        th_d = th_host.to(dev, non_blocking=True)
-        cw_d = cw_host.to(dev, non_blocking=True)
-        loss, gt, gc = step(th_d, cw_d)
-        res = torch.cat([loss.reshape(1).float(), gt.reshape(-1).float(), gc.reshape(-1).float()])
-        out_host.copy_(res, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        float(out_host[0])
+        e2e_step()
     e_end.record()
     torch.cuda.synchronize()
     e_ms = e_start.elapsed_time(e_end) / args.steps

@@ -1983,25 +1983,33 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     }
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) T[threadIdx.x + k * NT] = v[k];
+    for (int k = 0; k < VPT; ++k) {
+      T[threadIdx.x + k * NT] = v[k];
+      U[lo16(pk[k])] = v[k] * coef[k];
+    }
 
-    // ---- Neumann series: T current term, U preorder scan buffer ----
+    // ---- Neumann series: term and preorder scan buffers ping-pong between (T, U) and
+    // (SLb, U + NTV) (both free until the split phase), so a term's gathers and the next term's
+    // scatter need no barrier between them: three barriers per term (scatter, scan, scan exit).
     for (int n = 0; n < a.neumann_terms; ++n) {
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = T[threadIdx.x + k * NT] * coef[k];
+      float* Tc = (n & 1) ? SLb : T;
+      float* Tn = (n & 1) ? T : SLb;
+      float* Uc = (n & 1) ? U + NTV : U;
+      float* Un = (n & 1) ? U : U + NTV;
       __syncthreads();
-      const float A = block_exclusive_scan_ch<VPT>(U, red);
-      float nv[VPT];
+      const float A = block_exclusive_scan_ch<VPT>(Uc, red);
+      const bool more = n + 1 < a.neumann_terms;
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         const int s = threadIdx.x + k * NT;
-        const float sub = U[hi16(pk[k])] - U[lo16(pk[k])];
-        nv[k] = T[s] * diag[k] + pp[k] * (A - sub) + T[lo16(pa[k])] * edge[k];
-        v[k] += nv[k];
+        const float sub = Uc[hi16(pk[k])] - Uc[lo16(pk[k])];
+        const float nv = Tc[s] * diag[k] + pp[k] * (A - sub) + Tc[lo16(pa[k])] * edge[k];
+        v[k] += nv;
+        if (more) {
+          Tn[s] = nv;
+          Un[lo16(pk[k])] = nv * coef[k];
+        }
       }
-      __syncthreads();
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) T[threadIdx.x + k * NT] = nv[k];
     }
     if (a.v_out) {
 #pragma unroll
