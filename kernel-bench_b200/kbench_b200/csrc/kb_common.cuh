@@ -109,6 +109,71 @@ __device__ __forceinline__ void subtree_sums_levels(float* buf, const long long*
   }
 }
 
+// Exclusive prefix sums of a block-wide sequence held in registers: thread t holds entries
+// [t*CH, (t+1)*CH) in v, which become their exclusive prefixes; returns the total.  The same
+// additions in the same order as block_exclusive_scan_ch.  ONE barrier: tmp (>= 32 floats) is
+// read after it, so the caller must pass another barrier before tmp is written again.
+template <int CH>
+__device__ __forceinline__ float reg_exclusive_scan(float (&v)[CH], float* tmp) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  float local = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) local += v[j];
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) tmp[wid] = incl;
+  __syncthreads();
+  float t = lane < nw ? tmp[lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, t, o);
+    if (lane >= o) t += y;
+  }
+  const float prev = __shfl_up_sync(0xffffffffu, t, 1);
+  const float wbase = __shfl_sync(0xffffffffu, lane == 0 ? 0.f : prev, wid);
+  const float total = __shfl_sync(0xffffffffu, t, nw - 1);
+  float run = wbase + incl - local;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const float x = v[j];
+    v[j] = run;
+    run += x;
+  }
+  return total;
+}
+
+// Stores CH consecutive floats at dst (16-byte aligned when CH % 4 == 0).
+template <int CH>
+__device__ __forceinline__ void store_chunk(float* dst, const float (&v)[CH]) {
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4)
+      *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) dst[j] = v[j];
+  }
+}
+
+// Loads CH consecutive floats from src (16-byte aligned when CH % 4 == 0).
+template <int CH>
+__device__ __forceinline__ void load_chunk(float (&v)[CH], const float* src) {
+  if constexpr (CH % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(src + j);
+      v[j] = q.x; v[j + 1] = q.y; v[j + 2] = q.z; v[j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) v[j] = src[j];
+  }
+}
+
 // Exclusive prefix sums in place over buf[0 .. blockDim.x*CH) (the caller zero-pads the tail);
 // thread t owns the contiguous chunk [t*CH, (t+1)*CH).  Returns the total.  tmp >= 32 floats.
 // Syncs on exit (the caller syncs before, after writing buf).

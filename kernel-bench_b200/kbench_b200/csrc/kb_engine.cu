@@ -1981,34 +1981,70 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       const unsigned par = lo16(pa[k]);
       edge[k] = hi16(pa[k]) ? T[par] : U[par];  // zero column for the root / padding
     }
+    // ---- Neumann series over preorder positions ----
+    // Thread t owns positions q = t*VPT + j, so the preorder prefix that gives every subtree sum
+    // is a register scan with one barrier, and each term costs two barriers (scan, publish).
+    // The five per-column vectors move to their positions q = pre(s) once, through T, U,
+    // U + NTV, SLb and SRb (all free until the split phase); row 4 of the packed tables gives,
+    // per position, the subtree end and the parent's position.
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      T[threadIdx.x + k * NT] = v[k];
-      U[lo16(pk[k])] = v[k] * coef[k];
+      const unsigned q = lo16(pk[k]);
+      T[q] = v[k];
+      U[q] = diag[k];
+      U[NTV + q] = pp[k];
+      SLb[q] = coef[k];
+      SRb[q] = edge[k];
+    }
+    const int q0 = threadIdx.x * VPT;
+    unsigned pq[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) pq[j] = __ldg(c.packed + 4 * NTV + q0 + j);
+    __syncthreads();
+    float tq[VPT], dq[VPT], cq[VPT], ppq[VPT], eq[VPT], vq[VPT];
+    load_chunk<VPT>(tq, T + q0);
+    load_chunk<VPT>(dq, U + q0);
+    load_chunk<VPT>(ppq, U + NTV + q0);
+    load_chunk<VPT>(cq, SLb + q0);
+    load_chunk<VPT>(eq, SRb + q0);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) vq[j] = tq[j];
+    // T: the current term by position, U: its exclusive prefix.  A term's gathers come before
+    // the next term's scan barrier and its stores after it, so one buffer pair suffices.
+    for (int n = 0; n < a.neumann_terms; ++n) {
+      float x[VPT];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) x[j] = tq[j] * cq[j];
+      const float A = reg_exclusive_scan<VPT>(x, red);
+      store_chunk<VPT>(U + q0, x);
+      store_chunk<VPT>(T + q0, tq);
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const float sub = U[lo16(pq[j])] - x[j];
+        const float nv = tq[j] * dq[j] + ppq[j] * (A - sub) + T[hi16(pq[j])] * eq[j];
+        vq[j] += nv;
+        tq[j] = nv;
+      }
     }
 
-    // ---- Neumann series: term and preorder scan buffers ping-pong between (T, U) and
-    // (SLb, U + NTV) (both free until the split phase), so a term's gathers and the next term's
-    // scatter need no barrier between them: three barriers per term (scatter, scan, scan exit).
-    for (int n = 0; n < a.neumann_terms; ++n) {
-      float* Tc = (n & 1) ? SLb : T;
-      float* Tn = (n & 1) ? T : SLb;
-      float* Uc = (n & 1) ? U + NTV : U;
-      float* Un = (n & 1) ? U : U + NTV;
+    // ---- column gradient of the self-loop Pibar term; the solved row back to columns ----
+    {
+      float x[VPT];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) x[j] = vq[j] * cq[j];
+      const float A = reg_exclusive_scan<VPT>(x, red);
+      store_chunk<VPT>(U + q0, x);
+      store_chunk<VPT>(T + q0, vq);
       __syncthreads();
-      const float A = block_exclusive_scan_ch<VPT>(Uc, red);
-      const bool more = n + 1 < a.neumann_terms;
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         const int s = threadIdx.x + k * NT;
-        const float sub = Uc[hi16(pk[k])] - Uc[lo16(pk[k])];
-        const float nv = Tc[s] * diag[k] + pp[k] * (A - sub) + Tc[lo16(pa[k])] * edge[k];
-        v[k] += nv;
-        if (more) {
-          Tn[s] = nv;
-          Un[lo16(pk[k])] = nv * coef[k];
-        }
+        const unsigned q = lo16(pk[k]);
+        v[k] = T[q];
+        const float sub = U[hi16(pk[k])] - U[q];
+        ACC[G_COL * NTV + s] += U[NTV + q] * (A - sub);
       }
     }
     if (a.v_out) {
@@ -2016,21 +2052,6 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       for (int k = 0; k < VPT; ++k) {
         const int s = threadIdx.x + k * NT;
         if (s < S) a.v_out[(size_t)row * S + s] = v[k];
-      }
-    }
-
-    // ---- column gradient of the self-loop Pibar term ----
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) U[lo16(pk[k])] = v[k] * coef[k];
-    __syncthreads();
-    {
-      const float A = block_exclusive_scan_ch<VPT>(U, red);
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int s = threadIdx.x + k * NT;
-        const float sub = U[hi16(pk[k])] - U[lo16(pk[k])];
-        ACC[G_COL * NTV + s] += pp[k] * (A - sub);
       }
     }
 
@@ -2262,17 +2283,21 @@ int engine_width(int S, int& bd) {
 
 // Threads and columns per thread of the backward kernel: the engine's padded width NTV with
 // (where the row allows) KB_BWD_COLS columns per thread, so narrow rows leave room for several
-// CTAs per SM.
+// CTAs per SM.  The block stays a whole number of warps (its scans and reductions take one value
+// from lane 31 of every warp) and at most 1024 threads: fewer columns per thread where NTV / 4
+// is not a multiple of 32 (NTV = 608 for S = 599 runs 608 threads x 1 column), more where NTV
+// exceeds 4096.
 #ifndef KB_BWD_COLS
 #define KB_BWD_COLS 4
 #endif
 int bwd_width(int S, int& bd) {
   int b0;
   const int ntv = engine_width(S, b0) * b0;
-  bd = ntv / KB_BWD_COLS;
-  if (bd < 32) bd = 32;
-  if (bd > 1024) bd = 1024;
-  return ntv / bd;
+  int v = KB_BWD_COLS;
+  while (v > 1 && (ntv % (32 * v) != 0 || ntv / v < 32)) v /= 2;
+  while (ntv / v > 1024) v *= 2;
+  bd = ntv / v;
+  return v;
 }
 
 // Padded width, threads and columns per thread of the forward tour kernel (mirrors

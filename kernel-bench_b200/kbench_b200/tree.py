@@ -138,6 +138,12 @@ def pack_columns(parent, child1, child2, sub_start, sub_end, ntv=None):
                                                  is the ancestor-or-self path sum of x
     row 2  preorder:   pre | pre_end << 16       subtree of x = preorder range [pre, pre_end)
     row 3  parent:     parent | (x is the parent's first child) << 16   (0xFFFF = root)
+
+    With ``ntv`` (padded to ntv columns) a fifth row is indexed by PREORDER POSITION q instead of
+    by column (the backward kernel's Neumann sweep runs with thread t owning positions
+    [t*VPT, (t+1)*VPT)):
+
+    row 4  position q: pre_end(x) | pre(parent(x)) << 16   for the column x with pre(x) = q
     """
     import numpy as np
     par = np.asarray(parent, dtype=np.int64)
@@ -181,6 +187,13 @@ def pack_columns(parent, child1, child2, sub_start, sub_end, ntv=None):
         real[0] = c1f | (c2f << 16)
         real[3] = pf | (first << 16)
         out = np.concatenate([real, ext], axis=1)
+        pre_p = out[2] & 0xFFFF
+        end_p = out[2] >> 16
+        par_p = out[3] & 0xFFFF
+        col_of = np.empty(ntv, dtype=np.int64)
+        col_of[pre_p] = np.arange(ntv, dtype=np.int64)  # preorder (padded) is a permutation
+        pos_row = end_p[col_of] | (pre_p[par_p[col_of]] << 16)
+        out = np.concatenate([out, pos_row[None, :]], axis=0)
     return out.astype(np.uint32).view(np.int32)
 
 

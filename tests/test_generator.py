@@ -106,3 +106,24 @@ def test_packed_column_tables(small):
             want += P[c]
             c = sh["node_parent"][c]
         assert abs(path[x] - want) < 1e-9
+    # row 4, by preorder position: subtree end and the parent's position of the column there
+    pre, end, par = pk[2] & 0xFFFF, pk[2] >> 16, pk[3] & 0xFFFF
+    assert sorted(pre.tolist()) == list(range(ntv))
+    assert pk.shape[0] == 5
+    for x in range(ntv):
+        q = int(pre[x])
+        assert int(pk[4][q] & 0xFFFF) == int(end[x])
+        assert int(pk[4][q] >> 16) == int(pre[par[x]])
+    # the subtree sums the Neumann sweep takes from a prefix over positions match a direct sum
+    w = np.concatenate([rng.random(S), np.zeros(ntv - S)])
+    xq = np.zeros(ntv)
+    xq[pre] = w
+    excl = np.concatenate([[0.0], np.cumsum(xq)])
+    for x in range(S):
+        want, stack = 0.0, [x]
+        while stack:
+            c = stack.pop()
+            want += w[c]
+            stack += [k for k in (sh["node_child1"][c], sh["node_child2"][c]) if 0 <= k < S]
+        q = int(pre[x])
+        assert abs(excl[int(pk[4][q] & 0xFFFF)] - excl[q] - want) < 1e-9

@@ -1,5 +1,5 @@
-"""Parity at the benchmark's row widths (S = 511 and S = 4095, the configs' species trees) on
-small gene families, so the CPU oracle finishes in seconds: the fused engine (forward tour kernel
+"""Parity at the benchmark's row widths (S = 511 and S = 4095, the configs' species trees) and two
+odd widths (S = 79, S = 599) on small gene families, so the CPU oracle finishes in seconds: the fused engine (forward tour kernel
 and the packed-table kernel it replaces, backward level kernel) against the oracle, with the
 production solver settings (pi_iters = 16, neumann_terms = 16)."""
 
@@ -16,6 +16,10 @@ pytestmark = pytest.mark.gpu
 CASES = {
     "S511": gen.ProblemConfig("wide511", 256, 24, 3, 8, 0, solver_options=dict(gen.CONFIGS[2].solver_options)),
     "S4095": gen.ProblemConfig("wide4095", 2048, 32, 3, 10, 0, solver_options=dict(gen.CONFIGS[3].solver_options)),
+    # widths whose padded row is not a multiple of 128 columns (NTV = 96 and 608): the backward
+    # runs them one column per thread so that its block stays whole warps
+    "S79": gen.ProblemConfig("wide79", 40, 24, 3, 8, 0, solver_options=dict(gen.CONFIGS[1].solver_options)),
+    "S599": gen.ProblemConfig("wide599", 300, 24, 3, 8, 0, solver_options=dict(gen.CONFIGS[2].solver_options)),
 }
 _REF = {}
 
