@@ -1032,17 +1032,21 @@ struct Flow {
   int n_items;             // C * groups
 };
 
-// Per-CTA state of the dataflow loop (shared memory; thread 0 sets next = -1 before the loop).
+// Per-CTA state of the dataflow loop (shared memory; the poller sets next = -1 before the loop).
 struct FlowSlot {
   int row;   // the claimed item, broadcast to the CTA
-  int next;  // queue ticket taken ahead by flow_finish_row, -1 = none
+  int next;  // queue ticket taken ahead by flow_finish_row, -1 = none (read by the poller only)
 };
+
+// The one thread that takes queue tickets and waits on them: thread 32 (warp 1, so that warp 0
+// releases dependent rows meanwhile), or thread 0 in a one-warp block (no ticket taken ahead).
+__device__ __forceinline__ unsigned flow_poller() { return blockDim.x > 32 ? 32u : 0u; }
 
 // Claims the next queue slot (the ticket taken ahead, if any) and waits (bounded) until it holds
 // a row.  Returns the row, -1 when every row has been taken, -2 on a timeout (error recorded).
 // Called by all threads.
 __device__ __forceinline__ int flow_next_row(const Flow& f, FlowSlot* st) {
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == flow_poller()) {
     const unsigned idx = st->next >= 0 ? (unsigned)st->next : atomicAdd(f.head, 1u);
     st->next = -1;
     int row = -1;
@@ -1064,13 +1068,14 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, FlowSlot* st) {
     st->row = row;
   }
   __syncthreads();
-  const int row = st->row;
-  __syncthreads();
-  return row;
+  // st->row is written again only in the next call, after flow_finish_row's barrier, which every
+  // thread reaches after this read
+  return st->row;
 }
 
 // After a row's outputs are written by the whole CTA: release the rows that wait on it (one lane
-// of warp 0 per dependent row) while thread 32 takes the CTA's next queue ticket.
+// of warp 0 per dependent row) while the poller (thread 32) takes the CTA's next queue ticket; the
+// ticket stays with the thread that waits on it, so no barrier follows.
 __device__ __forceinline__ void flow_finish_row(const Flow& f, int row, FlowSlot* st) {
   __threadfence();  // every thread's outputs (stores and atomics) are device-visible ...
   __syncthreads();  // ... before warp 0 releases the dependent rows
@@ -1088,7 +1093,6 @@ __device__ __forceinline__ void flow_finish_row(const Flow& f, int row, FlowSlot
     const unsigned idx = atomicAdd(f.head, 1u);
     st->next = idx < (unsigned)f.n_items ? (int)idx : f.n_items;  // >= n_items: nothing left
   }
-  __syncthreads();  // next is visible to thread 0
 }
 
 template <int VF>
@@ -1096,8 +1100,8 @@ __global__ void __launch_bounds__(512, 1) flow_forward_kernel(Fwd4Args args, Flo
   extern __shared__ __align__(16) float sm[];
   __shared__ FlowSlot fs;
   __shared__ __align__(8) unsigned long long bars[2];
+  if (threadIdx.x == flow_poller()) fs.next = -1;
   if (threadIdx.x == 0) {
-    fs.next = -1;
     mbar_init(bars, 1);
     mbar_init(bars + 1, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1715,8 +1719,8 @@ __global__ void __launch_bounds__(512, 1) flow_tangent2_kernel(TanArgs a, Flow f
   extern __shared__ __align__(16) float sm[];
   __shared__ FlowSlot fs;
   __shared__ __align__(8) unsigned long long bar;  // the split staging's bulk copies (3 arrivals)
+  if (threadIdx.x == flow_poller()) fs.next = -1;
   if (threadIdx.x == 0) {
-    fs.next = -1;
     mbar_init(&bar, 3);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1851,7 +1855,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     for (int j = 0; j < G_N; ++j) ACC[j * NTV + s] = 0.f;
   }
   __shared__ FlowSlot fs;
-  if (threadIdx.x == 0) fs.next = -1;
+  if (threadIdx.x == flow_poller()) fs.next = -1;
   int b = blockIdx.x;
   int since_flush = 0;  // DF: rows accumulated in the fp32 shared sums since the last fp64 flush
   for (;;) {
