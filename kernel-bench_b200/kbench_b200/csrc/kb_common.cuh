@@ -176,9 +176,11 @@ __device__ __forceinline__ void load_chunk(float (&v)[CH], const float* src) {
 
 // Exclusive prefix sums in place over buf[0 .. blockDim.x*CH) (the caller zero-pads the tail);
 // thread t owns the contiguous chunk [t*CH, (t+1)*CH).  Returns the total.  tmp >= 32 floats.
-// Syncs on exit (the caller syncs before, after writing buf).
-template <int CH>
-__device__ __forceinline__ float block_exclusive_scan_ch(float* buf, float* tmp) {
+// Syncs on exit (the caller syncs before, after writing buf).  With SUM, *bsum (one value per
+// thread) also becomes its block sum, on the scan's middle barrier (tmp >= 64 floats then; the
+// same additions as block_sum).
+template <int CH, bool SUM = false>
+__device__ __forceinline__ float block_exclusive_scan_ch(float* buf, float* tmp, float* bsum = nullptr) {
   const int tid = threadIdx.x;
   const int lane = tid & 31, wid = tid >> 5, nw = (blockDim.x + 31) >> 5;
   float v[CH];
@@ -203,7 +205,15 @@ __device__ __forceinline__ float block_exclusive_scan_ch(float* buf, float* tmp)
     if (lane >= o) incl += y;
   }
   if (lane == 31) tmp[wid] = incl;
+  if constexpr (SUM) {
+    const float ws = warp_sum(*bsum);
+    if (lane == 0) tmp[32 + wid] = ws;
+  }
   __syncthreads();
+  if constexpr (SUM) {
+    const float r = lane < nw ? tmp[32 + lane] : 0.0f;
+    *bsum = warp_sum(r);
+  }
   float wbase = 0.f, total;
   {
     float t = lane < nw ? tmp[lane] : 0.f;

@@ -277,6 +277,28 @@ __device__ __forceinline__ void dts_row2(const LevelConsts& c, const float* __re
 // (padded to blockDim.x * 2 * VPT floats, tail zero).  Returns path[] for the own columns.
 template <int VPT>
 __device__ __forceinline__ void tour_pathsums(float* T2, float* tmp, const unsigned* tr, const float* pv, int S,
+                                              float* path);
+
+// The same over all NTV = blockDim.x * VPT padded columns (the padded tour is a permutation of
+// its 2 * NTV slots, so every slot is written and nothing needs clearing), fused with the block
+// sum of `bsum` (one value per thread, returned).  Three barriers.
+template <int VPT>
+__device__ __forceinline__ float tour_pathsums_padded(float* T2, float* tmp, const unsigned* tr, const float* pv,
+                                                      float bsum, float* path) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    T2[lo16(tr[k])] = pv[k];
+    T2[hi16(tr[k])] = -pv[k];
+  }
+  __syncthreads();
+  block_exclusive_scan_ch<2 * VPT, true>(T2, tmp, &bsum);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) path[k] = T2[lo16(tr[k])] + pv[k];
+  return bsum;
+}
+
+template <int VPT>
+__device__ __forceinline__ void tour_pathsums(float* T2, float* tmp, const unsigned* tr, const float* pv, int S,
                                               float* path) {
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -1919,7 +1941,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     const float rms = safe_max(a.row_max[row]);
     float pp[VPT];
     float psum = 0.f;
-    __syncthreads();
+    if (has_splits && !a.dts_saved) __syncthreads();  // dts_row2's readers of T and U are done
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
@@ -1930,10 +1952,10 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       pp[k] = s < S ? ex2(w - rms) : 0.f;
       psum += pp[k];
     }
-    for (int i = threadIdx.x; i < 2 * NTV; i += NT) T[i] = 0.f;  // tour buffer (T and U)
-    const float row_sum = block_sum(psum, red);
+    // P and the tour buffer (T and U) are free: the previous row's readers finished before the
+    // barriers of the queue and of the activity check
     float anc[VPT];
-    tour_pathsums<VPT>(T, red, tr, pp, NTV, anc);
+    const float row_sum = tour_pathsums_padded<VPT>(T, red, tr, pp, psum, anc);
     const float leafv = leaf >= 0 ? c.leaf_logp[(size_t)item * S + leaf] : neg_inf();
     float diag[VPT], coef[VPT];
     float a3v[VPT], a4v[VPT];
@@ -1971,19 +1993,20 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
         a4v[k] = wL * e4 * inv_sum;
       }
     }
-    __syncthreads();  // everyone done with the tour scan results
+    // the edge weights go through SLb / SRb (free until the split phase; no copy in flight),
+    // so the tour scan's readers of T and U need no barrier here
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
-      T[s] = a3v[k];  // edge weight (speciation into child c1) of parent column s
-      U[s] = a4v[k];  // ... into child c2
+      SLb[s] = a3v[k];  // edge weight (speciation into child c1) of parent column s
+      SRb[s] = a4v[k];  // ... into child c2
     }
     __syncthreads();
     float edge[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const unsigned par = lo16(pa[k]);
-      edge[k] = hi16(pa[k]) ? T[par] : U[par];  // zero column for the root / padding
+      edge[k] = hi16(pa[k]) ? SLb[par] : SRb[par];  // zero column for the root / padding
     }
     // ---- Neumann series over preorder positions ----
     // Thread t owns positions q = t*VPT + j, so the preorder prefix that gives every subtree sum
