@@ -1912,8 +1912,9 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       v[k] = s < S ? (DF ? __ldcg(rrow + s) : rrow[s]) : 0.f;  // DF: parents add with atomics (L2)
       amax = fmaxf(amax, fabsf(v[k]));
     }
-    amax = block_max(amax, red);
-    const bool active = a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold);
+    // the block max compares above the threshold iff some thread's own max does: one barrier
+    const bool active =
+        __syncthreads_or(a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold)) != 0;
     if (!active) {
       if (DF) flow_finish_row(f, (int)row, &fs);
       continue;
