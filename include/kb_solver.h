@@ -279,9 +279,10 @@ int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const flo
  * weights only (use_col_weights must be 0).  tour_tables: [3,NTV] uint32 tables of
  * kbench_b200/tree.py pack_forward() (children columns, byte offsets of the children's and the
  * column's own Euler-tour slots); when given and kb_tour_layout(S) accepts S, the tour kernel
- * runs (dts_save and tour_consts, from kb_lin_consts_tour, must then be non-NULL).  Otherwise packed: [4,NTV] tables of pack_columns(...,
- * ntv) with NTV from the engine width (children, Euler-tour enter/exit, preorder start/end,
- * parent | first-child flag; two 16-bit fields each). */
+ * runs (dts_save and tour_consts, from kb_lin_consts_tour, must then be non-NULL).  Otherwise
+ * packed: the [5,NTV] tables of pack_columns(..., ntv) with NTV from the engine width, of which
+ * this kernel reads rows 0-3 (children, Euler-tour enter/exit, preorder start/end, parent |
+ * first-child flag; two 16-bit fields each). */
 int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                      const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src, float* pi,
                      float* pibar, float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
@@ -333,8 +334,9 @@ int kb_tour_layout(int S, int* ntv, int* threads, int* cols_per_thread);
  * and added to that CTA's fp64 slot of grad_slots [n_slots, 8, NTV] at the end; slots persist
  * across levels and are reduced in a fixed order by kb_reduce_grad_slots), and every split's child
  * cotangents added into accumulated_rhs.  dts_saved may be NULL (recomputed); v_out [C,S] (may be
- * NULL) receives the solved adjoint row of every active row.  packed_padded: [4,NTV] tables of
- * pack_columns(..., ntv) with NTV = threads x columns-per-thread (kbench_b200/tree.py). */
+ * NULL) receives the solved adjoint row of every active row.  packed_padded: [5,NTV] tables of
+ * pack_columns(..., ntv) with NTV = threads x columns-per-thread (kbench_b200/tree.py): rows 0-3
+ * by column, row 4 by preorder position (subtree end | parent's position). */
 int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                       const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
                       const float* pibar_row_max, const float* dts_saved, float* accumulated_rhs, float* v_out,

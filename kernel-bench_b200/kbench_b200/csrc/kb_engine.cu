@@ -1826,7 +1826,7 @@ __device__ __forceinline__ void block_scan_pair_ch(float2* buf, float* red, floa
 }
 
 struct BwdArgs {
-  LevelConsts c;           // c.packed: padded [4, NTV] tables (invalid child/parent -> zero column NTV-1)
+  LevelConsts c;           // c.packed: padded [5, NTV] tables (invalid child/parent -> zero column NTV-1)
   SplitCSR sp;
   const float* Pi;
   const float* Pibar;
