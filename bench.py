@@ -168,7 +168,7 @@ def algorithmic_bytes(plan, S):
 # species tree with a 12,709-row family (the capture runs ``bench.py --traffic-case``); rows
 # are independent units, so a full-family launch moves ~C times these.
 TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782290944 + 542546688) / 12709,
-                               "kb_flow_backward": (1977673728 + 786529536) / 12709}
+                               "kb_flow_backward": (2066200832 + 815406592) / 12709}
 
 
 def launch_traffic(name, C, S):
