@@ -17,7 +17,8 @@ memory and the loss + gradients copied back every step.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the numpy oracle under
 ``oracle/``) on a bounded sample of the same workload (a family with the same species tree and
-fewer rows), extrapolated per row; on N>1 only rank 0 runs it.
+fewer rows), extrapolated per row, on every host thread (one single-threaded process per thread,
+all passes started together); on N>1 only rank 0 runs it.
 
 ``--config 4`` measures the batched workload instead: 1024 families (S=1023, ~16k rows each)
 sharing one theta, split into contiguous blocks per rank, each block processed in chunks of
