@@ -326,6 +326,13 @@ int kb_lin_consts_tour(const float* dl, const float* ebar, const float* mc, cons
  * *ntv = 0 when NTV would exceed 4096 (kb_level_forward then uses its packed-table kernel). */
 int kb_tour_layout(int S, int* ntv, int* threads, int* cols_per_thread);
 
+/* Layout of the backward kernels (kb_level_backward, kb_flow_backward) for S columns (host only;
+ * no reference counterpart -- the reference sizes its Triton blocks per launch): the engine's
+ * padded width NTV (that of the packed_padded tables), threads per CTA (always whole warps, at
+ * most 1024) and columns per thread (1, 2, 4 or 8, threads x columns = NTV).  Returns 3
+ * (KB_ERR_SIZE) where that needs more than 8 columns per thread (S = 8192) or S > KB_MAX_S. */
+int kb_backward_layout(int S, int* ntv, int* threads, int* cols_per_thread);
+
 /* Backward of one dependency level (replaces, for the rows listed, active_mask_from_rhs_absmax_
  * fused + compute_dts_forward + wave_backward_uniform_fused + dts_cross_backward_accum_fused +
  * uniform_cross_pibar_vjp_tree_from_ud_fused as driven by kbench/api/_implicit_grad.py:

@@ -2513,6 +2513,17 @@ extern "C" int kb_tour_layout(int S, int* ntv, int* threads, int* cols_per_threa
   return n > 0 ? KB_OK : KB_ERR_SIZE;
 }
 
+extern "C" int kb_backward_layout(int S, int* ntv, int* threads, int* cols_per_thread) {
+  if (S <= 0 || ntv == nullptr || threads == nullptr || cols_per_thread == nullptr) return KB_ERR_ARG;
+  if (S > KB_MAX_S) return KB_ERR_SIZE;
+  int bd = 0;
+  const int v = bwd_width(S, bd);
+  *ntv = bd * v;
+  *threads = bd;
+  *cols_per_thread = v;
+  return v <= 8 ? KB_OK : KB_ERR_SIZE;  // the kernels are built for 1, 2, 4 and 8 columns
+}
+
 extern "C" int kb_level_tangent(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                                 const long long* sr, const float* lsp, const float* Pi, const float* Pibar,
                                 const float* dts_saved, float* dPi, float* dPibar, long long dir_stride, int D,

@@ -58,3 +58,21 @@ def test_tour_layout_matches_host_tables():
         else:
             assert st == _lib.KB_OK and (ntv.value, nt.value, vf.value) == want
             assert nt.value % 32 == 0 and vf.value in (2, 4, 8) and ntv.value > S
+
+
+def test_backward_layout_is_whole_warps_over_the_padded_width():
+    """The backward kernels' block for every S up to the library maximum: whole warps (their scans
+    take lane 31 of every warp), at most 1024 threads, threads x columns = the padded width the
+    host builds the column tables for (kbench_b200.tree.engine_width)."""
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("libkb_solver.so not built")
+    from kbench_b200 import tree
+    lib = _lib.lib()
+    ntv, nt, v = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    for S in range(1, 8192):
+        assert lib.kb_backward_layout(S, ctypes.byref(ntv), ctypes.byref(nt), ctypes.byref(v)) == _lib.KB_OK
+        bd, vpt = tree.engine_width(S)
+        assert ntv.value == bd * vpt == nt.value * v.value
+        assert nt.value % 32 == 0 and 32 <= nt.value <= 1024 and v.value in (1, 2, 4, 8)
+    for S in (8192, 8193):
+        assert lib.kb_backward_layout(S, ctypes.byref(ntv), ctypes.byref(nt), ctypes.byref(v)) == _lib.KB_ERR_SIZE
