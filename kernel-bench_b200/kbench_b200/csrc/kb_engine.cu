@@ -1857,9 +1857,14 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
   const int S = c.S;
   const int NT = blockDim.x;
   const int NTV = NT * VPT;
+  // Shared memory, per phase of a row: the tour scan uses T and U[0, NTV) as one 2 NTV buffer;
+  // the edge weights pass through SLb / SRb; the move to preorder positions uses T, U, U + NTV,
+  // SLb and SRb; the Neumann sweep keeps the term in T and its prefix in U (U + NTV: the path
+  // weights, read back by the column gradient); the splits stage child rows in SLb / SRb and
+  // scan float2 pairs in U.
   float* P = sm;               // Pi row (log; -inf on padding), later speciation cotangents
-  float* T = sm + NTV;         // Neumann term / tour (with U) / speciation cotangents
-  float* U = sm + 2 * NTV;     // preorder scan buffer (2 NTV: float2 pairs in the split phase)
+  float* T = sm + NTV;         // tour (with U) / Neumann term / speciation cotangents
+  float* U = sm + 2 * NTV;     // 2 NTV: tour, preorder prefix, float2 pairs in the split phase
   float2* U2 = reinterpret_cast<float2*>(U);
   float* ACC = sm + 4 * NTV;   // G_N rows of NTV fp32 column sums (this CTA)
   float* SLb = ACC + G_N * NTV;  // staged child Pi rows of the current split (NTV + 4 each)
