@@ -95,6 +95,8 @@ CASES = {
     "tiny_s7": (gen.ProblemConfig("tiny", 4, 6, 3, 4, 12), 7, {}),
     "twofam_s31": (gen.ProblemConfig("twofam", 16, 20, 4, 10, 60, n_families=2), 31,
                    {"pi_iters": 4, "neumann_terms": 5}),
+    # S = 79: a padded width (96) that is not a multiple of 128 columns
+    "odd_s79": (gen.ProblemConfig("odd79", 40, 16, 3, 8, 0), 79, {}),
 }
 
 
