@@ -125,6 +125,41 @@ def extract_parameters_uniform(theta, unnorm_row_max):
     return r[:, 0].copy(), r[:, 1].copy(), r[:, 2].copy(), mc
 
 
+def col_weights_are_uniform(col_weights) -> bool:
+    """``solver.py:11-13``: every entry equal (or no weights given)."""
+    if col_weights is None:
+        return True
+    w = np.asarray(col_weights).reshape(-1)
+    return bool(np.all(w == w[0]))
+
+
+def extract_parameters_weighted(theta, col_weights, tree: Tree):
+    """``extract_parameters.py:68-93`` (statewise, not itemwise, ``uniform_fast=False``) in fp32:
+    col_log_probs = log_softmax(w) / ln 2 (``:37-38``), the column normaliser
+    ``-log2(1 - ancestor-or-self mass)`` (``:41-65``, one ancestor per round, self first), and
+    max_coupling = log_pT + normaliser.  Returns (log_pS, log_pD, log_pL, max_coupling, clp)."""
+    S = tree.S
+    pS, pD, pL, log_pT = extract_parameters_uniform(theta, np.zeros(S, F32))
+    w = _f(col_weights).reshape(-1)
+    m = w.max()
+    lse = (m + np.log(np.exp(w - m, dtype=F32).sum(dtype=F32))).astype(F32)
+    clp = ((w - lse) / F32(LN2)).astype(F32)
+    col_p = np.exp2(clp).astype(F32)
+    anc = np.zeros(S, F32)
+    cur = np.arange(S)
+    for _ in range(tree.max_depth):
+        valid = (cur >= 0) & (cur < S)
+        safe = np.where(valid, cur, 0)
+        anc = (anc + np.where(valid, col_p[safe], F32(0.0))).astype(F32)
+        cur = np.where(valid, tree.parent[safe], -1)
+    vm = (F32(1.0) - anc).astype(F32)
+    tiny = np.finfo(np.float32).tiny
+    with np.errstate(divide="ignore"):
+        norm = np.where(vm > 0.0, -np.log2(np.maximum(vm, tiny)), -np.inf).astype(F32)
+    mc = (log_pT + norm).astype(F32)
+    return pS, pD, pL, mc, clp
+
+
 def extract_parameters_vjp(theta, col_weights, tree: Tree, g_pS, g_pD, g_pL, g_mt, g_col,
                            *, uniform_fast=True):
     """VJP of ``extract_parameters_weighted_cols`` (``extract_parameters.py:68-93``, with
@@ -385,17 +420,23 @@ def leaf_initial(consts: dict, col_logp, tree: Tree, leaf_state, leaf_logp,
 
 def forward(static: dict, theta, col_weights=None, *, pi_iters=None, e_init=None):
     """theta -> (loss, saved): ``kbench/runtime.py:63-74`` -> ``solver.py:16-96`` (E fixed point,
-    ``forward.py:8-117`` wave loop) -> ``solver.py:132-142`` NLL. Uniform column weights only."""
+    ``forward.py:8-117`` wave loop) -> ``solver.py:132-142`` NLL; non-uniform ``col_weights``
+    take the weighted-column parameters and kernels (``use_col_weights``) as the reference does."""
     sh = static["state_helpers"]
     wl = static["wave_layout"]
     so = static["solver_options"]
     tree = Tree(sh)
     S = tree.S
-    pS, pD, pL, mc = extract_parameters_uniform(theta, sh["unnorm_row_max"])
-    col_logp = np.full(S, -math.log2(S), dtype=F32)
+    ucw = not col_weights_are_uniform(col_weights)  # solver.py:27-44
+    if ucw:
+        pS, pD, pL, mc, col_logp = extract_parameters_weighted(theta, col_weights, tree)
+    else:
+        pS, pD, pL, mc = extract_parameters_uniform(theta, sh["unnorm_row_max"])
+        col_logp = np.full(S, -math.log2(S), dtype=F32)
     E0 = np.full(S, float(so.get("e_init", -1.0) if e_init is None else e_init), dtype=F32)
     E, E_s1, E_s2, Ebar, n_e = e_fixed_point(E0, pS, pD, pL, mc, col_logp, tree,
-                                             max_iter=so["e_max_iter"], tol=so["e_tol"])
+                                             max_iter=so["e_max_iter"], tol=so["e_tol"],
+                                             use_col_weights=ucw)
     pi_iters = int(so["pi_iters"] if pi_iters is None else pi_iters)
     consts = {
         "dl": (F32(1.0) + pD + E).astype(F32), "ebar": Ebar, "e": E,
@@ -417,14 +458,14 @@ def forward(static: dict, theta, col_weights=None, *, pi_iters=None, e_init=None
             if it == 0 and not has_leaf:
                 continue
             if it == 0:
-                pi_out[ws:ws + W] = leaf_initial(consts, col_logp, tree, leaf_state, pS)
+                pi_out[ws:ws + W] = leaf_initial(consts, col_logp, tree, leaf_state, pS, use_col_weights=ucw)
                 continue
             src = dts_r if (it == 1 and not has_leaf) else pi_in[ws:ws + W]
             new = wave_step(src, consts, col_logp, tree, leaf_state=leaf_state, leaf_logp=pS,
-                            dts_r=dts_r)
+                            dts_r=dts_r, use_col_weights=ucw)
             pi_out[ws:ws + W] = new
             if it == pi_iters - 1:
-                pib, rmax = pibar_rows(new, mc, col_logp, tree)
+                pib, rmax = pibar_rows(new, mc, col_logp, tree, use_col_weights=ucw)
                 pibar[ws:ws + W] = pib
                 row_max[ws:ws + W] = rmax
     roots = np.asarray(wl["root_row_ids"], dtype=np.int64)
@@ -694,15 +735,17 @@ def bicgstab(Av, b, *, max_iter=500, tol=1e-7, breakdown_tol=1e-30):
 def backward(static: dict, theta, col_weights, saved: dict, acc_dtype=F32):
     """(forward intermediates) -> (grad_theta, grad_col): ``kbench/runtime.py:77-115`` ->
     ``kbench/api/_implicit_grad.py:98-370`` (reverse wave loop) and ``:373-475`` (E adjoint and
-    theta VJP). Uniform column weights (``use_col_weights=False``)."""
-    acc = backward_accumulators(static, saved, acc_dtype)
+    theta VJP); ``use_col_weights`` = not uniform ``col_weights`` (``runtime.py:84``)."""
+    acc = backward_accumulators(static, saved, acc_dtype,
+                                use_col_weights=not col_weights_are_uniform(col_weights))
     n_fam = int(np.asarray(static["wave_layout"]["root_row_ids"]).shape[0])
     return e_adjoint_and_theta_vjp(static, theta, col_weights, saved, Tree(static["state_helpers"]),
                                    acc["E"], acc["Ebar"], acc["E_s1"], acc["E_s2"], acc["pD"], acc["pS"],
                                    acc["mt"], acc["col"], n_fam=n_fam)
 
 
-def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list | None = None) -> dict:
+def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list | None = None,
+                          use_col_weights: bool = False) -> dict:
     """The reverse wave loop of ``kbench/api/_implicit_grad.py:98-370`` alone: the fp32 column
     accumulators ``pD, pS, mt, E, Ebar, E_s1, E_s2, col`` (``:144-158``) that the E adjoint and
     theta VJP consume.
@@ -751,7 +794,7 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
             Pi, Pibar, row_max, ws, W, dts_r, rhs, consts, col_logp, tree,
             neumann_terms=int(so["neumann_terms"]),
             leaf_state=None if has_splits else leaf_state_all[ws:ws + W],
-            leaf_logp=pS, active=act, grad_col=g_col)
+            leaf_logp=pS, active=act, grad_col=g_col, use_col_weights=use_col_weights)
         if cache is not None:
             cache.append(dict(ws=ws, W=W, v=np.where(act[:, None], v_k, F32(0.0)).astype(F32), dts_r=dts_r,
                               active=act, has_splits=has_splits, meta=meta))
@@ -764,7 +807,7 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
                                              active=act, grad_log_pD=g_pD, grad_log_pS=g_pS,
                                              grad_mt=g_mt, mt=mc, row_max_all=row_max)
             pibar_vjp_tree(Pi, col_logp, ud, A, side, meta, tree, acc, active=act,
-                           row_max_all=row_max, grad_col=g_col)
+                           row_max_all=row_max, grad_col=g_col, use_col_weights=use_col_weights)
     out = {"pD": g_pD, "pS": g_pS, "mt": g_mt, "E": g_E, "Ebar": g_Ebar, "E_s1": g_Es1, "E_s2": g_Es2,
            "col": g_col}
     return {k: v.astype(F32) for k, v in out.items()}
@@ -780,11 +823,13 @@ def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, tree: Tree, g_E, 
     pS = _f(saved["log_pS"]).reshape(-1); pD = _f(saved["log_pD"]).reshape(-1)
     pL = _f(saved["log_pL"]).reshape(-1); mc = _f(saved["max_coupling"]).reshape(-1)
     col_logp = _f(saved["col_log_probs"]).reshape(-1)
-    E_new, Es1, Es2, Ebar, _ = e_step_forward(E, pS, pD, pL, mc, col_logp, tree)
+    ucw = not col_weights_are_uniform(col_weights)
+    E_new, Es1, Es2, Ebar, _ = e_step_forward(E, pS, pD, pL, mc, col_logp, tree, ucw)
     zeros = np.zeros(S, F32)
 
     def vjp_E(g_new, g1, g2, gb):
-        return e_step_vjp(E, E_new, Es1, Es2, Ebar, pS, pD, pL, col_logp, tree, g_new, g1, g2, gb)
+        return e_step_vjp(E, E_new, Es1, Es2, Ebar, pS, pD, pL, col_logp, tree, g_new, g1, g2, gb,
+                          use_col_weights=ucw)
 
     ge_aux = vjp_E(zeros, g_Es1, g_Es2, g_Ebar)[0]
     norm = F32(1.0) - F32(np.exp2(E).mean(dtype=F32))

@@ -97,11 +97,19 @@ CASES = {
                    {"pi_iters": 4, "neumann_terms": 5}),
     # S = 79: a padded width (96) that is not a multiple of 128 columns
     "odd_s79": (gen.ProblemConfig("odd79", 40, 16, 3, 8, 0), 79, {}),
+    # non-uniform column weights (col_weights ~ N(0,1), seed 77): the weighted column path
+    "weighted_s31": (gen.ProblemConfig("weighted", 16, 20, 4, 10, 0), 3131, {"_col_weights_seed": 77}),
 }
 
 
 def run_case(runtime, name, cfg, seed, overrides):
+    overrides = dict(overrides)
+    cw_seed = overrides.pop("_col_weights_seed", None)
     cap = gen.generate(cfg, seed=seed, solver_options=overrides)
+    if cw_seed is not None:
+        S = int(cap["meta"]["S"])
+        w = np.random.Generator(np.random.PCG64(cw_seed)).standard_normal(S).astype(np.float32)
+        cap["inputs"]["col_weights"] = torch.from_numpy(w)
     static = runtime.make_static(cap, "cpu")
     theta = cap["inputs"]["theta"]
     cw = cap["inputs"]["col_weights"]
