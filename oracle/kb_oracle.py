@@ -611,12 +611,13 @@ def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, t
 
 
 def dts_cross_backward(Pi, Pibar, v_k, ws, meta, log_pD, log_pS, tree: Tree, acc_rhs, *,
-                       active, grad_log_pD, grad_log_pS, grad_mt, mt, row_max_all):
+                       active, grad_log_pD, grad_log_pS, grad_mt, mt, row_max_all, side_threshold=0.0):
     """``dts_cross_backward_accum_fused`` as the backward glue calls it
     (``experiments/pristine_kernels/wave_backward.py:1529-1945``; call flags at
     ``kbench/api/_implicit_grad.py:300-331``: merged S-term, parameter and mt reductions, staged
-    Pibar u_d with side-active flags). Mutates acc_rhs and the grads. Returns
-    (pibar_ud [2N,S], pibar_A [2N], side_active [2N])."""
+    Pibar u_d with side-active flags: with ``side_threshold`` > 0 a side is active when the sum
+    of its |u_d| exceeds it (``:1776-1779, 1877-1884``), else when any u_d is nonzero). Mutates
+    acc_rhs and the grads. Returns (pibar_ud [2N,S], pibar_A [2N], side_active [2N])."""
     S = tree.S
     sl = np.asarray(meta["sl"]); sr = np.asarray(meta["sr"])
     red = np.asarray(meta["reduce_idx"]); lsp = np.asarray(meta["log_split_probs"], dtype=F32)
@@ -647,8 +648,12 @@ def dts_cross_backward(Pi, Pibar, v_k, ws, meta, log_pD, log_pS, tree: Tree, acc
         ud[N + i] = ud_r
         A[i] = ud_l.sum(dtype=F32)
         A[N + i] = ud_r.sum(dtype=F32)
-        side[i] = np.abs(ud_l).max() != 0
-        side[N + i] = np.abs(ud_r).max() != 0
+        if side_threshold > 0.0:
+            side[i] = np.abs(ud_l).sum(dtype=F32) > F32(side_threshold)
+            side[N + i] = np.abs(ud_r).sum(dtype=F32) > F32(side_threshold)
+        else:
+            side[i] = np.abs(ud_l).max() != 0
+            side[N + i] = np.abs(ud_r).max() != 0
         grad_log_pD += vd[0]
         grad_log_pS += (vd[3] + vd[4]).astype(F32)
         grad_mt += (vd[1] + vd[2]).astype(F32)
@@ -805,7 +810,8 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
         if has_splits:
             ud, A, side = dts_cross_backward(Pi, Pibar, v_k, ws, meta, pD, pS, tree, acc,
                                              active=act, grad_log_pD=g_pD, grad_log_pS=g_pS,
-                                             grad_mt=g_mt, mt=mc, row_max_all=row_max)
+                                             grad_mt=g_mt, mt=mc, row_max_all=row_max,
+                                             side_threshold=float(so.get("pibar_side_threshold", 0.0)))
             pibar_vjp_tree(Pi, col_logp, ud, A, side, meta, tree, acc, active=act,
                            row_max_all=row_max, grad_col=g_col, use_col_weights=use_col_weights)
     out = {"pD": g_pD, "pS": g_pS, "mt": g_mt, "E": g_E, "Ebar": g_Ebar, "E_s1": g_Es1, "E_s2": g_Es2,

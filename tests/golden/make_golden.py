@@ -99,6 +99,8 @@ CASES = {
     "odd_s79": (gen.ProblemConfig("odd79", 40, 16, 3, 8, 0), 79, {}),
     # non-uniform column weights (col_weights ~ N(0,1), seed 77): the weighted column path
     "weighted_s31": (gen.ProblemConfig("weighted", 16, 20, 4, 10, 0), 3131, {"_col_weights_seed": 77}),
+    # the other adjoint options: no activity pruning, and a Pibar-side activity threshold
+    "options_s63": (1, 6363, {"use_adjoint_pruning": False, "pibar_side_threshold": 1e-3}),
 }
 
 
