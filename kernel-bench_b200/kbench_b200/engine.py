@@ -134,16 +134,6 @@ def build_plan(static) -> LevelPlan:
     return plan
 
 
-_SM_COUNT: dict = {}
-
-
-def _sm_count(dev) -> int:
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    if idx not in _SM_COUNT:
-        _SM_COUNT[idx] = int(torch.cuda.get_device_properties(idx).multi_processor_count)
-    return _SM_COUNT[idx]
-
-
 def supported(static) -> bool:
     """The fused engine's layouts: one shared item row (statewise, not itemwise) and rows of at
     most 4,095 columns (the tour kernels' 4,096-column padded width); anything else runs on the

@@ -13,10 +13,6 @@ from .. import _lib, tree
 from ._common import f32, require_cuda_f32, rows_of
 
 
-def _as_item_state(t, S, G):
-    return rows_of(t, G, S)
-
-
 def _launch_e_step_forward_2d(E, log_pS_mat, log_pD_mat, log_pL_mat, max_coupling_mat, col_log_probs,
                               node_parent, node_child1, node_child2, max_ancestor_depth, *,
                               max_diff_out=None, out=None, use_col_weights=True):
