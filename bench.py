@@ -214,17 +214,10 @@ def cpu_sample_case(n_genes, S_species_leaves=2048):
 
 def run_cpu_oracle_sample(full_rows, seed, n_genes=512, species_leaves=2048):
     """Time the oracle (forward + backward) on the sample; returns (solves/s, seconds, rows)."""
-    import numpy as np
-    from kbench_b200 import gen
-    from oracle import kb_oracle as O
-    cap = gen.generate(cpu_sample_case(n_genes, species_leaves), seed=seed, as_torch=False)
-    st = dict(cap["static"])
-    st["solver_options"] = cap["meta"]["solver_options"]
+    run, rows = _oracle_sample_fn("solve", (n_genes, species_leaves, seed))
     t0 = time.perf_counter()
-    loss, saved = O.forward(st, cap["inputs"]["theta"], cap["inputs"]["col_weights"])
-    O.backward(st, cap["inputs"]["theta"], cap["inputs"]["col_weights"], saved)
+    run()
     dt = time.perf_counter() - t0
-    rows = int(cap["meta"]["C"])
     # per-row work is the same (same S, same iteration counts): scale to the full family
     solve_s = dt * full_rows / rows
     return 1.0 / solve_s, dt, rows
@@ -359,23 +352,10 @@ def traffic_case(args):
 def hvp_oracle_sample(cfg, seed, n_genes):
     """Time one oracle HVP (point cache excluded) on a small family of config ``cfg``'s species
     tree; returns (seconds per HVP, rows of the sample)."""
-    import numpy as np
-    from kbench_b200 import gen
-    from oracle import kb_oracle as O
-    from oracle import kb_oracle_hvp as OH
-    c = gen.CONFIGS[cfg]
-    case = gen.ProblemConfig("hvp_sample", c.n_species, n_genes, 2, max(4, n_genes // 3), 0,
-                             solver_options=dict(c.solver_options))
-    cap = gen.generate(case, seed=seed, as_torch=False)
-    st = dict(cap["static"])
-    st["solver_options"] = cap["meta"]["solver_options"]
-    theta, cw = cap["inputs"]["theta"], cap["inputs"]["col_weights"]
-    _, saved = O.forward(st, theta, cw)
-    cache = OH.point_cache(st, theta, cw, saved)
-    u = np.random.default_rng(seed).standard_normal(theta.size).astype(np.float32)
+    run, rows = _oracle_sample_fn("hvp", (cfg, seed, n_genes))
     t0 = time.perf_counter()
-    OH.hvp(st, theta, cw, saved, u, cache=cache)
-    return time.perf_counter() - t0, int(cap["meta"]["C"])
+    run()
+    return time.perf_counter() - t0, rows
 
 
 def hvp_arm(args, world, rank, local):
