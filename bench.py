@@ -68,10 +68,11 @@ def parse_args():
     ap.add_argument("--hvp", action="store_true",
                     help="exact-Hessian HVPs/s (newton/hvp_exact.py) on the --hvp-config family")
     ap.add_argument("--hvp-config", type=int, default=2, help="--hvp: the problem config (default 2, S=511)")
-    ap.add_argument("--traffic-case", action="store_true",
-                    help="two forward + backward passes of a reduced config-3 family (the config-3 species tree, "
-                         "2,048 genes: ~12.7k rows, 208 MB per [C,S] buffer), the case the DRAM-traffic capture "
-                         "is taken on")
+    ap.add_argument("--traffic-case", nargs="?", const="reduced", choices=("reduced", "config3"), default=None,
+                    help="two forward + backward passes and nothing else, for ncu captures: 'reduced' (default) is "
+                         "a reduced config-3 family (the config-3 species tree, 2,048 genes: ~12.7k rows, 208 MB per "
+                         "[C,S] buffer) for multi-pass captures; 'config3' is the full config-3 family, for "
+                         "single-pass captures (DRAM bytes, durations) of the full-size launches")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
@@ -330,13 +331,17 @@ HVP_BYTES_PER_ROW_ELEM = 13 * 4
 
 
 def traffic_case(args):
-    """--traffic-case: the reduced config-3 family that the DRAM-traffic ncu capture runs on (a full
-    config-3 launch is too large to capture).  Rows are independent units, so per-row traffic
-    scales to the full family."""
+    """--traffic-case: two forward + backward passes, nothing timed, for ncu.  'reduced': a
+    config-3 species tree with a smaller gene family, small enough for multi-pass captures (the
+    full set of sections); 'config3': the benchmark's family itself, for single-pass metrics
+    (DRAM bytes read / written and durations) of the full-size launches."""
     import torch
     from kbench_b200 import engine, gen, runtime
-    cfg = gen.ProblemConfig("traffic", gen.CONFIGS[3].n_species, 2048, 32, 682, 0,
-                            solver_options=dict(gen.CONFIGS[3].solver_options))
+    if args.traffic_case == "config3":
+        cfg = 3
+    else:
+        cfg = gen.ProblemConfig("traffic", gen.CONFIGS[3].n_species, 2048, 32, 682, 0,
+                                solver_options=dict(gen.CONFIGS[3].solver_options))
     cap = gen.generate(cfg, seed=3000)
     static = runtime.make_static(cap, "cuda")
     theta, cw = cap["inputs"]["theta"].cuda(), cap["inputs"]["col_weights"].cuda()

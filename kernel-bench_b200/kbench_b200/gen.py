@@ -463,6 +463,10 @@ def to_torch(obj):
     """Recursively convert numpy arrays to torch tensors (CPU)."""
     import torch
     if isinstance(obj, np.ndarray):
+        if obj.size == 0:
+            # torch.from_numpy gives empty arrays a zero stride, which byte views (the reference
+            # capture's content hash) reject; an ordinary empty tensor has unit strides
+            return torch.empty(obj.shape, dtype=torch.from_numpy(np.zeros(1, obj.dtype)).dtype)
         return torch.from_numpy(np.ascontiguousarray(obj))
     if isinstance(obj, dict):
         return {k: to_torch(v) for k, v in obj.items()}

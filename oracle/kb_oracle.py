@@ -19,12 +19,32 @@ kernels under ``TRITON_INTERPRET=1`` on the CPU) on generated problems and store
 from __future__ import annotations
 
 import math
+import types
+from pathlib import Path
 
 import numpy as np
 
 F32 = np.float32
 NEG_INF = F32(-np.inf)
 LN2 = 0.6931471805599453
+
+
+def at_precision(dtype) -> types.ModuleType:
+    """A fresh copy of this module whose arithmetic type is ``dtype`` (e.g. ``numpy.float64``).
+
+    Every array, constant and default argument of the copy is built from its module-level ``F32``,
+    so the copy evaluates the same algorithm (same operations in the same order, same stopping
+    rules) at the higher precision: the yardstick for how far fp32 implementations of it -- the
+    reference's and ours -- are from the algorithm's exact value."""
+    name = np.dtype(dtype).name
+    src = Path(__file__).read_text()
+    anchor = "\nF32 = np.float32\n"
+    if anchor not in src:
+        raise RuntimeError("kb_oracle: dtype anchor not found")
+    mod = types.ModuleType(f"kb_oracle_{name}")
+    mod.__file__ = __file__
+    exec(compile(src.replace(anchor, f"\nF32 = np.{name}\n", 1), __file__, "exec"), mod.__dict__)
+    return mod
 
 
 def _f(x):
