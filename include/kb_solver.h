@@ -219,7 +219,9 @@ int kb_active_mask(const float* rhs, long long row_stride, int W, int S, float t
  * per active row, v = sum_{n<=neumann_terms} (J^T)^n rhs and the parameter buckets aw0..aw4,
  * aw345 ([W,S] each; zero on inactive rows; v_k rows of inactive rows untouched).
  * const_mode: 0 shared [S] constants, 1 row-expanded [W,S], 2 item rows [G,S] via item_idx.
- * leaf_mode: 0 [S], 1 [G], 2 [G,S], 3 scalar. grad_col (may be NULL) is accumulated. */
+ * leaf_mode: 0 [S], 1 [G], 2 [G,S], 3 scalar. grad_col (may be NULL) is accumulated.
+ * last_relres (may be NULL; [W]): |last Neumann term| / max(|v|, FLT_MIN) per row, 0 on inactive
+ * rows -- the return_last_increment output (wave_backward.py:1596-1613). */
 int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
                     const float* rhs, long long rhs_row_stride, const unsigned char* active, const float* dl,
                     const float* ebar, const float* e, const float* sl1, const float* sl2, int const_mode,
@@ -228,8 +230,22 @@ int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_
                     const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1, const int* lv_c2,
                     int use_leaf_index, const int* leaf_state, const float* leaf_logp, int leaf_mode,
                     const float* leaf_term, const long long* item_idx, int neumann_terms, float* grad_col,
-                    float* v_k, float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4, int ws,
-                    int W, int S, void* stream);
+                    float* v_k, float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4,
+                    float* last_relres, int ws, int W, int S, void* stream);
+
+/* The operator of the self-loop solve, A x = x - J_self^T x, per active row (one application of
+ * the single-term kernel with OUTPUT_A, wave_backward.py:485-638, as the GMRES self-loop solver
+ * calls it, :1439-1492); y rows of inactive rows are zero.  Same row coefficients as
+ * kb_wave_adjoint (arguments as there); x rows at stride x_row_stride, y dense [W,S]. */
+int kb_wave_adjoint_apply(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
+                          const unsigned char* active, const float* dl, const float* ebar, const float* e,
+                          const float* sl1, const float* sl2, int const_mode, const float* col_log_probs,
+                          int use_col_weights, const int* node_child1, const int* node_child2,
+                          const int* node_parent, const int* jumps, int K, const long long* lv_ptr, int n_levels,
+                          const int* lv_par, const int* lv_c1, const int* lv_c2, int use_leaf_index,
+                          const int* leaf_state, const float* leaf_logp, int leaf_mode, const float* leaf_term,
+                          const long long* item_idx, const float* x, long long x_row_stride, float* y, int ws,
+                          int W, int S, void* stream);
 
 /* Replaces dts_cross_backward_accum_fused (wave_backward.py:2319-2535): per split, the Pi
  * cotangents of both children (including the merged speciation terms) are added into

@@ -1036,7 +1036,10 @@ __global__ void __launch_bounds__(512, 1) level_forward_tour_kernel(Fwd4Args arg
 // row keeps a count of unfinished child rows; a CTA that finishes a row decrements the counts of
 // the row's parents and appends those that reach zero to a device queue; persistent CTAs take
 // queue slots in order.  Every wait on a queue slot is bounded: past the limit the CTA records an
-// error and leaves (the host then reports the failure; it never hangs).
+// error and leaves (the host then reports the failure; it never hangs).  A CTA waiting on a slot
+// relies on the CTAs that will fill it being resident, so the grid is sized from the occupancy
+// query and launched cooperatively: the launch either makes every CTA co-resident or fails (on a
+// GPU shared with other work, e.g. under MPS with fewer SMs), reported as a launch error.
 
 // Work items are (group, row) pairs, item = group * C + row: one group for the forward and the
 // backward, one per tangent direction pair; an item waits for the same group's dependencies.
@@ -2263,13 +2266,29 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
   }
 }
 
-// Fixed-order sum of the per-CTA slots -> the eight fp32 cotangent vectors.
-__global__ void reduce_slots_kernel(const double* __restrict__ slots, int n_slots, int NTV, int S, float* out) {
+// Fixed-order sum of the per-CTA slots -> the eight fp32 cotangent vectors.  Block (x, j) covers
+// 32 columns of accumulator row j: lane = column (coalesced reads), warp w sums its contiguous
+// range of slots in order, then warp 0 adds the warps' partials in warp order -- the same
+// association every run, however many slots there are.
+#define KB_SLOT_WARPS 8
+__global__ void __launch_bounds__(32 * KB_SLOT_WARPS) reduce_slots_kernel(const double* __restrict__ slots, int n_slots,
+                                                                         int NTV, int S, float* out) {
+  __shared__ double part[KB_SLOT_WARPS][32];
   const int j = blockIdx.y;
-  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < S; s += gridDim.x * blockDim.x) {
-    double t = 0.0;
-    for (int b = 0; b < n_slots; ++b) t += slots[((size_t)b * G_N + j) * NTV + s];
-    out[(size_t)j * S + s] = (float)t;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int s = blockIdx.x * 32 + lane;
+  const int per = (n_slots + KB_SLOT_WARPS - 1) / KB_SLOT_WARPS;
+  const int b0 = w * per, b1 = min(n_slots, b0 + per);
+  double t = 0.0;
+  if (s < S)
+    for (int b = b0; b < b1; ++b) t += slots[((size_t)b * G_N + j) * NTV + s];
+  part[w][lane] = t;
+  __syncthreads();
+  if (w == 0 && s < S) {
+    double r = part[0][lane];
+#pragma unroll
+    for (int k = 1; k < KB_SLOT_WARPS; ++k) r += part[k][lane];
+    out[(size_t)j * S + s] = (float)r;
   }
 }
 
@@ -2503,8 +2522,9 @@ extern "C" int kb_reduce_grad_slots(const double* grad_slots, int n_slots, int S
   if (S <= 0 || n_slots <= 0) return KB_ERR_ARG;
   int bd;
   const int vpt = engine_width(S, bd);
-  dim3 grid((S + 255) / 256, G_N);
-  reduce_slots_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(grad_slots, n_slots, bd * vpt, S, out8);
+  dim3 grid((S + 31) / 32, G_N);
+  reduce_slots_kernel<<<grid, 32 * KB_SLOT_WARPS, 0, (cudaStream_t)stream>>>(grad_slots, n_slots, bd * vpt, S,
+                                                                              out8);
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
 
@@ -2647,7 +2667,13 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flow_forward_kernel<V>, nt, smem) !=          \
             cudaSuccess || per_sm < 1)                                                                       \
       return KB_ERR_LAUNCH;                                                                                  \
-    flow_forward_kernel<V><<<(C < n_sm * per_sm ? C : n_sm * per_sm), nt, smem, st>>>(a4, f);                \
+    {                                                                                                        \
+      void* kargs[] = {(void*)&a4, (void*)&f};                                                               \
+      if (cudaLaunchCooperativeKernel((const void*)flow_forward_kernel<V>,                                   \
+                                      dim3(C < n_sm * per_sm ? C : n_sm * per_sm), dim3(nt), kargs, smem,   \
+                                      st) != cudaSuccess)                                                    \
+        return KB_ERR_LAUNCH;                                                                                \
+    }                                                                                                        \
     break;
   switch (vf) {
     KB_FF_CASE(2) KB_FF_CASE(4) KB_FF_CASE(8)
@@ -2698,7 +2724,12 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
     if (smem > 48 * 1024 && cudaFuncSetAttribute((const void*)level_backward_kernel<V, true>,             \
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))  \
       return KB_ERR_LAUNCH;                                                                                \
-    level_backward_kernel<V, true><<<grid, bd, smem, st>>>(a, f);                                          \
+    {                                                                                                      \
+      void* kargs[] = {(void*)&a, (void*)&f};                                                              \
+      if (cudaLaunchCooperativeKernel((const void*)level_backward_kernel<V, true>, dim3(grid), dim3(bd),  \
+                                      kargs, smem, st) != cudaSuccess)                                     \
+        return KB_ERR_LAUNCH;                                                                              \
+    }                                                                                                      \
     break;
   switch (vpt) {
     KB_FB_CASE(1) KB_FB_CASE(2) KB_FB_CASE(4) KB_FB_CASE(8)
@@ -2757,7 +2788,13 @@ extern "C" int kb_flow_tangent(int C, const long long* row_split_ptr, const long
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, flow_tangent2_kernel<V>, nt, smem) !=         \
             cudaSuccess || per_sm < 1)                                                                       \
       return KB_ERR_LAUNCH;                                                                                  \
-    flow_tangent2_kernel<V><<<(n_items < n_sm * per_sm ? n_items : n_sm * per_sm), nt, smem, st>>>(a, f);    \
+    {                                                                                                        \
+      void* kargs[] = {(void*)&a, (void*)&f};                                                                \
+      if (cudaLaunchCooperativeKernel((const void*)flow_tangent2_kernel<V>,                                  \
+                                      dim3(n_items < n_sm * per_sm ? n_items : n_sm * per_sm), dim3(nt),    \
+                                      kargs, smem, st) != cudaSuccess)                                       \
+        return KB_ERR_LAUNCH;                                                                                \
+    }                                                                                                        \
     break;
   switch (vf) {
     KB_FT_CASE(2) KB_FT_CASE(4) KB_FT_CASE(8)

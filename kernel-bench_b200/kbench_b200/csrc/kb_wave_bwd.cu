@@ -13,6 +13,8 @@
 // Neumann term, the bottom-up subtree sums and the coefficient rows stay in shared memory and
 // registers, so a row is read from HBM once and its outputs written once (the reference makes
 // neumann_terms + 3 launches, each a full read/write of several [W,S] scratch tensors).
+#include <cfloat>
+
 #include "kb_common.cuh"
 #include "kb_solver.h"
 
@@ -72,6 +74,10 @@ struct AdjArgs {
   float* aw345;
   float* aw3;
   float* aw4;
+  float* last_relres;        // [W] or null: |last Neumann term| / |v| per row (0 on inactive rows)
+  const float* apply_in;     // apply mode (apply_out != null): y = x - J^T x of one row per CTA,
+  long long apply_rs;        //   x = apply_in rows (stride apply_rs); nothing else is written
+  float* apply_out;          //   [W,S], zero on inactive rows
   int ws;
   int W;
   int S;
@@ -144,9 +150,14 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
   const size_t ob = (size_t)w * S;
   if (a.active && a.active[w] == 0) {
     for (int s = threadIdx.x; s < S; s += blockDim.x) {
-      a.aw0[ob + s] = 0.f; a.aw1[ob + s] = 0.f; a.aw2[ob + s] = 0.f;
-      a.aw345[ob + s] = 0.f; a.aw3[ob + s] = 0.f; a.aw4[ob + s] = 0.f;
+      if (a.apply_out) {
+        a.apply_out[ob + s] = 0.f;
+      } else {
+        a.aw0[ob + s] = 0.f; a.aw1[ob + s] = 0.f; a.aw2[ob + s] = 0.f;
+        a.aw345[ob + s] = 0.f; a.aw3[ob + s] = 0.f; a.aw4[ob + s] = 0.f;
+      }
     }
+    if (a.last_relres && threadIdx.x == 0) a.last_relres[w] = 0.f;
     return;
   }
   const long long rg = (long long)a.ws + w;
@@ -192,7 +203,7 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
       const int x = a.c1[s], y = a.c2[s];
       if (x >= 0 && x < S) EDGE[x] = s1w;
       if (y >= 0 && y < S) EDGE[y] = s2w;
-      v[k] = a.rhs[(size_t)w * a.rhs_rs + s];
+      v[k] = a.apply_out ? a.apply_in[(size_t)w * a.apply_rs + s] : a.rhs[(size_t)w * a.rhs_rs + s];
     }
   }
   __syncthreads();
@@ -209,7 +220,8 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
       T[s] = v[k];
     }
   }
-  for (int n = 0; n < a.neumann_terms; ++n) {
+  const int n_terms = a.apply_out ? 1 : a.neumann_terms;
+  for (int n = 0; n < n_terms; ++n) {
     float usum = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
@@ -241,6 +253,28 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
       if (s < S) T[s] = nv[k];
     }
     __syncthreads();
+  }
+  if (a.apply_out) {  // T holds J^T x
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * blockDim.x;
+      if (s < S) a.apply_out[ob + s] = a.apply_in[(size_t)w * a.apply_rs + s] - T[s];
+    }
+    return;
+  }
+  if (a.last_relres) {  // T holds the last term added to v
+    float tt = 0.f, vv = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int s = threadIdx.x + k * blockDim.x;
+      if (s < S) {
+        tt += T[s] * T[s];
+        vv += v[k] * v[k];
+      }
+    }
+    tt = block_sum(tt, red);
+    vv = block_sum(vv, red);
+    if (threadIdx.x == 0) a.last_relres[w] = sqrtf(tt) / fmaxf(sqrtf(vv), FLT_MIN);
   }
   if (a.grad_col) {
     float usum = 0.f;
@@ -585,6 +619,48 @@ extern "C" int kb_active_mask(const float* rhs, long long row_stride, int W, int
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
 
+namespace {
+
+AdjArgs adjoint_args(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
+                     const unsigned char* active, const float* dl, const float* ebar, const float* e,
+                     const float* sl1, const float* sl2, int const_mode, const float* col_log_probs,
+                     int use_col_weights, const int* node_child1, const int* node_child2, const int* node_parent,
+                     const int* jumps, int K, const long long* lv_ptr, int n_levels, const int* lv_par,
+                     const int* lv_c1, const int* lv_c2, int use_leaf_index, const int* leaf_state,
+                     const float* leaf_logp, int leaf_mode, const float* leaf_term, const long long* item_idx,
+                     int ws, int W, int S) {
+  AdjArgs a = {};
+  a.Pi = Pi; a.Pibar = Pibar; a.row_max = pibar_row_max; a.dts = dts;
+  a.active = active; a.dl = dl; a.ebar = ebar; a.e = e; a.sl1 = sl1; a.sl2 = sl2; a.const_mode = const_mode;
+  a.col = col_log_probs; a.use_col = use_col_weights; a.c1 = node_child1; a.c2 = node_child2;
+  a.parent = node_parent; a.jumps = jumps; a.K = K; a.lv_ptr = lv_ptr; a.n_levels = n_levels;
+  a.lv_par = lv_par; a.lv_c1 = lv_c1; a.lv_c2 = lv_c2; a.use_leaf_index = use_leaf_index;
+  a.leaf_state = leaf_state; a.leaf_logp = leaf_logp; a.leaf_mode = leaf_mode; a.leaf_term = leaf_term;
+  a.item_idx = item_idx; a.ws = ws; a.W = W; a.S = S;
+  return a;
+}
+
+int launch_adjoint(const AdjArgs& a, void* stream) {
+  const int S = a.S;
+  int bd;
+  const int vpt = vpt_for(S, bd);
+  const size_t smem = (size_t)(4 * S + 64) * sizeof(float);
+  cudaStream_t st = (cudaStream_t)stream;
+#define KB_ADJ_CASE(V)                                                            \
+  case V:                                                                         \
+    if (smem_attr((const void*)wave_adjoint_kernel<V>, smem)) return KB_ERR_LAUNCH; \
+    wave_adjoint_kernel<V><<<a.W, bd, smem, st>>>(a);                             \
+    break;
+  switch (vpt) {
+    KB_ADJ_CASE(1) KB_ADJ_CASE(2) KB_ADJ_CASE(4) KB_ADJ_CASE(8) KB_ADJ_CASE(16)
+    default: return KB_ERR_SIZE;
+  }
+#undef KB_ADJ_CASE
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+}  // namespace
+
 extern "C" int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
                                const float* rhs, long long rhs_row_stride, const unsigned char* active,
                                const float* dl, const float* ebar, const float* e, const float* sl1,
@@ -595,35 +671,40 @@ extern "C" int kb_wave_adjoint(const float* Pi, const float* Pibar, const float*
                                const int* leaf_state, const float* leaf_logp, int leaf_mode,
                                const float* leaf_term, const long long* item_idx, int neumann_terms,
                                float* grad_col, float* v_k, float* aw0, float* aw1, float* aw2, float* aw345,
-                               float* aw3, float* aw4, int ws, int W, int S, void* stream) {
+                               float* aw3, float* aw4, float* last_relres, int ws, int W, int S, void* stream) {
   if (S <= 0 || W < 0 || K < 0 || neumann_terms < 0 || n_levels < 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (W == 0) return KB_OK;
-  AdjArgs a;
-  a.Pi = Pi; a.Pibar = Pibar; a.row_max = pibar_row_max; a.dts = dts; a.rhs = rhs; a.rhs_rs = rhs_row_stride;
-  a.active = active; a.dl = dl; a.ebar = ebar; a.e = e; a.sl1 = sl1; a.sl2 = sl2; a.const_mode = const_mode;
-  a.col = col_log_probs; a.use_col = use_col_weights; a.c1 = node_child1; a.c2 = node_child2;
-  a.parent = node_parent; a.jumps = jumps; a.K = K; a.lv_ptr = lv_ptr; a.n_levels = n_levels;
-  a.lv_par = lv_par; a.lv_c1 = lv_c1; a.lv_c2 = lv_c2; a.use_leaf_index = use_leaf_index;
-  a.leaf_state = leaf_state; a.leaf_logp = leaf_logp; a.leaf_mode = leaf_mode; a.leaf_term = leaf_term;
-  a.item_idx = item_idx; a.neumann_terms = neumann_terms; a.grad_col = grad_col; a.v_k = v_k;
+  AdjArgs a = adjoint_args(Pi, Pibar, pibar_row_max, dts, active, dl, ebar, e, sl1, sl2, const_mode, col_log_probs,
+                           use_col_weights, node_child1, node_child2, node_parent, jumps, K, lv_ptr, n_levels,
+                           lv_par, lv_c1, lv_c2, use_leaf_index, leaf_state, leaf_logp, leaf_mode, leaf_term,
+                           item_idx, ws, W, S);
+  a.rhs = rhs; a.rhs_rs = rhs_row_stride;
+  a.neumann_terms = neumann_terms; a.grad_col = grad_col; a.v_k = v_k;
   a.aw0 = aw0; a.aw1 = aw1; a.aw2 = aw2; a.aw345 = aw345; a.aw3 = aw3; a.aw4 = aw4;
-  a.ws = ws; a.W = W; a.S = S;
-  int bd;
-  const int vpt = vpt_for(S, bd);
-  const size_t smem = (size_t)(4 * S + 64) * sizeof(float);
-  cudaStream_t st = (cudaStream_t)stream;
-#define KB_ADJ_CASE(V)                                                            \
-  case V:                                                                         \
-    if (smem_attr((const void*)wave_adjoint_kernel<V>, smem)) return KB_ERR_LAUNCH; \
-    wave_adjoint_kernel<V><<<W, bd, smem, st>>>(a);                               \
-    break;
-  switch (vpt) {
-    KB_ADJ_CASE(1) KB_ADJ_CASE(2) KB_ADJ_CASE(4) KB_ADJ_CASE(8) KB_ADJ_CASE(16)
-    default: return KB_ERR_SIZE;
-  }
-#undef KB_ADJ_CASE
-  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+  a.last_relres = last_relres;
+  return launch_adjoint(a, stream);
+}
+
+extern "C" int kb_wave_adjoint_apply(const float* Pi, const float* Pibar, const float* pibar_row_max,
+                                     const float* dts, const unsigned char* active, const float* dl,
+                                     const float* ebar, const float* e, const float* sl1, const float* sl2,
+                                     int const_mode, const float* col_log_probs, int use_col_weights,
+                                     const int* node_child1, const int* node_child2, const int* node_parent,
+                                     const int* jumps, int K, const long long* lv_ptr, int n_levels,
+                                     const int* lv_par, const int* lv_c1, const int* lv_c2, int use_leaf_index,
+                                     const int* leaf_state, const float* leaf_logp, int leaf_mode,
+                                     const float* leaf_term, const long long* item_idx, const float* x,
+                                     long long x_row_stride, float* y, int ws, int W, int S, void* stream) {
+  if (S <= 0 || W < 0 || K < 0 || n_levels < 0 || !x || !y) return KB_ERR_ARG;
+  if (S > KB_MAX_S) return KB_ERR_SIZE;
+  if (W == 0) return KB_OK;
+  AdjArgs a = adjoint_args(Pi, Pibar, pibar_row_max, dts, active, dl, ebar, e, sl1, sl2, const_mode, col_log_probs,
+                           use_col_weights, node_child1, node_child2, node_parent, jumps, K, lv_ptr, n_levels,
+                           lv_par, lv_c1, lv_c2, use_leaf_index, leaf_state, leaf_logp, leaf_mode, leaf_term,
+                           item_idx, ws, W, S);
+  a.apply_in = x; a.apply_rs = x_row_stride; a.apply_out = y;
+  return launch_adjoint(a, stream);
 }
 
 extern "C" int kb_dts_adjoint(const float* Pi, const float* Pibar, const float* v_k, const unsigned char* active,

@@ -241,7 +241,8 @@ def root_rhs(Pi, root_ids):
 
 
 @torch.no_grad()
-def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumulation=False, cache=None):
+def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumulation=False, cache=None,
+                  collect_backward_relres=False):
     """Reference ``_implicit_grad.py:98-370`` followed by :func:`e_adjoint_and_theta_vjp`.
 
     ``exact_accumulation=False`` reproduces the reference's accumulation exactly: every wave's
@@ -256,7 +257,12 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
     ``newton/hvp_exact.py:37-45``): ``waves`` -- per wave in the order processed (reverse wave
     order) ``ws, W, v`` (adjoint rows, zero on inactive rows), ``dts_r, active_mask, has_splits,
     has_leaf_term, meta`` --, ``accum`` (the column cotangent accumulators) and ``wE`` (the
-    E-side adjoint)."""
+    E-side adjoint).
+
+    ``collect_backward_relres`` (reference ``_implicit_grad.py:117,189-195,263-288,355``): the
+    reverse wave loop runs as usual, then ``(relres, vk_mag)`` is returned instead of the
+    gradients -- per family the largest ``|last Neumann term| / |v|`` and the largest ``|v|`` over
+    its active rows."""
     so = static.solver_options
     wl, sh = static.wave_layout, static.state_helpers
     Pi, Pibar = saved["pi_wave"], saved["pibar_wave"]
@@ -276,6 +282,11 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
     item_idx = static.rate_item_idx
     leaf_state = wl["leaf_state_index"].to(device=dev, dtype=torch.int32).contiguous()
     chunk = 64 if exact_accumulation else None
+    if collect_backward_relres:
+        row_item = wl["item_idx"].to(device=dev, dtype=torch.long)
+        n_fam = int(row_item.max().item()) + 1 if row_item.numel() else 0
+        relres = torch.zeros(n_fam, device=dev, dtype=torch.float32)
+        vk_mag = torch.zeros(n_fam, device=dev, dtype=torch.float32)
 
     def flush():
         for n in ("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2"):
@@ -303,8 +314,15 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
                 item_idx=item_idx, item_indexed_consts=True, compact_level_ptr=sh["compact_level_ptr"],
                 compact_level_parents=sh["compact_level_parents"], compact_level_child1=sh["compact_level_child1"],
                 compact_level_child2=sh["compact_level_child2"], grad_col_log_probs=g.col, use_col_weights=ucw,
-                self_loop_solver=so.self_loop_solver)
-            vb, aw0, aw1, aw2, aw345, aw3, aw4 = out
+                self_loop_solver=so.self_loop_solver, return_last_increment=collect_backward_relres)
+            vb, aw0, aw1, aw2, aw345, aw3, aw4 = out[:7]
+            if collect_backward_relres:
+                wave_item = row_item[ws + a:ws + b]
+                on = active[a:b].reshape(b - a, -1).ne(0).any(dim=1)
+                vk_norm = torch.where(on, vb.float().norm(dim=1), torch.zeros_like(vb[:, 0]))
+                vk_mag.scatter_reduce_(0, wave_item, vk_norm, reduce="amax", include_self=True)
+                if out[7] is not None:
+                    relres.scatter_reduce_(0, wave_item, out[7].float(), reduce="amax", include_self=True)
             v_k[a:b] = vb
             dbg = getattr(static, "_debug_sums", None)
             if dbg is not None:
@@ -349,6 +367,8 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
                     side_active_threshold=so.pibar_side_threshold)
                 if exact_accumulation:
                     flush()
+    if collect_backward_relres:
+        return relres, vk_mag
     if exact_accumulation:
         for n in ("pD", "pS", "mt", "E", "Ebar", "E_s1", "E_s2"):
             getattr(g, n)[0] = g_total[n].float()

@@ -60,6 +60,47 @@ def _leaf_mode(use_leaf_index, leaf_logp, item_idx, item_indexed):
     return 0
 
 
+def _gmres_fixed(apply_a, b, max_iter: int):
+    """Solve ``A v = b`` by unrestarted GMRES with a fixed number of Arnoldi steps, the whole wave
+    ``[W,S]`` being ONE vector (reference ``wave_backward.py:831-912``): the Krylov basis is built
+    by classical Gram-Schmidt with one re-orthogonalisation pass, the iteration stops early when
+    the new basis vector's norm falls to ``eps * max(|b|, 1)``, and ``v`` minimises the residual
+    through the least-squares solve of the small Hessenberg system.  ``apply_a`` (one launch of
+    the row operator) runs on the device; the dense orthogonalisation is a few matrix-vector
+    products over the basis."""
+    m = int(max_iter)
+    if m < 1:
+        return torch.zeros_like(b)
+    beta = torch.linalg.vector_norm(b)
+    if float(beta) == 0.0:
+        return torch.zeros_like(b)
+    dt, dev = b.dtype, b.device
+    basis = torch.empty((m + 1, b.numel()), dtype=dt, device=dev)
+    basis[0] = b.reshape(-1) / beta
+    hess = torch.zeros((m + 1, m), dtype=dt, device=dev)
+    g = torch.zeros((m + 1,), dtype=dt, device=dev)
+    g[0] = beta
+    steps = m
+    stop = torch.finfo(dt).eps * torch.clamp(beta, min=1.0)
+    for j in range(m):
+        w = apply_a(basis[j].view(b.shape)).reshape(-1)
+        q = basis[: j + 1]
+        h1 = torch.mv(q, w)
+        w1 = torch.addmv(w, q.t(), h1, beta=1.0, alpha=-1.0)
+        h2 = torch.mv(q, w1)
+        w2 = torch.addmv(w1, q.t(), h2, beta=1.0, alpha=-1.0)
+        hess[: j + 1, j] = h1 + h2
+        nrm = torch.linalg.vector_norm(w2)
+        hess[j + 1, j] = nrm
+        if bool(nrm <= stop):
+            steps = j + 1
+            break
+        if j + 1 < m:
+            basis[j + 1] = w2 / torch.clamp(nrm, min=torch.finfo(dt).tiny)
+    y = torch.linalg.lstsq(hess[: steps + 1, :steps], g[: steps + 1]).solution
+    return torch.mv(basis[:steps].t(), y).view(b.shape)
+
+
 def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_squeezed, DL_const, Ebar, E,
                                 SL1_const, SL2_const, col_log_probs, node_child1, node_child2, leaf_term_wt,
                                 neumann_terms=3, leaf_state_idx=None, leaf_logp=None, has_leaf_term=True,
@@ -68,16 +109,22 @@ def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_sq
                                 compact_level_parents=None, compact_level_child1=None, compact_level_child2=None,
                                 grad_col_log_probs=None, use_col_weights=True, self_loop_grad_targets=None,
                                 initial_v=None, self_loop_solver="neumann", return_last_increment=False):
-    """Reference ``wave_backward.py:1737-1867``: per active row, the Neumann-series adjoint
-    ``v = sum_{n=0..N} (J_self^T)^n rhs`` and the per-element parameter cotangents.
+    """Reference ``wave_backward.py:1737-1867``: per active row, the adjoint ``v`` of the self-loop
+    -- ``self_loop_solver="neumann"``: the series ``v = sum_{n=0..N} (J_self^T)^n rhs``;
+    ``"gmres"``: ``N`` GMRES steps on ``(I - J_self^T) v = rhs`` over the whole wave -- and the
+    per-element parameter cotangents.
 
     Returns ``(v_k, aw0, aw1, aw2, aw345, aw3, aw4)`` (new [W,S] tensors; aw* zero and v_k
-    unspecified on inactive rows); accumulates ``grad_col_log_probs`` in place."""
+    unspecified on inactive rows in the Neumann solve, zero in the GMRES solve), plus, with
+    ``return_last_increment``, the per-row ``|last Neumann term| / |v|`` ([W], zero on inactive
+    rows; None for the GMRES solve or N = 0, as the reference); accumulates ``grad_col_log_probs``
+    in place."""
     require_cuda_f32("GPUREC self-loop 2D fast path", Pi_star, Pibar_star, rhs)
-    if str(self_loop_solver).strip().lower() != "neumann":
-        raise NotImplementedError("self_loop_solver='gmres' is not implemented by the sm_100a backend")
-    if initial_v is not None or self_loop_grad_targets is not None or return_last_increment:
-        raise NotImplementedError("initial_v / self_loop_grad_targets / return_last_increment are not supported")
+    solver = str(self_loop_solver).strip().lower()
+    if solver not in ("neumann", "gmres"):
+        raise ValueError(f"unsupported self-loop solver {self_loop_solver!r}")
+    if initial_v is not None or self_loop_grad_targets is not None:
+        raise NotImplementedError("initial_v / self_loop_grad_targets are not supported")
     requested_has_leaf_term = bool(has_leaf_term)
     use_leaf_index = requested_has_leaf_term and leaf_state_idx is not None and leaf_logp is not None
     const_mode = _const_mode(DL_const, item_idx, bool(item_indexed_consts))
@@ -103,26 +150,47 @@ def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_sq
                      compact_level_child1=compact_level_child1, compact_level_child2=compact_level_child2)
     shape = (W, S)
     v_k, aw0, aw1, aw2, aw345, aw3, aw4 = (torch.empty(shape, device=dev, dtype=torch.float32) for _ in range(7))
+    want_rel = bool(return_last_increment) and solver == "neumann" and int(neumann_terms) > 0
+    last_rel = torch.empty((W,), device=dev, dtype=torch.float32) if want_rel else None
+    out = (v_k, aw0, aw1, aw2, aw345, aw3, aw4)
     if W == 0:
-        return v_k, aw0, aw1, aw2, aw345, aw3, aw4
+        return (*out, last_rel) if return_last_increment else out
     has_materialized = leaf_term_wt is not None
     leaf_term = None
     if requested_has_leaf_term and not use_leaf_index and has_materialized:
         leaf_term = f32(leaf_term_wt)
+    st = _lib.stream_handle(dev)
+    mask_u8 = u8(active_mask)
+    head = (f32(Pi_star).data_ptr(), f32(Pibar_star).data_ptr(), f32(pibar_row_max).data_ptr(),
+            _lib.ptr(None if dts_r is None else f32(dts_r)))
+    tail = (_lib.ptr(mask_u8), f32(DL_const).data_ptr(), f32(Ebar).data_ptr(), f32(E).data_ptr(),
+            f32(SL1_const).data_ptr(), f32(SL2_const).data_ptr(), const_mode, f32(col_log_probs).data_ptr(),
+            int(bool(use_col_weights)), tt.child1.data_ptr(), tt.child2.data_ptr(), tt.parent.data_ptr(),
+            tt.jumps.data_ptr(), tt.K, tt.lv_ptr.data_ptr(), tt.n_levels, tt.lv_par.data_ptr(), tt.lv_c1.data_ptr(),
+            tt.lv_c2.data_ptr(), int(use_leaf_index), _lib.ptr(i32(leaf_state_idx) if use_leaf_index else None),
+            _lib.ptr(f32(leaf_logp) if use_leaf_index else None), leaf_mode, _lib.ptr(leaf_term),
+            _lib.ptr(i64(item_idx)))
+    n_terms = int(neumann_terms)
     rhs_c = rhs if rhs.stride(1) == 1 else rhs.contiguous()
-    _lib.call("kb_wave_adjoint", f32(Pi_star).data_ptr(), f32(Pibar_star).data_ptr(),
-              f32(pibar_row_max).data_ptr(), _lib.ptr(None if dts_r is None else f32(dts_r)), rhs_c.data_ptr(),
-              int(rhs_c.stride(0)), _lib.ptr(u8(active_mask)), f32(DL_const).data_ptr(), f32(Ebar).data_ptr(),
-              f32(E).data_ptr(), f32(SL1_const).data_ptr(), f32(SL2_const).data_ptr(), const_mode,
-              f32(col_log_probs).data_ptr(), int(bool(use_col_weights)), tt.child1.data_ptr(),
-              tt.child2.data_ptr(), tt.parent.data_ptr(), tt.jumps.data_ptr(), tt.K, tt.lv_ptr.data_ptr(),
-              tt.n_levels, tt.lv_par.data_ptr(), tt.lv_c1.data_ptr(), tt.lv_c2.data_ptr(), int(use_leaf_index),
-              _lib.ptr(i32(leaf_state_idx) if use_leaf_index else None),
-              _lib.ptr(f32(leaf_logp) if use_leaf_index else None), leaf_mode, _lib.ptr(leaf_term),
-              _lib.ptr(i64(item_idx)), int(neumann_terms), _lib.ptr(grad_col_log_probs), v_k.data_ptr(),
-              aw0.data_ptr(), aw1.data_ptr(), aw2.data_ptr(), aw345.data_ptr(), aw3.data_ptr(), aw4.data_ptr(),
-              ws, W, S, _lib.stream_handle(dev))
-    return v_k, aw0, aw1, aw2, aw345, aw3, aw4
+    if solver == "gmres":
+        b = rhs_c.float().reshape(W, S)
+        if active_mask is not None:
+            b = b * active_mask.reshape(W, -1).to(device=dev, dtype=torch.bool).any(dim=1, keepdim=True).float()
+        b = b.contiguous()
+        a_out = torch.empty(shape, device=dev, dtype=torch.float32)
+
+        def apply_a(x):
+            x = x.contiguous()
+            _lib.call("kb_wave_adjoint_apply", *head, *tail, x.data_ptr(), S, a_out.data_ptr(), ws, W, S, st)
+            return a_out
+
+        v = _gmres_fixed(apply_a, b, n_terms).contiguous()
+        v_k.copy_(v)
+        rhs_c, n_terms = v, 0  # the buckets and the column gradient of the solved rows
+    _lib.call("kb_wave_adjoint", *head, rhs_c.data_ptr(), int(rhs_c.stride(0)), *tail, n_terms,
+              _lib.ptr(grad_col_log_probs), v_k.data_ptr(), aw0.data_ptr(), aw1.data_ptr(), aw2.data_ptr(),
+              aw345.data_ptr(), aw3.data_ptr(), aw4.data_ptr(), _lib.ptr(last_rel), ws, W, S, st)
+    return (*out, last_rel) if return_last_increment else out
 
 
 def _param_ref(param, *, S, item_indexed, device):

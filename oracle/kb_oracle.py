@@ -562,14 +562,57 @@ def _self_loop_terms(Pi, Pibar, rows, consts, tree, leaf_state, leaf_logp, dts_r
     return e, inv_sum, w_L
 
 
+def gmres_fixed(apply_a, b, max_iter):
+    """Unrestarted GMRES with a fixed number of Arnoldi steps (``kbench/core/kernels/
+    wave_backward.py:831-912``, ``experiments/pristine_kernels/wave_backward.py:574-655``): the
+    Krylov basis by classical Gram-Schmidt with one re-orthogonalisation pass, an early stop when
+    the new vector's norm falls to ``eps * max(|b|, 1)``, and the least-squares solve of the
+    Hessenberg system.  ``b`` is the whole wave as one vector."""
+    m = int(max_iter)
+    shape = b.shape
+    b = _f(b).reshape(-1)
+    if m < 1:
+        return np.zeros(shape, F32)
+    beta = F32(np.sqrt(np.dot(b, b)))
+    if float(beta) == 0.0:
+        return np.zeros(shape, F32)
+    V = np.zeros((m + 1, b.size), F32)
+    V[0] = b / beta
+    H = np.zeros((m + 1, m), F32)
+    g = np.zeros(m + 1, F32)
+    g[0] = beta
+    steps = m
+    stop = F32(np.finfo(F32).eps) * max(beta, F32(1.0))
+    for j in range(m):
+        w = _f(apply_a(V[j].reshape(shape))).reshape(-1)
+        Q = V[: j + 1]
+        h1 = (Q @ w).astype(F32)
+        w1 = (w - Q.T @ h1).astype(F32)
+        h2 = (Q @ w1).astype(F32)
+        w2 = (w1 - Q.T @ h2).astype(F32)
+        H[: j + 1, j] = h1 + h2
+        nrm = F32(np.sqrt(np.dot(w2, w2)))
+        H[j + 1, j] = nrm
+        if nrm <= stop:
+            steps = j + 1
+            break
+        if j + 1 < m:
+            V[j + 1] = w2 / max(nrm, F32(np.finfo(F32).tiny))
+    y = np.linalg.lstsq(H[: steps + 1, :steps], g[: steps + 1], rcond=None)[0].astype(F32)
+    return (V[:steps].T @ y).astype(F32).reshape(shape)
+
+
 def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, tree: Tree,
                   *, neumann_terms, leaf_state=None, leaf_logp=None, active=None,
-                  grad_col=None, use_col_weights=False):
+                  grad_col=None, use_col_weights=False, self_loop_solver="neumann", last_out=None):
     """``wave_backward_uniform_fused`` (``experiments/pristine_kernels/wave_backward.py:
-    1270-1736`` retained 2D path): precompute (``:203-417``), Neumann ``v = sum_n (J^T)^n rhs``
-    (``:419-570``), column gradient (``:654-745``) and the parameter store (``:747-966``).
-    Returns (v_k, aw0, aw1, aw2, aw345, aw3, aw4); v_k rows of inactive rows are NaN
-    (uninitialised in the reference)."""
+    1270-1736`` retained 2D path): precompute (``:203-417``), the self-loop adjoint -- Neumann
+    ``v = sum_n (J^T)^n rhs`` (``:419-570``) or GMRES on ``(I - J^T) v = rhs`` over the wave's
+    active rows (``:1136-1185``) --, column gradient (``:654-745``) and the parameter store
+    (``:747-966``).  Returns (v_k, aw0, aw1, aw2, aw345, aw3, aw4); v_k rows of inactive rows are
+    NaN in the Neumann solve (uninitialised in the reference), zero in the GMRES solve.
+    ``last_out`` ([W], Neumann with at least one term) receives ``|last term| / |v|`` per row
+    (zero on inactive rows; ``:1275-1292``)."""
     S = tree.S
     act = np.ones(W, dtype=bool) if active is None else np.asarray(active, dtype=bool)
     rows_l = np.nonzero(act)[0]
@@ -602,16 +645,29 @@ def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, t
     par_ok = par >= 0
     par_safe = np.where(par_ok, par, 0)
     rhs_a = _f(rhs)[rows_l]
-    v = rhs_a.copy()
-    term = rhs_a
-    for _ in range(int(neumann_terms)):
+
+    def jt(term):
         u = (term * coeff).astype(F32)
         A = u.sum(axis=-1, dtype=F32)
         corr = tree.subtree_sums_inplace(u.copy())
         base = (term * diag + p_prime * (A[:, None] - corr)).astype(F32)
-        res = (base + np.where(par_ok, term[:, par_safe], F32(0.0)) * edge).astype(F32)
-        v = (v + res).astype(F32)
-        term = res
+        return (base + np.where(par_ok, term[:, par_safe], F32(0.0)) * edge).astype(F32)
+
+    if str(self_loop_solver).strip().lower() == "gmres":
+        v = gmres_fixed(lambda x: (x - jt(x)).astype(F32), rhs_a, int(neumann_terms))
+        v_k[:] = F32(0.0)
+    else:
+        v = rhs_a.copy()
+        term = rhs_a
+        for _ in range(int(neumann_terms)):
+            res = jt(term)
+            v = (v + res).astype(F32)
+            term = res
+        if last_out is not None and int(neumann_terms) > 0:
+            last_out[:] = F32(0.0)
+            num = np.sqrt((term.astype(np.float64) ** 2).sum(axis=-1))
+            den = np.maximum(np.sqrt((v.astype(np.float64) ** 2).sum(axis=-1)), np.finfo(np.float32).tiny)
+            last_out[rows_l] = (num / den).astype(F32)
     v_k[rows_l] = v
     if grad_col is not None:
         u = (v * coeff).astype(F32)
@@ -770,7 +826,7 @@ def backward(static: dict, theta, col_weights, saved: dict, acc_dtype=F32):
 
 
 def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list | None = None,
-                          use_col_weights: bool = False) -> dict:
+                          use_col_weights: bool = False, relres: dict | None = None) -> dict:
     """The reverse wave loop of ``kbench/api/_implicit_grad.py:98-370`` alone: the fp32 column
     accumulators ``pD, pS, mt, E, Ebar, E_s1, E_s2, col`` (``:144-158``) that the E adjoint and
     theta VJP consume.
@@ -782,7 +838,11 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
 
     ``cache`` (a list) receives one dict per wave in the order processed (reverse wave order):
     ``ws, W, v`` (the adjoint rows, zero on inactive rows), ``dts_r, active, has_splits, meta``
-    -- the point cache of the exact-Hessian HVP (``newton/ggn.py:152-162``)."""
+    -- the point cache of the exact-Hessian HVP (``newton/ggn.py:152-162``).
+
+    ``relres`` (a dict) receives the reference glue's ``collect_backward_relres`` diagnostics
+    (``kbench/api/_implicit_grad.py:189-195, 263-288``): per family the largest
+    ``|last Neumann term| / |v|`` (``relres``) and largest ``|v|`` (``vk_mag``) over active rows."""
     sh = static["state_helpers"]
     wl = static["wave_layout"]
     so = static["solver_options"]
@@ -807,6 +867,12 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
     rp = Pi[roots]
     acc[roots] = -_safe_exp2_ratio(rp, lse_rows(rp)[:, None])
     leaf_state_all = np.asarray(wl["leaf_state_index"], dtype=np.int64)
+    solver = so.get("self_loop_solver", "neumann")
+    if relres is not None:
+        row_item = np.asarray(wl["item_idx"], dtype=np.int64)
+        n_fam = int(row_item.max()) + 1 if row_item.size else 0
+        relres["relres"] = np.zeros(n_fam, F32)
+        relres["vk_mag"] = np.zeros(n_fam, F32)
     thr = float(so.get("adjoint_pruning_threshold", 1e-6))
     prune = bool(so.get("use_adjoint_pruning", True))
     for meta in reversed(wl["wave_metas"]):
@@ -815,11 +881,19 @@ def backward_accumulators(static: dict, saved: dict, acc_dtype=F32, cache: list 
         act = active_mask(rhs, thr, prune)
         has_splits = "sl" in meta
         dts_r = dts_forward(Pi, Pibar, meta, pD, pS, tree, active=act) if has_splits else None
+        last = np.zeros(W, F32) if relres is not None else None
         v_k, aw0, aw1, aw2, aw345, aw3, aw4 = wave_backward(
             Pi, Pibar, row_max, ws, W, dts_r, rhs, consts, col_logp, tree,
             neumann_terms=int(so["neumann_terms"]),
             leaf_state=None if has_splits else leaf_state_all[ws:ws + W],
-            leaf_logp=pS, active=act, grad_col=g_col, use_col_weights=use_col_weights)
+            leaf_logp=pS, active=act, grad_col=g_col, use_col_weights=use_col_weights,
+            self_loop_solver=solver, last_out=last)
+        if relres is not None:
+            items = row_item[ws:ws + W]
+            vn = np.where(act, np.sqrt((np.nan_to_num(v_k).astype(np.float64) ** 2).sum(axis=-1)), 0.0)
+            np.maximum.at(relres["vk_mag"], items, vn.astype(F32))
+            if str(solver).strip().lower() == "neumann" and int(so["neumann_terms"]) > 0:
+                np.maximum.at(relres["relres"], items, last)
         if cache is not None:
             cache.append(dict(ws=ws, W=W, v=np.where(act[:, None], v_k, F32(0.0)).astype(F32), dts_r=dts_r,
                               active=act, has_splits=has_splits, meta=meta))

@@ -101,12 +101,19 @@ CASES = {
     "weighted_s31": (gen.ProblemConfig("weighted", 16, 20, 4, 10, 0), 3131, {"_col_weights_seed": 77}),
     # the other adjoint options: no activity pruning, and a Pibar-side activity threshold
     "options_s63": (1, 6363, {"use_adjoint_pruning": False, "pibar_side_threshold": 1e-3}),
+    # the GMRES self-loop solver (neumann_terms = Arnoldi steps per wave)
+    "gmres_s64": (1, 6464, {"self_loop_solver": "gmres", "neumann_terms": 8}),
+    # the backward's convergence diagnostics (collect_backward_relres: per family the largest
+    # |last Neumann term| / |v| and |v|), on a two-family problem
+    "relres_s32": (gen.ProblemConfig("relres", 16, 20, 4, 10, 60, n_families=2), 3232,
+                   {"pi_iters": 6, "neumann_terms": 4, "_collect_relres": True}),
 }
 
 
 def run_case(runtime, name, cfg, seed, overrides):
     overrides = dict(overrides)
     cw_seed = overrides.pop("_col_weights_seed", None)
+    collect_relres = overrides.pop("_collect_relres", False)
     cap = gen.generate(cfg, seed=seed, solver_options=overrides)
     if cw_seed is not None:
         S = int(cap["meta"]["S"])
@@ -127,10 +134,34 @@ def run_case(runtime, name, cfg, seed, overrides):
     }
     for k, v in saved.items():
         out[k] = v.detach().numpy()
+    if collect_relres:
+        relres, vk_mag = backward_relres(static, theta, cw, saved)
+        out["relres"] = relres.detach().numpy()
+        out["vk_mag"] = vk_mag.detach().numpy()
     arrays = flatten_case(cap, out)
     np.savez_compressed(HERE / f"{name}.npz", **arrays)
     print(f"[{name}] S={cap['meta']['S']} C={cap['meta']['C']} waves={cap['meta']['n_waves']} "
           f"loss={float(loss):.6f} fwd {t1 - t0:.1f}s bwd {t2 - t1:.1f}s")
+
+
+def backward_relres(static, theta, cw, saved):
+    """The reference glue's backward with ``collect_backward_relres=True`` (same arguments as
+    ``kbench/runtime.py:77-115`` passes): per family (relres, vk_mag)."""
+    from kbench.api._implicit_grad import implicit_grad_loglik_vjp_wave
+    from kbench.core.inference.solver import col_weights_are_uniform
+    so = static.solver_options
+    return implicit_grad_loglik_vjp_wave(
+        static.wave_layout, static.state_helpers, Pi_star_wave=saved["pi_wave"],
+        Pibar_star_wave=saved["pibar_wave"], E_star=saved["E"], Ebar=saved["Ebar"], E_s1=saved["E_s1"],
+        E_s2=saved["E_s2"], log_pS=saved["log_pS"], log_pD=saved["log_pD"], log_pL=saved["log_pL"],
+        max_coupling_mat=saved["max_coupling"], col_log_probs=saved["col_log_probs"],
+        use_col_weights=not col_weights_are_uniform(cw), theta=theta, col_weights=cw,
+        item_idx=static.rate_item_idx, uniform_pibar_row_max=saved["pibar_row_max"], statewise=static.statewise,
+        itemwise=static.itemwise, neumann_terms=so.neumann_terms, self_loop_solver=so.self_loop_solver,
+        bicgstab_max_iter=so.bicgstab_max_iter, bicgstab_tol=so.bicgstab_tol,
+        bicgstab_breakdown_tol=so.bicgstab_breakdown_tol, adjoint_pruning_threshold=so.adjoint_pruning_threshold,
+        use_adjoint_pruning=so.use_adjoint_pruning, pibar_side_threshold=so.pibar_side_threshold,
+        collect_backward_relres=True)
 
 
 TANGENT_DIRECTIONS = 2

@@ -35,3 +35,23 @@ def test_forward_backward_vs_reference_golden(name, engine, cuda):
         assert_close(k, saved[k].cpu().numpy(), out[k])
     assert_close("grad_theta", gt.cpu().numpy(), out["grad_theta"])
     assert_close("grad_col", gc.cpu().numpy(), out["grad_col"])
+
+
+RELRES = [n for n in NAMES if "relres" in load_golden(n)[1]]
+
+
+@pytest.mark.parametrize("name", RELRES)
+def test_backward_relres_vs_reference_golden(name, cuda):
+    """``return_last_increment`` through the call-by-call driver's ``collect_backward_relres``
+    (the reference glue's diagnostics mode) against the reference's values."""
+    from kbench_b200 import gen, glue, runtime
+    cap, out = load_golden(name)
+    capt = gen.to_torch(cap)
+    static = runtime.make_static(capt, cuda, engine="wrappers")
+    theta = capt["inputs"]["theta"].to(cuda)
+    cw = capt["inputs"]["col_weights"].to(cuda)
+    gsaved = {k: torch.as_tensor(out[k]).to(cuda) for k in runtime.FORWARD_SAVED_NAMES if k in out}
+    gsaved["root_rows"] = gsaved["pi_wave"][static.wave_layout["root_row_ids"]]
+    relres, vk_mag = glue.implicit_grad(static, theta, cw, gsaved, collect_backward_relres=True)
+    assert_close("relres", relres.cpu().numpy(), out["relres"])
+    assert_close("vk_mag", vk_mag.cpu().numpy(), out["vk_mag"])

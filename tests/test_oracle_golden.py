@@ -42,3 +42,19 @@ def test_planted_mistake_is_caught():
     bad[bad.shape[0] // 2, 3] += 0.01
     with pytest.raises(AssertionError):
         assert_close("pi_wave", bad, out["pi_wave"])
+
+
+RELRES = [n for n in NAMES if "relres" in load_golden(n)[1]]
+
+
+@pytest.mark.parametrize("name", RELRES)
+def test_oracle_backward_relres_matches_reference(name):
+    """The backward's convergence diagnostics (reference glue with ``collect_backward_relres``):
+    per family the largest |last Neumann term| / |v| and the largest |v|."""
+    cap, out = load_golden(name)
+    saved = {k: out[k] for k in SAVED}
+    rel: dict = {}
+    O.backward_accumulators(oracle_static(cap), saved, relres=rel,
+                            use_col_weights=not O.col_weights_are_uniform(cap["inputs"]["col_weights"]))
+    assert_close("relres", rel["relres"], out["relres"])
+    assert_close("vk_mag", rel["vk_mag"], out["vk_mag"])
