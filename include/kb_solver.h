@@ -298,7 +298,10 @@ int kb_lin_consts(const float* dl, const float* ebar, const float* mc, const flo
  * runs (dts_save and tour_consts, from kb_lin_consts_tour, must then be non-NULL).  Otherwise
  * packed: the [5,NTV] tables of pack_columns(..., ntv) with NTV from the engine width, of which
  * this kernel reads rows 0-3 (children, Euler-tour enter/exit, preorder start/end, parent |
- * first-child flag; two 16-bit fields each). */
+ * first-child flag; two 16-bit fields each).  The row iterations run in linear space relative to
+ * a per-row scale; rows outside its exact range (see kb_engine.cu) are recomputed in log space
+ * and counted in fallback_count; force_log_space != 0 sends every row there (set by the caller
+ * when a constant 2^dl+2^ebar, 2^(mc+e), 2^sl1 or 2^sl2 is below 2^-26). */
 int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, const long long* sl,
                      const long long* sr, const float* lsp, const float* Pi_src, const float* Pibar_src, float* pi,
                      float* pibar, float* pibar_row_max, float* dts_save, float* residual, int* fallback_count,
@@ -309,7 +312,8 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
                      int use_col_weights, const int* node_parent, const int* node_child1, const int* node_child2,
                      const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                      const long long* item_idx, const int* leaf_state, const unsigned* packed,
-                     const unsigned* tour_tables, const float* tour_consts, int pi_iters, int S, void* stream);
+                     const unsigned* tour_tables, const float* tour_consts, int force_log_space, int pi_iters,
+                     int S, void* stream);
 
 /* The whole forward wave sweep in ONE persistent launch with a dataflow schedule (replaces the
  * per-level kb_level_forward launches, same per-row arithmetic as its tour kernel): a row starts
@@ -330,7 +334,7 @@ int kb_flow_forward(int C, const long long* row_split_ptr, const long long* sl, 
                     const int* node_parent, const int* node_child1, const int* node_child2,
                     const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                     const long long* item_idx, const int* leaf_state, const unsigned* tour_tables,
-                    const float* tour_consts, int pi_iters, int S, void* stream);
+                    const float* tour_consts, int force_log_space, int pi_iters, int S, void* stream);
 
 /* The tour kernel's per-column constants, interleaved and zero-padded to NTV = kb_tour_layout(S):
  * out4 [G, NTV, 4] = (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2) from the [G,S] constant rows. */

@@ -17,7 +17,12 @@
 // iteration costs FMAs and shared-memory gathers instead of ~10 MUFU ex2/lg2 per element.  The
 // row is renormalised by its max every iteration (P <= 1).  If any nonzero element falls below
 // 2^-100 of the row max (where fp32 linear values would lose precision) the row is recomputed
-// with the log-space iteration, so results never silently degrade.  Final Pi, Pibar and the row
+// with the log-space iteration, so results never silently degrade.  The same holds only while
+// every product of a kept value (>= 2^-100) with a constant 2^dl+2^ebar, 2^(mc+e), 2^sl1, 2^sl2,
+// or with the dts / leaf rescaling 2^(Rd-R), stays a normal fp32 number (>= 2^-126): a row whose
+// initial values span more than 100 binades, or whose scale grows by more than 2^26, takes the
+// log-space path too, and a problem whose constants fall below 2^-26 (extreme rates) sets
+// force_log so that every row does.  Final Pi, Pibar and the row
 // max are written once; the split reduction is also saved for the backward.
 //
 // Backward.  Reverse level order (a row's adjoint is complete once every level above it ran).
@@ -210,6 +215,7 @@ struct FwdArgs {
   float* dts_save;  // [C,S] or null
   float* residual;  // [C] or null
   int* fallback_count;  // device counter of rows recomputed in log space (may be null)
+  int force_log;        // every row takes the log-space iteration (constants below 2^-26)
   int n_rows;
   int pi_iters;
 };
@@ -384,9 +390,11 @@ __global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
   // with the dts / leaf terms taken relative to the new scale R + log2(zmax).
   float z[VPT], td[VPT];
   float zmax_l = 0.f, zsum_l = 0.f;
+  bool init_bad = a.force_log != 0;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
+    init_bad |= (s < S) && !is_neg_inf(x[k]) && (x[k] - Rd < -100.f);  // beyond the linear range
     z[k] = s < S ? ex2(x[k] - Rd) : 0.f;
     td[k] = is_leaf ? 0.f : z[k];
     PB[s] = z[k];
@@ -396,10 +404,10 @@ __global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
     zsum_l += z[k];
   }
   float R = Rd;
-  bool fallback = false;
+  bool fallback = __syncthreads_or(init_bad) != 0;
   int cur = 0;
   float dres = 0.f;  // last-iteration residual max|Pi_new - Pi_prev| (finite entries)
-  for (int it = 1; it < a.pi_iters; ++it) {
+  for (int it = 1; it < a.pi_iters && !fallback; ++it) {
     float* Tc = T2 + cur * 2 * NTV;
     float* Pc = PB + cur * NTV;
     float* Tn = T2 + (cur ^ 1) * 2 * NTV;
@@ -412,7 +420,7 @@ __global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
     const float fd = ex2(Rd - Rn);
     const float lf = is_leaf ? ex2(leafv - Rn) : 0.f;
     const float thresh = 7.8886091e-31f;  // 2^-100 of the (unit) row scale
-    bool bad = false;
+    bool bad = Rn - Rd > 26.f;  // dts / leaf terms rescaled below the normal range
     zmax_l = 0.f;
     zsum_l = 0.f;
 #pragma unroll
@@ -870,10 +878,12 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
   unsigned ce[VF], tr[VF];
   float z[VF], td[VF], kA[VF], kB[VF], kC1[VF], kC2[VF];
   float zmax_l = 0.f, zsum_l = 0.f;
+  bool bad = a.force_log != 0;
 #pragma unroll
   for (int k = 0; k < VF; ++k) {
     const int s = tid + k * NT;
     const bool real = s < S;
+    bad |= real && !is_neg_inf(x[k]) && (x[k] - Rd < -100.f);  // beyond the linear range
     ce[k] = __ldg(tb + NTV + s);
     tr[k] = __ldg(tb + 2 * NTV + s);
     const float4 kk = __ldg(k4 + s);  // zero on padded columns
@@ -886,7 +896,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     zsum_l += z[k];
   }
   float R = Rd;
-  bool bad = false, fallback = false;
+  bool fallback = false;
   float dres = 0.f;
   const int last = a.pi_iters - 1;
   for (int it = 1; it <= last; ++it) {
@@ -925,7 +935,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
         sts_at(Tn, tr[k] >> 16) = -zn;
       }
     }
-    bad = mincode < 0x0D7FFFFFu;  // bits(2^-100) - 1
+    bad = mincode < 0x0D7FFFFFu || Rn - Rd > 26.f;  // bits(2^-100) - 1; dts term below the normal range
     R = Rn;
   }
   if (!fallback && __syncthreads_or(bad)) fallback = true;
@@ -2415,8 +2425,8 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
                                 const int* node_parent, const int* node_child1, const int* node_child2,
                                 const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                                 const long long* item_idx, const int* leaf_state, const unsigned* packed,
-                                const unsigned* tour_tables, const float* tour_consts, int pi_iters, int S,
-                                void* stream) {
+                                const unsigned* tour_tables, const float* tour_consts, int force_log_space,
+                                int pi_iters, int S, void* stream) {
   if (S <= 0 || n_rows < 0 || K < 0 || pi_iters < 2 || use_col_weights != 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
@@ -2428,6 +2438,7 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   a.sp = SplitCSR{rows, split_ptr, sl, sr, lsp};
   a.Pi_src = Pi_src; a.Pibar_src = Pibar_src; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = n_rows;
+  a.force_log = force_log_space != 0;
   a.pi_iters = pi_iters;
   cudaStream_t st = (cudaStream_t)stream;
   int nt4, vf4;
@@ -2628,7 +2639,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
                                const int* node_child1, const int* node_child2, const int* node_subtree_start,
                                const int* node_subtree_end, const int* jumps, int K, const long long* item_idx,
                                const int* leaf_state, const unsigned* tour_tables, const float* tour_consts,
-                               int pi_iters, int S, void* stream) {
+                               int force_log_space, int pi_iters, int S, void* stream) {
   if (S <= 0 || C < 0 || K < 0 || pi_iters < 2 || n_ready0 < 0 || n_ready0 > C || max_polls < 1) return KB_ERR_ARG;
   if (tour_tables == nullptr || tour_consts == nullptr || dts_save == nullptr || counters == nullptr) return KB_ERR_ARG;
   int nt, vf;
@@ -2644,6 +2655,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
   a.sp = SplitCSR{nullptr, nullptr, sl, sr, lsp};
   a.Pi_src = pi; a.Pibar_src = pibar; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = C;
+  a.force_log = force_log_space != 0;
   a.pi_iters = pi_iters;
   Fwd4Args a4;
   a4.f = a;

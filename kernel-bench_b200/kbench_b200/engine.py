@@ -213,6 +213,22 @@ class Prep:
     k: dict
     lin: torch.Tensor
     k4: torch.Tensor | None   # tour kernel constants [G, NTV, 4] (None where the tour kernel does not apply)
+    force_log: bool = False   # constants outside the linear iteration's exact range: every row in log space
+
+
+# Smallest log2 of a linear-iteration constant for which the forward kernels' linear-space update is
+# exact: nonzero row values are kept >= 2^-100 of the row scale (smaller ones send the row to the
+# log-space iteration), so a product with a constant >= 2^-26 stays >= 2^-126, a normal fp32 number.
+LINEAR_MIN_LOG2 = -26.0
+
+
+def linear_range_ok(k: dict) -> bool:
+    """Whether every finite exponent of the forward's linear constants -- log2(2^dl + 2^ebar) (at
+    least max(dl, ebar)), mc + e, sl1, sl2 -- is at least ``LINEAR_MIN_LOG2``.  Below it (extreme
+    rates) a term could underflow to zero where the reference's log-space update keeps it finite,
+    so the engine then runs every row's iterations in log space."""
+    ex = torch.stack([torch.maximum(k["dl"], k["ebar"]), k["mc"] + k["e"], k["sl1"], k["sl2"]])
+    return not bool(((ex < LINEAR_MIN_LOG2) & torch.isfinite(ex)).any())
 
 
 @torch.no_grad()
@@ -236,7 +252,7 @@ def prepare(static, theta, col_weights) -> Prep:
         _lib.call("kb_lin_consts_tour", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(),
                   k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), G, S, k4.data_ptr(),
                   _lib.stream_handle(dev))
-    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin, k4)
+    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin, k4, not linear_range_ok(k))
 
 
 def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | None = None):
@@ -291,7 +307,8 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                 k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(),
                 pSp.data_ptr(), prs, crs, tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
                 topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
-                leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), int(so.pi_iters), S, st)
+                leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), int(prep.force_log),
+                int(so.pi_iters), S, st)
         if int(fl["counters"][2].item()) != 0:
             raise RuntimeError("kb_flow_forward: a dataflow wait gave up (dependency counts inconsistent)")
         roots = pi[wl["root_row_ids"]]
@@ -311,7 +328,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                   tt.child1.data_ptr(), tt.child2.data_ptr(), topo.pre.data_ptr(), topo.pre_end.data_ptr(),
                   tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
                   _lib.ptr(tt.tour if use_tour else None), _lib.ptr(prep.k4 if use_tour else None),
-                  int(so.pi_iters), S, st)
+                  int(prep.force_log), int(so.pi_iters), S, st)
     roots = pi[wl["root_row_ids"]]
     out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
     return out, {"dts_wave": dts}

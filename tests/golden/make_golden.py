@@ -107,6 +107,13 @@ CASES = {
     # |last Neumann term| / |v| and |v|), on a two-family problem
     "relres_s32": (gen.ProblemConfig("relres", 16, 20, 4, 10, 60, n_families=2), 3232,
                    {"pi_iters": 6, "neumann_terms": 4, "_collect_relres": True}),
+    # rates off the benchmark distribution (theta columns shifted by (dup, loss, transfer) log2-odds):
+    # rows whose values span more than 100 binades (the forward kernels' per-row log-space
+    # recomputation), with every linear constant still >= 2^-26
+    "rowfallback_s63": (gen.ProblemConfig("y", 32, 48, 8, 80, 300), 11, {"_theta_shift": (0.0, 5.0, -10.0)}),
+    # transfer 2^-30 below the benchmark's: constants below 2^-26, every row in log space
+    "forcelog_s31": (gen.ProblemConfig("x", 16, 24, 4, 20, 60), 11,
+                     {"pi_iters": 6, "neumann_terms": 4, "_theta_shift": (0.0, 0.0, -30.0)}),
 }
 
 
@@ -114,7 +121,10 @@ def run_case(runtime, name, cfg, seed, overrides):
     overrides = dict(overrides)
     cw_seed = overrides.pop("_col_weights_seed", None)
     collect_relres = overrides.pop("_collect_relres", False)
+    theta_shift = overrides.pop("_theta_shift", None)
     cap = gen.generate(cfg, seed=seed, solver_options=overrides)
+    if theta_shift is not None:
+        cap["inputs"]["theta"] = cap["inputs"]["theta"] + torch.tensor(theta_shift, dtype=torch.float32)
     if cw_seed is not None:
         S = int(cap["meta"]["S"])
         w = np.random.Generator(np.random.PCG64(cw_seed)).standard_normal(S).astype(np.float32)

@@ -47,3 +47,23 @@ def test_dataflow_arrays_release_every_row_in_dependency_order(config, seed):
             assert pos[p] < pos[sl[n]] and pos[p] < pos[sr[n]]
     roots = cap["static"]["wave_layout"]["root_row_ids"].numpy()
     assert set(plan.ready_b.numpy().tolist()) == set(roots.tolist())
+
+
+def test_linear_range_decision():
+    """The engine sends every row to the log-space iteration exactly when a finite exponent of
+    the linear constants (max(dl, ebar), mc + e, sl1, sl2) is below 2^-26; -inf entries (absent
+    terms) do not count."""
+    import torch
+    from kbench_b200 import engine
+    S = 5
+    base = {k: torch.full((1, S), -3.0) for k in ("dl", "ebar", "mc", "e", "sl1", "sl2")}
+    assert engine.linear_range_ok(base)
+    k = dict(base, dl=torch.full((1, S), -40.0))  # hidden by ebar in 2^dl + 2^ebar
+    assert engine.linear_range_ok(k)
+    k = dict(base, dl=torch.full((1, S), -40.0), ebar=torch.full((1, S), -27.0))
+    assert not engine.linear_range_ok(k)
+    k = dict(base, mc=torch.full((1, S), -24.0))  # mc + e = -27
+    assert not engine.linear_range_ok(k)
+    sl = torch.full((1, S), -3.0)
+    sl[0, 2] = float("-inf")
+    assert engine.linear_range_ok(dict(base, sl1=sl))
