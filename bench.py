@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's own Triton path on this GPU (baseline/_ref) at N=1")
     ap.add_argument("--families", type=int, default=None, help="config 4: families in the whole batch")
     ap.add_argument("--chunk", type=int, default=128, help="config 4: families per chunk on a GPU")
     ap.add_argument("--directions", type=int, default=32, help="config 5: tangent directions per pass")
@@ -166,34 +168,27 @@ def algorithmic_bytes(plan, S):
     return fwd, bwd
 
 
-# DRAM bytes per row of the dataflow kernels at S = 4095, from one ncu capture on the config-3
-# species tree with a 12,709-row family (the capture runs ``bench.py --traffic-case``); rows
-# are independent units, so a full-family launch moves ~C times these.
-TRAFFIC_BYTES_PER_ROW_S4095 = {"kb_flow_forward": (782290944 + 542546688) / 12709,
-                               "kb_flow_backward": (2066200832 + 815406592) / 12709}
+# Counters of ONE launch of each dataflow kernel on the benchmark's own config-3 family (seed 3000,
+# C = 128,282 rows), from single-pass ncu captures of the full-size launches
+# (``bench.py --traffic-case config3``): DRAM bytes read and written, and warp instructions
+# executed.  Empty until captured for the current build; the bench then reports null.
+CONFIG3_ROWS = 128282
+CONFIG3_COUNTERS: dict = {}
 
 
-def launch_traffic(name, C, S):
-    """Measured-and-scaled DRAM bytes of one launch of ``name`` (None where not measured)."""
-    per_row = TRAFFIC_BYTES_PER_ROW_S4095.get(name)
-    return None if per_row is None or S != 4095 else round(per_row * C)
+def launch_counters(name, C, S):
+    """The captured counters of one launch of ``name`` on the config-3 family, else None."""
+    if S != 4095 or C != CONFIG3_ROWS:
+        return None
+    return CONFIG3_COUNTERS.get(name)
 
 
-def algorithmic_mufu(C, S, n_splits, pi_iters):
-    """MUFU (ex2 / lg2 / rcp) operations the reference's math performs per pass (its own counting:
-    per element per wave-step call 7 ex2 + 2 lg2 + 1 more pair on the final iteration, per
-    split-element 5 ex2 + 1 lg2 in the forward; per element 14 in the backward's precompute and per
-    split-element 6 + 7 in its dts recompute and cross terms plus 1 per side-element of the Pibar
-    trees).  This kernel replaces most of them by FMAs (linear-space iterations), so the rate below
-    is the reference-equivalent SFU rate, reported beside the HBM fraction."""
-    fwd = C * S * (10 * (pi_iters - 1) + 2) + 6 * n_splits * S
-    bwd = 14 * C * S + 13 * n_splits * S + 2 * n_splits * S
-    return fwd, bwd
-
-
-def mufu_peak_tops(sm_mhz):
-    """Nominal SFU peak: 148 SMs x 16 MUFU results per clock x the sampled max SM clock."""
-    return 148 * 16 * float(sm_mhz) * 1e6 / 1e12
+def issue_roofline(warp_inst, ms, sm_mhz):
+    """Issue-slot bound of a launch: 148 SMs x 4 schedulers x one warp instruction per clock at
+    the sampled SM clock; ``frac`` = that minimum time / the measured time."""
+    min_ms = warp_inst / (148 * 4 * float(sm_mhz) * 1e6) * 1e3
+    return {"warp_inst_per_launch": int(warp_inst), "min_ms": round(min_ms, 3), "sm_mhz": float(sm_mhz),
+            "frac": round(min_ms / ms, 4)}
 
 
 def kernel_bytes(name, per, fwd_b, bwd_b):
@@ -537,10 +532,32 @@ def reference_arm(args, world, rank):
         "scaling": "strong" if batched else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)", "impl": "reference",
         "config": {"workload": f"config{args.config} family, CPU sample", "sample_rows": rows},
+        "extrapolated": {"measured": f"{n_proc} processes x one {rows}-row forward+backward each, per pass",
+                         "formula": "seconds per solve = median pass wall time x full_rows / sample_rows / processes",
+                         "sample_rows": rows, "full_rows": full_rows, "processes": n_proc},
         "cpu_baseline": {"value": value, "unit": unit, "cores": n_proc, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def reference_triton_leg(cap, dev, our_value, steps=2):
+    """The unmodified reference's own Triton path (``baseline/_ref``: its stock ``kbench.runtime``
+    over its stock kernels) on the same problem and GPU, after this arm's measurements: median
+    forward / backward ms of ``steps`` solves after one warm-up solve (which includes Triton's JIT
+    compilation), CUDA events.  Not part of ``value``; the ratio is ``speedup``."""
+    import torch
+    from baseline import parity, reference
+    why = reference.unavailable_reason()
+    if why:
+        return {"unavailable": why}
+    t = parity.reference_timing(reference.stock_runtime(), cap, dev, steps)
+    torch.cuda.empty_cache()
+    return {"solves_per_s": round(t["solves_per_s"], 4), "ms_per_solve": round(t["ms_per_solve"], 1),
+            "fwd_ms": round(t["fwd_ms"], 1), "bwd_ms": round(t["bwd_ms"], 1), "steps": steps,
+            "first_solve_ms": round(t["first_solve_ms"], 1), "speedup": round(our_value / t["solves_per_s"], 2),
+            "what": "reference kbench.runtime.run_forward + run_backward (stock Triton kernels, default options "
+                    "of the captured problem), same generated family, same GPU"}
 
 
 def roofline_from_timers(timers, peak, peak_kind, steps):
@@ -944,30 +961,36 @@ def main():
         roofline = {
             "bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
             "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-            "traffic": launch_traffic(dominant, C, S),
-            "traffic_note": "dram__bytes_read+write per launch, scaled by rows from an ncu capture "
-                            "of bench.py --traffic-case (12,709 rows, same species tree)",
+            "traffic": None,
             "algorithmic_bytes_per_launch": alg_bytes / n_launch,
             "avg_launch_ms": k_ms / n_launch,
             "kernel_ms_per_step": {k: round(v, 3) for k, v in k_tot.items() if v > 0},
         }
-        # both candidate bounds per kernel: HBM (algorithmic bytes) and SFU (reference MUFU ops)
-        mf, mb = algorithmic_mufu(C, S, int(plan.n_splits), int(static.solver_options.pi_iters))
-        smx = (clocks or {}).get("sm_max_mhz") or 1965.0
-        mpk = mufu_peak_tops(smx)
+        # per dataflow kernel: HBM fraction of the algorithmic bytes and, where captured for this
+        # build, DRAM traffic and the issue-slot bound (warp instructions at the sampled clock)
+        smx = (clocks or {}).get("sm_mhz") or 1965.0
         per_kernel = {}
         for name, kms in k_tot.items():
             if kms <= 0 or not name.startswith("kb_flow_"):
                 continue
-            fwd_k = "forward" in name
-            kb = sum((fwd_b if fwd_k else bwd_b).values())
-            ops = mf if fwd_k else mb
-            per_kernel[name] = {"ms": round(kms, 3), "hbm_gbs": round(kb / (kms * 1e-3) / 1e9, 1),
-                                "hbm_frac": round(kb / (kms * 1e-3) / 1e9 / peak, 4),
-                                "sfu_equiv_tops": round(ops / (kms * 1e-3) / 1e12, 3),
-                                "sfu_frac": round(ops / (kms * 1e-3) / 1e12 / mpk, 4)}
+            kb = sum((fwd_b if "forward" in name else bwd_b).values())
+            entry = {"ms": round(kms, 3), "hbm_gbs": round(kb / (kms * 1e-3) / 1e9, 1),
+                     "hbm_frac": round(kb / (kms * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes": kb}
+            cnt = launch_counters(name, C, S)
+            if cnt is not None:
+                entry["dram_bytes"] = cnt["dram_read"] + cnt["dram_write"]
+                entry["dram_over_algorithmic"] = round(entry["dram_bytes"] / kb, 3)
+                if cnt.get("warp_inst"):
+                    entry["issue"] = issue_roofline(cnt["warp_inst"], kms, smx)
+            per_kernel[name] = entry
         roofline["per_kernel"] = per_kernel
-        roofline["sfu_peak"] = {"tops": round(mpk, 3), "source": f"nominal: 148 SMs x 16/clk x {smx:.0f} MHz"}
+        dom = per_kernel.get(dominant, {})
+        if "dram_bytes" in dom:
+            roofline["traffic"] = dom["dram_bytes"]
+            roofline["traffic_note"] = ("dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch on "
+                                        "this family (single-pass ncu capture of bench.py --traffic-case config3)")
+        if "issue" in dom:
+            roofline["issue_bound"] = dom["issue"]
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             sps, dt, rows = run_cpu_oracle_sample(C, seed=3000)
@@ -975,6 +998,9 @@ def main():
                    "sample": f"numpy oracle fwd+bwd of a {rows}-row family on the config-3 species tree "
                              f"(S={S}), {dt:.1f} s, extrapolated per row to C={C}"}
         value = world * 1000.0 / ms_max
+        ref_triton = None
+        if world == 1 and not args.no_reference_triton:
+            ref_triton = reference_triton_leg(cap, dev, value)
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "solves/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
@@ -992,6 +1018,7 @@ def main():
             "ms_per_solve": round(ms_max, 3), "fwd_ms": round(fwd_ms, 3), "bwd_ms": round(bwd_ms, 3),
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "reference_triton": ref_triton,
             "e2e": {"value": round(world * 1000.0 / e_ms, 4), "unit": "solves/s",
                     "h2d_bytes_per_step": int(theta.numel() * 4 + cw.numel() * 4),
                     "d2h_bytes_per_step": int(n_grad * 4)},
