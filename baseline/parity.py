@@ -137,6 +137,9 @@ def full_size_parity(config: int, cap: dict, device, *, ref_runtime, our_runtime
         same["wrappers_fp64_totals"] = glue.implicit_grad(st_w, theta, cw, sv_r, exact_accumulation=True)
     torch.cuda.synchronize()
     rep["same_state_vs_ref"] = {k: compare_grads(v, g_r) for k, v in same.items() if k != "ref"}
+    if "wrappers_fp64_totals" in same:
+        # the fused engine against the reference-structured driver with the engine's accumulation
+        rep["engine_vs_fp64_totals"] = compare_grads(same["engine"], same["wrappers_fp64_totals"])
     if exact_backward is not None:
         host = {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else v) for k, v in sv_r.items()}
         yard, yname = exact_backward(host), "fp64_oracle"
@@ -144,7 +147,7 @@ def full_size_parity(config: int, cap: dict, device, *, ref_runtime, our_runtime
         yard, yname = same.get("wrappers_fp64_totals"), "wrappers_fp64_totals"
     rep["same_state_yardstick"] = yname if yard is not None else None
     if yard is not None:
-        yard = tuple(torch.as_tensor(np.asarray(y)).to(device) for y in yard)
+        yard = tuple((y if torch.is_tensor(y) else torch.from_numpy(np.asarray(y))).to(device) for y in yard)
         rep["same_state_vs_yardstick"] = {k: compare_grads(v, yard) for k, v in same.items() if k != yname}
 
     # ---- end to end against the float64 evaluation ----

