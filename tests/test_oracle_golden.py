@@ -4,7 +4,8 @@ tests/golden/make_golden.py).  This pins the oracle that the GPU parity tests co
 import numpy as np
 import pytest
 
-from _util import assert_close, assert_loss, golden_names, load_golden, oracle_static
+from _util import (OFF_DISTRIBUTION, assert_close, assert_forward_well_conditioned, assert_loss, golden_names,
+                   load_golden, oracle_static)
 from oracle import kb_oracle as O
 
 NAMES = golden_names()
@@ -21,6 +22,9 @@ def test_oracle_forward_matches_reference(name):
     cap, out = load_golden(name)
     loss, saved = O.forward(oracle_static(cap), cap["inputs"]["theta"], cap["inputs"]["col_weights"])
     assert_loss(loss, out["loss"])
+    if name in OFF_DISTRIBUTION:
+        assert_forward_well_conditioned(name, saved, out)
+        return
     for k in ("pi_wave", "pibar_wave", "E", "Ebar", "pibar_row_max"):
         assert_close(k, saved[k], out[k])
 
