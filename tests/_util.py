@@ -95,10 +95,14 @@ def assert_close_vec(name, got, ref, rtol=RTOL, atol=ATOL):
 # Goldens with rates far off the benchmark distribution (tests/golden/make_golden.py): there the
 # Pibar denominator rowsum - ancestor pathsum (computed in fp32 relative to the row max, by the
 # reference too) cancels for columns on a row's dominant path, so those Pibar values -- and the Pi
-# elements they feed, all far below their row's mass -- depend on the summation order of any fp32
-# evaluation.  What fp32 determines there is compared instead (assert_forward_well_conditioned).
+# elements they dominate, each 20 or more binades below its row's largest value -- depend on the
+# summation order of any fp32 evaluation (measured on the GPU at three such rate settings: our
+# call-by-call driver, a per-element restatement of the reference's kernel, differs there from the
+# reference's CPU-interpreted kernel by up to 8 binades, and the loss is bitwise equal).  What
+# fp32 determines there is compared instead (assert_forward_well_conditioned): Pi elements
+# carrying at least 2^-20 (~1e-6) of their row's largest value, the row maxima, the E-step.
 OFF_DISTRIBUTION = frozenset({"forcelog_s31", "rowfallback_s63"})
-ROW_MASS_FLOOR_LOG2 = -24.0
+ROW_MASS_FLOOR_LOG2 = -20.0
 
 
 def assert_close_row_mass(name, got, ref, rtol=RTOL, atol=ATOL, floor_log2=ROW_MASS_FLOOR_LOG2):
