@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the strong-scaled batched workload (config 4) measured beside the headline")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's own Triton path on this GPU (baseline/_ref) at N=1")
     ap.add_argument("--families", type=int, default=None, help="config 4: families in the whole batch")
@@ -587,19 +589,20 @@ def roofline_from_timers(timers, peak, peak_kind, steps):
     }
 
 
-def batch_arm(args, world, rank, local):
-    """--config 4: families/s of the batched workload (chunked per GPU, sharded across ranks)."""
+def batch_setup(world, rank, local, n_total, chunk):
+    """This rank's share of the batched workload (config 4): its contiguous block of families,
+    generated by a spawn pool sized to this rank's share of the host's CPUs, loaded as chunks of
+    at most ``chunk`` families."""
     import torch
     import torch.distributed as dist
-    from kbench_b200 import _lib, batch, engine, gen
+    from kbench_b200 import batch
 
     dev = torch.device("cuda", local if world > 1 else 0)
-    n_total = int(args.families or gen.CONFIGS[4].n_families)
     f0, f1 = batch.family_block(n_total, world, rank)
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     workers = max(1, len(os.sched_getaffinity(0)) // max(1, local_world))
     t0 = time.perf_counter()
-    chunks = batch.build_chunks(4, f0, f1, args.chunk, workers=workers)
+    chunks = batch.build_chunks(4, f0, f1, chunk, workers=workers)
     gen_s = time.perf_counter() - t0
     allreduce = (lambda t: dist.all_reduce(t)) if world > 1 else None
     t0 = time.perf_counter()
@@ -608,16 +611,24 @@ def batch_arm(args, world, rank, local):
     theta = torch.from_numpy(chunks[0]["inputs"]["theta"]).to(dev)
     cw = torch.from_numpy(chunks[0]["inputs"]["col_weights"]).to(dev)
     S = int(chunks[0]["meta"]["S"])
-    rows, n_chunks = fb.rows, len(chunks)
-    del chunks
-    for _ in range(args.warmup):
+    info = {"f0": f0, "f1": f1, "rows": fb.rows, "n_chunks": len(chunks), "S": S, "generation_s": round(gen_s, 1),
+            "load_s": round(load_s, 1)}
+    return dev, fb, theta, cw, info
+
+
+def batch_timed(fb, theta, cw, dev, world, warmup, steps, *, on_timed_start=None, sampler=None):
+    """Device-timed steps of a family batch (barrier + synchronize on both sides; ``on_timed_start``
+    runs after the warm-up); returns (ms per step as the max over ranks, launches, clocks, last
+    StepResult)."""
+    import torch
+    import torch.distributed as dist
+    from kbench_b200 import _lib
+
+    for _ in range(warmup):
         fb.step(theta, cw)
     torch.cuda.synchronize()
-
-    timers = [(st, engine.LevelTimer()) for st in fb.statics]
-    for st, tm in timers:
-        st._level_timer = tm
-    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if on_timed_start is not None:
+        on_timed_start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -626,7 +637,7 @@ def batch_arm(args, world, rank, local):
         sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         res = fb.step(theta, cw)
     ev1.record()
     torch.cuda.synchronize()
@@ -634,15 +645,56 @@ def batch_arm(args, world, rank, local):
         dist.barrier()
     clocks = sampler.stop() if sampler else None
     launches = sum(_lib.LAUNCHES.values()) - launches0
-    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_t = torch.tensor([ev0.elapsed_time(ev1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    return float(ms_t.item()), launches, clocks, res
+
+
+def config4_strong(args, world, rank, local, warmup=1, steps=3):
+    """The batched workload (config 4: ``--families``, default all 1,024, S = 1,023) strong-scaled
+    over the N ranks of this run -- each rank owns a contiguous block of families, one all-reduce
+    of [loss, 8 x S accumulators] per step -- as a compact object for the headline line (a fixed
+    1 warm-up + 3 timed steps, so its cost does not grow with --steps)."""
+    import torch
+    from kbench_b200 import gen
+    n_total = int(args.families or gen.CONFIGS[4].n_families)
+    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk)
+    ms, launches, _, res = batch_timed(fb, theta, cw, dev, world, warmup, steps)
+    out = {"workload": f"config4: {n_total} families (S={info['S']}) in contiguous blocks over {world} rank(s), "
+                       f"chunks of <= {args.chunk}; one all-reduce of [loss, 8*S accumulators] per step",
+           "families": n_total, "families_per_s": round(n_total * 1000.0 / ms, 3), "ms_per_step": round(ms, 3),
+           "steps": steps, "warmup": warmup, "scaling": "strong", "rank0_rows": info["rows"],
+           "rank0_generation_s": info["generation_s"], "rank0_load_s": info["load_s"],
+           "gpu_launches_rank0": int(launches), "loss": float(res.loss)}
+    del fb
+    torch.cuda.empty_cache()
+    return out
+
+
+def batch_arm(args, world, rank, local):
+    """--config 4: families/s of the batched workload (chunked per GPU, sharded across ranks)."""
+    import torch
+    import torch.distributed as dist
+    from kbench_b200 import engine, gen
+
+    n_total = int(args.families or gen.CONFIGS[4].n_families)
+    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk)
+    f0, f1, rows, n_chunks, S = info["f0"], info["f1"], info["rows"], info["n_chunks"], info["S"]
+    gen_s, load_s = info["generation_s"], info["load_s"]
+    timers = [(st, engine.LevelTimer()) for st in fb.statics]
+
+    def attach():
+        for st, tm in timers:
+            st._level_timer = tm
+
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    ms_max, launches, clocks, res = batch_timed(fb, theta, cw, dev, world, args.warmup, args.steps,
+                                                on_timed_start=attach, sampler=sampler)
     peak, peak_kind = measured_peak()
     roofline = roofline_from_timers(timers, peak, peak_kind, args.steps) if rank == 0 else None
     for st, _ in timers:
         st._level_timer = None
-    ms_t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
 
     # end to end: theta / col_weights from pinned host memory, loss + gradients back every step
     n_out = 1 + 3 * S + S
@@ -952,6 +1004,12 @@ def main():
         dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
     e_ms = float(e_t.item())
 
+    # ---- the batched workload (config 4), strong-scaled over the same ranks ----
+    config4 = None
+    if not args.no_config4:
+        torch.cuda.empty_cache()
+        config4 = config4_strong(args, world, rank, local)
+
     if rank == 0:
         peak, peak_kind = measured_peak()
         k_tot = {name: v[0] / args.steps for name, v in totals.items()}
@@ -1022,6 +1080,7 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu,
             "reference_triton": ref_triton,
+            "config4": config4,
             "e2e": {"value": round(world * 1000.0 / e_ms, 4), "unit": "solves/s",
                     "h2d_bytes_per_step": int(theta.numel() * 4 + cw.numel() * 4),
                     "d2h_bytes_per_step": int(n_grad * 4)},

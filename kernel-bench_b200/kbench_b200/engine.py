@@ -51,6 +51,12 @@ class LevelPlan:
     child_idx: torch.Tensor      # int32
 
 
+def _sorted_unique(keys: np.ndarray) -> np.ndarray:
+    """Distinct values of an int64 array, ascending (a sort and one comparison pass)."""
+    k = np.sort(keys)
+    return k[np.concatenate(([True], k[1:] != k[:-1]))] if k.shape[0] else k
+
+
 def build_plan(static) -> LevelPlan:
     """Dependency levels and the per-row split CSR, from the reference wave layout."""
     cached = getattr(static, "_plan", None)
@@ -79,31 +85,35 @@ def build_plan(static) -> LevelPlan:
     else:
         par = sls = srs = np.zeros(0, np.int64)
         lsps = np.zeros(0, np.float32)
-    order_rows = np.lexsort((np.arange(C), level))
+    # stable argsorts and unique over int64 keys (row * C + row) keep this linear-ish for the
+    # multi-million-row statics of family batches
+    order_rows = np.argsort(level, kind="stable")
     pos = np.empty(C, dtype=np.int64)
     pos[order_rows] = np.arange(C)
-    order_splits = np.lexsort((np.arange(par.shape[0]), pos[par]))
+    order_splits = np.argsort(pos[par], kind="stable")
     counts = np.bincount(pos[par], minlength=C) if par.shape[0] else np.zeros(C, np.int64)
     split_ptr = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
     n_levels = int(level.max()) + 1 if C else 0
     level_ptr = [0] + np.cumsum(np.bincount(level, minlength=n_levels)).tolist()
-    children = []
     sp_sorted = par[order_splits]
     lv_of_split = level[sp_sorted]
     s_l, s_r = sls[order_splits], srs[order_splits]
-    for L in range(n_levels):
-        m = lv_of_split == L
-        children.append(int(np.unique(np.concatenate([s_l[m], s_r[m]])).shape[0]) if m.any() else 0)
+    if par.shape[0]:  # distinct child rows per level: unique (level, child) keys
+        lk = _sorted_unique(np.concatenate([lv_of_split * C + s_l, lv_of_split * C + s_r]))
+        children = np.bincount(lk // C, minlength=n_levels).tolist()
+    else:
+        children = [0] * n_levels
     # dataflow arrays
-    order_r = np.lexsort((np.arange(par.shape[0]), par)) if par.shape[0] else np.zeros(0, np.int64)
+    order_r = np.argsort(par, kind="stable") if par.shape[0] else np.zeros(0, np.int64)
     cnt_r = np.bincount(par, minlength=C) if par.shape[0] else np.zeros(C, np.int64)
     row_split_ptr = np.concatenate([[0], np.cumsum(cnt_r)]).astype(np.int64)
     if par.shape[0]:
-        pairs = np.unique(np.stack([np.concatenate([par, par]), np.concatenate([sls, srs])], axis=1), axis=0)
+        pk = _sorted_unique(np.concatenate([par * C + sls, par * C + srs]))  # sorted by (parent, child)
+        pairs = np.stack([pk // C, pk % C], axis=1)
     else:
         pairs = np.zeros((0, 2), np.int64)
     dep0 = np.bincount(pairs[:, 0], minlength=C).astype(np.int32) if pairs.shape[0] else np.zeros(C, np.int32)
-    by_child = pairs[np.lexsort((pairs[:, 0], pairs[:, 1]))] if pairs.shape[0] else pairs
+    by_child = pairs[np.argsort(pairs[:, 1] * C + pairs[:, 0])] if pairs.shape[0] else pairs
     cnt_c = np.bincount(by_child[:, 1], minlength=C) if pairs.shape[0] else np.zeros(C, np.int64)
     par_ptr = np.concatenate([[0], np.cumsum(cnt_c)]).astype(np.int64)
     ready0 = np.nonzero(dep0 == 0)[0].astype(np.int32)

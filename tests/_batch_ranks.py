@@ -51,7 +51,51 @@ class OracleSolver:
                                          a["col"], n_fam=n_fam)
 
 
-def gloo_rank(rank, world, port, chunk, out_dir):
+class EngineOnCpuSolver(batch.EngineSolver):
+    """The engine's batch solver with only its device steps replaced: ``load`` is the engine's own
+    (``runtime.make_static`` + ``engine.build_plan`` on the host), the column sums go into the
+    engine's fp64 slot layout ``[n_slots, 8, NTV]`` and are combined by the engine's
+    ``reduce_acc``; the forward + accumulating backward of a chunk, ``prepare`` and ``finish`` (CUDA
+    kernels) are computed by the oracle instead."""
+
+    N_SLOTS = 3
+
+    def __init__(self):
+        super().__init__("cpu")
+        self._next_slot = 0
+
+    def load(self, captured):
+        static = super().load(captured)
+        static._oracle_static = oracle_static(captured)
+        return static
+
+    def prepare(self, static, theta, col_weights):
+        return {}
+
+    def new_acc(self, static):
+        from kbench_b200 import tree
+        bd, vpt = tree.engine_width(int(static.state_helpers["S"]))
+        return torch.zeros((self.N_SLOTS, 8, bd * vpt), dtype=torch.float64)
+
+    def chunk(self, static, theta, col_weights, prep, acc):
+        st = static._oracle_static
+        loss, saved = O.forward(st, theta, col_weights)
+        a = O.backward_accumulators(st, saved)
+        S = int(st["state_helpers"]["S"])
+        slot = self._next_slot % self.N_SLOTS  # a CTA's slot: chunks spread over several
+        self._next_slot += 1
+        acc[slot, :, :S] += torch.from_numpy(np.stack([a[n] for n in batch.ACC_NAMES]).astype(np.float64))
+        prep["saved"], prep["static"] = saved, st
+        return torch.tensor(loss, dtype=torch.float64)
+
+    def finish(self, static, theta, col_weights, prep, acc8, n_fam):
+        return OracleSolver().finish(prep["static"], theta, col_weights, prep, acc8, n_fam)
+
+
+SOLVERS = {"oracle": OracleSolver, "engine_cpu": EngineOnCpuSolver}
+
+
+def gloo_rank(rank, world, port, chunk, out_dir, solver="oracle"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -60,7 +104,7 @@ def gloo_rank(rank, world, port, chunk, out_dir):
         n = TINY.n_families
         f0, f1 = batch.family_block(n, world, rank)
         chunks = batch.build_chunks(TINY, f0, f1, chunk, seed=SEED, workers=1)
-        fb = batch.FamilyBatch(chunks, n, OracleSolver(), allreduce=lambda t: dist.all_reduce(t))
+        fb = batch.FamilyBatch(chunks, n, SOLVERS[solver](), allreduce=lambda t: dist.all_reduce(t))
         theta = chunks[0]["inputs"]["theta"]
         col = chunks[0]["inputs"]["col_weights"]
         res = fb.step(theta, col)

@@ -90,3 +90,18 @@ def test_two_gloo_ranks_match_whole_batch(tmp_path):
         assert_close("grad_theta", o["grad_theta"], gt_ref)
         assert_close("grad_col", o["grad_col"], gc_ref)
     np.testing.assert_array_equal(outs[0]["grad_theta"], outs[1]["grad_theta"])
+
+
+def test_two_gloo_ranks_engine_solver_match_whole_batch(tmp_path):
+    """The rank loop over the engine's own batch solver (host-side static and plan building, fp64
+    slot layout and slot reduction; only the device steps computed by the oracle) on two gloo
+    ranks gives the whole-batch result."""
+    loss_ref, gt_ref, gc_ref = _whole_batch_reference()
+    world = 2
+    tmp.spawn(gloo_rank, args=(world, _free_port(), 1, str(tmp_path), "engine_cpu"), nprocs=world, join=True)
+    outs = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for o in outs:
+        assert_loss(float(o["loss"]), loss_ref)
+        assert_close("grad_theta", o["grad_theta"], gt_ref)
+        assert_close("grad_col", o["grad_col"], gc_ref)
+    np.testing.assert_array_equal(outs[0]["grad_theta"], outs[1]["grad_theta"])
