@@ -131,6 +131,8 @@ def full_size_parity(config: int, cap: dict, device, *, ref_runtime, our_runtime
 
     # ---- backward of one forward state (the reference's) ----
     same = {"ref": g_r, "ref_repeat": g_r2, "engine": our_runtime.run_backward(st_o, theta, cw, sv_r)}
+    # the engine's own run-to-run spread (its children's adjoint rows are added with fp32 atomics)
+    rep["engine_repeat"] = compare_grads(our_runtime.run_backward(st_o, theta, cw, sv_r), same["engine"])
     if glue is not None:
         st_w = our_runtime.make_static(cap, device, engine="wrappers")
         same["wrappers"] = glue.implicit_grad(st_w, theta, cw, sv_r)

@@ -15,7 +15,9 @@ Asserted:
     measured by two reference backward passes);
   - the fused engine against the same driver with fp64 totals (the engine's accumulation), to
     rel 1e-4 norm-wise: the engine's whole difference from the reference is the reference's
-    fp32 running-sum error (measured: 2.6e-5 norm-wise at config 2, ~1e-3 at config 3);
+    fp32 running-sum error (measured: 2.6e-5 norm-wise at config 2, ~1e-3 at config 3); and the
+    engine's own run-to-run spread (fp32 atomics into the children's adjoint rows) within the
+    tolerance;
   - config 2: every fp32 backward within 3e-4 norm-wise of the exact (fp64 oracle) backward of
     that state -- the fp32 floor of the algorithm (measured: 1.5-1.75e-4 for the reference and
     for ours alike; per-element fp32 rounding amplified by the implicit solve dominates there);
@@ -81,6 +83,7 @@ def _check(rep):
         noise = same["ref_repeat"][g]["tol_units"]
         assert same["wrappers"][g]["tol_units"] <= max(1.0, 4.0 * noise), (g, same)
         assert rep["engine_vs_fp64_totals"][g]["norm_rel"] <= parity.RTOL, (g, rep["engine_vs_fp64_totals"])
+        assert rep["engine_repeat"][g]["tol_units"] <= 1.0, (g, rep["engine_repeat"])
     if rep["same_state_yardstick"] == "fp64_oracle":
         for impl, errs in rep["same_state_vs_yardstick"].items():
             for g in parity.GRADS:
