@@ -1858,6 +1858,8 @@ struct BwdArgs {
 
 // accumulator rows of the per-CTA column sums
 enum { G_PD = 0, G_PS, G_MT, G_E, G_EBAR, G_ES1, G_ES2, G_COL, G_N };
+// the backward's shared fp32 rows 0..2 are G_PD, G_PS, G_MT (row 3 is G_COL)
+static_assert(G_PD == 0 && G_PS == 1 && G_MT == 2, "shared column-sum rows");
 
 #define KB_FLOW_FLUSH_ROWS 8
 
@@ -1870,6 +1872,11 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
   const int S = c.S;
   const int NT = blockDim.x;
   const int NTV = NT * VPT;
+  // Column sums: G_PD, G_PS, G_MT and G_COL (updated per split) in fp32 shared rows ACC, moved
+  // to the CTA's fp64 slot every few rows; G_E, G_EBAR, G_ES1, G_ES2 (once per row) straight to
+  // the slot by fp64 reductions (each address is one thread's column: program order, so the
+  // sums are deterministic).  KD / KS / KM hold log_pD, log_pS and mc when every row shares one
+  // item row (the split phase reads them per column and split).
   // Shared memory, per phase of a row: the tour scan uses T and U[0, NTV) as one 2 NTV buffer;
   // the edge weights pass through SLb / SRb; the move to preorder positions uses T, U, U + NTV,
   // SLb and SRb; the Neumann sweep keeps the term in T and its prefix in U (U + NTV: the path
@@ -1879,8 +1886,13 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
   float* T = sm + NTV;         // tour (with U) / Neumann term / speciation cotangents
   float* U = sm + 2 * NTV;     // 2 NTV: tour, preorder prefix, float2 pairs in the split phase
   float2* U2 = reinterpret_cast<float2*>(U);
-  float* ACC = sm + 4 * NTV;   // G_N rows of NTV fp32 column sums (this CTA)
-  float* SLb = ACC + G_N * NTV;  // staged child Pi rows of the current split (NTV + 4 each)
+  float* ACC = sm + 4 * NTV;   // rows G_PD, G_PS, G_MT (0..2) and G_COL (3): fp32 column sums
+  float* KD = ACC + 4 * NTV;   // log_pD, log_pS, mc of the shared item row
+  float* KS = KD + NTV;
+  float* KM = KS + NTV;
+  float* SLb = KM + NTV;  // staged child Pi rows of the current split (NTV + 4 each)
+  double* const slotd = a.slots + (size_t)blockIdx.x * G_N * NTV;
+  const bool shared_consts = c.prs == 0 && c.crs == 0;
   float* SRb = SLb + NTV + 4;
   float* red = SRb + NTV + 4;
   unsigned cc[VPT], tr[VPT], pk[VPT], pa[VPT];
@@ -1892,7 +1904,10 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     pk[k] = c.packed[2 * NTV + s];
     pa[k] = c.packed[3 * NTV + s];
 #pragma unroll
-    for (int j = 0; j < G_N; ++j) ACC[j * NTV + s] = 0.f;
+    for (int j = 0; j < 4; ++j) ACC[j * NTV + s] = 0.f;
+    KD[s] = shared_consts && s < S ? c.log_pD[s] : 0.f;
+    KS[s] = shared_consts && s < S ? c.log_pS[s] : 0.f;
+    KM[s] = shared_consts && s < S ? c.mc[s] : 0.f;
   }
   __shared__ FlowSlot fs;
   if (threadIdx.x == flow_poller()) fs.next = -1;
@@ -2090,7 +2105,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
         const unsigned q = lo16(pk[k]);
         v[k] = T[q];
         const float sub = U[hi16(pk[k])] - U[q];
-        ACC[G_COL * NTV + s] += U[NTV + q] * (A - sub);
+        ACC[3 * NTV + s] += U[NTV + q] * (A - sub);
       }
     }
     if (a.v_out) {
@@ -2133,10 +2148,10 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
         ACC[G_PD * NTV + s] += q0;
         ACC[G_PS * NTV + s] += q3 + q4 + q5;
         ACC[G_MT * NTV + s] += q2;
-        ACC[G_E * NTV + s] += q0 + q2;
-        ACC[G_EBAR * NTV + s] += q1;
-        ACC[G_ES1 * NTV + s] += q4;
-        ACC[G_ES2 * NTV + s] += q3;
+        atomicAdd(slotd + (size_t)G_E * NTV + s, (double)(q0 + q2));
+        atomicAdd(slotd + (size_t)G_EBAR * NTV + s, (double)q1);
+        atomicAdd(slotd + (size_t)G_ES1 * NTV + s, (double)q4);
+        atomicAdd(slotd + (size_t)G_ES2 * NTV + s, (double)q3);
       }
     }
 
@@ -2144,7 +2159,9 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     // Per split: the split's Pi cotangents (5 terms) and Pibar cotangents of both children, then
     // both Pibar VJP trees at once (one scan of (left, right) pairs over the preorder numbering,
     // fused with the side-activity sums), and one atomic add per child element.  The next split's
-    // child rows are fetched asynchronously while the current split's trees are scanned.
+    // child rows are fetched asynchronously while the current split's trees are scanned; the
+    // children's Pibar values are loaded before the staging wait, and the children's column
+    // weights for the trees come from the staged Pi rows (not re-read after the scan).
     if (has_splits) {
       float pip[VPT];
 #pragma unroll
@@ -2156,28 +2173,39 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
       for (long long i = i0; i < i1; ++i) {
         const long long l = a.sp.sl[i], r = a.sp.sr[i];
         const float lsp = a.sp.lsp[i];
-        const float* pil = a.Pi + (size_t)l * S;
-        const float* pir = a.Pi + (size_t)r * S;
         const float* pbl = a.Pibar + (size_t)l * S;
         const float* pbr = a.Pibar + (size_t)r * S;
         const float rml = a.row_max[l], rmr = a.row_max[r];
+        const float rmls = safe_max(rml), rmrs = safe_max(rmr);
         const size_t mcl = (size_t)(c.item_idx[l] * c.crs), mcr = (size_t)(c.item_idx[r] * c.crs);
-        cp_async_wait_all();
-        __syncthreads();  // split i staged; the previous split's readers of P, T, U2 are done
-        float cl[VPT], cr[VPT];
+        float bl[VPT], br[VPT];  // the children's Pibar at the own columns: issued before the wait
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
           const int s = threadIdx.x + k * NT;
-          cl[k] = cr[k] = 0.f;
+          bl[k] = s < S ? __ldcg(pbl + s) : neg_inf();
+          br[k] = s < S ? __ldcg(pbr + s) : neg_inf();
+        }
+        cp_async_wait_all();
+        __syncthreads();  // split i staged; the previous split's readers of P, T, U2 are done
+        float cl[VPT], cr[VPT], wl[VPT], wr[VPT];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          const int s = threadIdx.x + k * NT;
+          cl[k] = cr[k] = wl[k] = wr[k] = 0.f;
           float v3 = 0.f, v4 = 0.f, udl = 0.f, udr = 0.f;
           if (s < S) {
             const float pl = cSL[s], pr = cSR[s];
-            const float ld = c.log_pD[pb + s];
-            const float ls = c.log_pS[pb + s];
+            {  // the children's column weights 2^(Pi + col - row max), used by the Pibar VJP trees
+              const float cw = c.use_col ? c.col[s] : 0.f;
+              wl[k] = ex2((c.use_col ? pl + cw : pl) - rmls);
+              wr[k] = ex2((c.use_col ? pr + cw : pr) - rmrs);
+            }
+            const float ld = shared_consts ? KD[s] : c.log_pD[pb + s];
+            const float ls = shared_consts ? KS[s] : c.log_pS[pb + s];
             const unsigned ca = lo16(cc[k]), cbb = hi16(cc[k]);
             const float d0 = ld + pl + pr;
-            const float d1 = pl + pbr[s];
-            const float d2 = pr + pbl[s];
+            const float d1 = pl + br[k];
+            const float d2 = pr + bl[k];
             const float d3 = ls + cSL[ca] + cSR[cbb];
             const float d4 = ls + cSR[ca] + cSL[cbb];
             const float ppar = pip[k];
@@ -2192,9 +2220,10 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
             ACC[G_MT * NTV + s] += vd1 + vd2;
             cl[k] = vd0 + vd1;
             cr[k] = vd0 + vd2;
-            const float bl = pbl[s], br = pbr[s];
-            udl = is_neg_inf(bl) ? 0.f : vd2 * ex2(rml + c.mc[mcl + s] - bl);
-            udr = is_neg_inf(br) ? 0.f : vd1 * ex2(rmr + c.mc[mcr + s] - br);
+            const float mcL = shared_consts ? KM[s] : c.mc[mcl + s];
+            const float mcR = shared_consts ? KM[s] : c.mc[mcr + s];
+            udl = is_neg_inf(bl[k]) ? 0.f : vd2 * ex2(rml + mcL - bl[k]);
+            udr = is_neg_inf(br[k]) ? 0.f : vd1 * ex2(rmr + mcR - br[k]);
           }
           P[s] = v3;  // P no longer holds Pi (pip registers do)
           T[s] = v4;
@@ -2219,7 +2248,6 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
         const bool side_r = !a.side_thr_enabled || sabs_r > a.side_thr;
         float* rl = a.acc + (size_t)l * S;
         float* rr = a.acc + (size_t)r * S;
-        const float rmls = safe_max(rml), rmrs = safe_max(rmr);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
           const int x = threadIdx.x + k * NT;
@@ -2229,18 +2257,9 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
             const float stl = first ? P[par] : T[par];
             const float str = first ? T[par] : P[par];
             const float2 ue = U2[hi16(pk[k])], ub = U2[lo16(pk[k])];
-            float tl = 0.f, trr = 0.f;
-            if (side_l) {
-              float w = pil[x];
-              if (c.use_col) w += c.col[x];
-              tl = ex2(w - rmls) * (Al - (ue.x - ub.x));
-            }
-            if (side_r) {
-              float w = pir[x];
-              if (c.use_col) w += c.col[x];
-              trr = ex2(w - rmrs) * (Ar - (ue.y - ub.y));
-            }
-            ACC[G_COL * NTV + x] += tl + trr;
+            const float tl = side_l ? wl[k] * (Al - (ue.x - ub.x)) : 0.f;
+            const float trr = side_r ? wr[k] * (Ar - (ue.y - ub.y)) : 0.f;
+            ACC[3 * NTV + x] += tl + trr;
             atomicAdd(rl + x, cl[k] + stl + tl);
             atomicAdd(rr + x, cr[k] + str + trr);
           }
@@ -2258,8 +2277,8 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
         for (int k = 0; k < VPT; ++k) {
           const int s = threadIdx.x + k * NT;
 #pragma unroll
-          for (int j = 0; j < G_N; ++j) {
-            slot[(size_t)j * NTV + s] += (double)ACC[j * NTV + s];
+          for (int j = 0; j < 4; ++j) {
+            slot[(size_t)(j == 3 ? G_COL : j) * NTV + s] += (double)ACC[j * NTV + s];
             ACC[j * NTV + s] = 0.f;
           }
         }
@@ -2272,7 +2291,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
 #pragma unroll
-    for (int j = 0; j < G_N; ++j) slot[(size_t)j * NTV + s] += (double)ACC[j * NTV + s];
+    for (int j = 0; j < 4; ++j) slot[(size_t)(j == 3 ? G_COL : j) * NTV + s] += (double)ACC[j * NTV + s];
   }
 }
 
@@ -2510,7 +2529,7 @@ extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, in
   int bd;
   const int vpt = bwd_width(S, bd);
   const int ntv = bd * vpt;
-  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
+  const size_t smem = (size_t)(11 * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = n_rows < n_slots ? n_rows : n_slots;
   cudaStream_t st = (cudaStream_t)stream;
   const Flow nof{};
@@ -2729,7 +2748,7 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   int bd;
   const int vpt = bwd_width(S, bd);
   const int ntv = bd * vpt;
-  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
+  const size_t smem = (size_t)(11 * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   const int grid = C < n_slots ? C : n_slots;  // persistent CTAs, one fp64 slot each
 #define KB_FB_CASE(V)                                                                                      \
   case V:                                                                                                  \
@@ -2821,7 +2840,7 @@ extern "C" int kb_backward_ctas(int S, int* n_ctas) {
   int bd;
   const int vpt = bwd_width(S, bd);
   const int ntv = bd * vpt;
-  const size_t smem = (size_t)((4 + G_N) * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
+  const size_t smem = (size_t)(11 * ntv + 2 * (ntv + 4) + 128) * sizeof(float);
   int dev = 0, n_sm = 0, per_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
