@@ -177,7 +177,7 @@ def algorithmic_bytes(plan, S):
 CONFIG3_ROWS = 128282
 CONFIG3_COUNTERS: dict = {
     "kb_flow_forward": {"dram_read": 18417902080, "dram_write": 6217162240, "warp_inst": 23781305587},
-    "kb_flow_backward": {"dram_read": 43530014720, "dram_write": 13455690240, "warp_inst": 40369368854},
+    "kb_flow_backward": {"dram_read": 45366837504, "dram_write": 16917131776, "warp_inst": 40822535893},
 }
 
 
