@@ -52,7 +52,9 @@ int kb_e_fixed_point(const float* E0, float* E_out, float* E_tmp, float* E_s1, f
  * device array of KB_NOALLOC_ESTEP_MAX floats (256 KiB, held by every GPU that loads the library
  * until exit).  G*S above KB_NOALLOC_ESTEP_MAX returns KB_ERR_SIZE.  The first call on a device
  * looks the array's address up (cudaGetSymbolAddress, no allocation) -- make it before any stream
- * capture.  All calls share the array; calls that overlap on the GPU race. */
+ * capture.  The address is cached per device ordinal for the process's lifetime: it assumes the
+ * CUDA runtime's primary context on that device (no cudaDeviceReset between calls, no other
+ * driver context made current).  All calls share the array; calls that overlap on the GPU race. */
 #define KB_NOALLOC_ESTEP_MAX 65536
 int kb_e_fixed_point_noalloc(const float* E0, float* E_out, float* E_s1, float* E_s2, float* Ebar,
                              const float* log_pS, const float* log_pD, const float* log_pL,

@@ -33,22 +33,24 @@ def _problem(cfg, device, seed=None):
                 max_iter=static.solver_options.e_max_iter, tol=static.solver_options.e_tol)
 
 
-def _outputs(S, device):
-    return [torch.empty((1, S), device=device) for _ in range(4)] + [torch.zeros(1, dtype=torch.int32, device=device)]
+def _outputs(S, device, G=1):
+    return [torch.empty((G, S), device=device) for _ in range(4)] + [torch.zeros(G, dtype=torch.int32, device=device)]
 
 
 def _args(pb, E0, outs):
     tt = pb["tt"]
     pS, pD, pL, mc = pb["rows"]
+    G = int(pS.shape[0])
     return [E0.data_ptr(), outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), outs[3].data_ptr(),
             pS.data_ptr(), pD.data_ptr(), pL.data_ptr(), mc.data_ptr(), pb["clp"].data_ptr(), tt.parent.data_ptr(),
-            tt.child1.data_ptr(), tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K, pb["S"], 1, int(pb["max_iter"]),
+            tt.child1.data_ptr(), tt.child2.data_ptr(), tt.jumps.data_ptr(), tt.K, pb["S"], G, int(pb["max_iter"]),
             float(pb["tol"]), pb["ucw"], outs[4].data_ptr(), _lib.stream_handle()]
 
 
 def _allocating(pb, E0, device):
-    outs = _outputs(pb["S"], device)
-    tmp = torch.empty((1, pb["S"]), device=device)
+    G = int(E0.shape[0])
+    outs = _outputs(pb["S"], device, G)
+    tmp = torch.empty((G, pb["S"]), device=device)
     args = _args(pb, E0, outs)
     args.insert(2, tmp.data_ptr())  # E_tmp follows E_out
     _lib.call("kb_e_fixed_point", *args)
@@ -56,7 +58,7 @@ def _allocating(pb, E0, device):
 
 
 def _no_alloc(pb, E0, device):
-    outs = _outputs(pb["S"], device)
+    outs = _outputs(pb["S"], device, int(E0.shape[0]))
     _lib.call("kb_e_fixed_point_noalloc", *_args(pb, E0, outs))
     return outs
 
@@ -66,7 +68,7 @@ def _assert_same(got, ref):
         fin = torch.isfinite(r)
         assert torch.equal(torch.isfinite(g), fin)
         assert torch.all((g[fin] - r[fin]).abs() <= ATOL + RTOL * r[fin].abs())
-    assert int(got[4].item()) == int(ref[4].item())
+    assert torch.equal(got[4], ref[4])
 
 
 def test_no_alloc_matches_allocating_entry_point(cuda):
@@ -76,6 +78,27 @@ def test_no_alloc_matches_allocating_entry_point(cuda):
         ref = _allocating(pb, E0, cuda)
         first = _no_alloc(pb, E0, cuda)    # first call on this device also performs the set-up
         second = _no_alloc(pb, E0, cuda)   # reuses the shared array holding the previous contents
+        torch.cuda.synchronize()
+        _assert_same(first, ref)
+        _assert_same(second, ref)
+
+
+def test_no_alloc_item_rows_and_both_buffer_parities(cuda):
+    """Several item rows (each its own fixed point, G x S elements of the shared array) and
+    iteration caps of 3 and 4, so that the final iterate ends in either half of the array's
+    ping-pong pair, then the problem's own cap; two calls in a row each time."""
+    base = _problem(1, cuda)
+    S, G = base["S"], 4
+    shift = torch.linspace(-0.3, 0.3, G, device=cuda).reshape(G, 1)
+    pS, pD, pL, mc = base["rows"]
+    rows = [pS.expand(G, S).contiguous(), (pD + shift).contiguous(), (pL - shift).contiguous(),
+            mc.expand(G, S).contiguous()]
+    E0 = torch.full((G, S), -1.0, device=cuda)
+    for cap_iters in (3, 4, int(base["max_iter"])):
+        pb = dict(base, rows=rows, max_iter=cap_iters)
+        ref = _allocating(pb, E0, cuda)
+        first = _no_alloc(pb, E0, cuda)
+        second = _no_alloc(pb, E0, cuda)
         torch.cuda.synchronize()
         _assert_same(first, ref)
         _assert_same(second, ref)
