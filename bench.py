@@ -77,6 +77,9 @@ def parse_args():
                          "a reduced config-3 family (the config-3 species tree, 2,048 genes: ~12.7k rows, 208 MB per "
                          "[C,S] buffer) for multi-pass captures; 'config3' is the full config-3 family, for "
                          "single-pass captures (DRAM bytes, durations) of the full-size launches")
+    ap.add_argument("--per-kernel", action="store_true",
+                    help="per-wrapper times of one forward + backward pass driven by the reference's own glue, "
+                         "over the reference's stock Triton kernels and over this project's (--config, default 2)")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
@@ -546,6 +549,40 @@ def reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def per_kernel_arm(args, world, rank):
+    """--per-kernel: the reference's glue (``kbench.runtime``) runs one warm-up and one timed pass
+    over the reference's own Triton kernels (``baseline/_ref``) and over this project's wrappers
+    (a checkout copy whose kernel modules re-export them), each in its own process
+    (``baseline/wrapper_bench.py``); one JSON line with both per-wrapper tables."""
+    if rank != 0:
+        return
+    import subprocess
+    from baseline import reference
+    why = reference.unavailable_reason()
+    cfg = 2 if args.config == 3 else args.config  # the micro-bench config of the benchmark text
+    if why:
+        print(json.dumps({"per_kernel": None, "unavailable": why}), flush=True)
+        return
+    env = dict(os.environ)
+    env["PYTHONPATH"] = str(ROOT / "kernel-bench_b200")
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        roots = {"reference_triton": reference.REF, "ours": reference.checkout_copy(Path(tmp) / "kernel-bench")}
+        for name, root in roots.items():
+            res = subprocess.run([sys.executable, str(ROOT / "baseline" / "wrapper_bench.py"), "--root", str(root),
+                                  "--config", str(cfg)], env=env, capture_output=True, text=True, timeout=1800)
+            line = [ln for ln in res.stdout.splitlines() if ln.startswith("WRAPPER_BENCH ")]
+            out[name] = json.loads(line[-1].split(" ", 1)[1]) if line else {"error": res.stderr[-2000:]}
+    ratio = {}
+    ref_w, our_w = out["reference_triton"].get("wrappers", {}), out["ours"].get("wrappers", {})
+    for k in ref_w:
+        if k in our_w and our_w[k]["ms"] > 0:
+            ratio[k] = round(ref_w[k]["ms"] / our_w[k]["ms"], 2)
+    print(json.dumps({"per_kernel": True, "config": cfg, "driver": "reference glue (kbench.runtime), one timed pass",
+                      "reference_triton": out["reference_triton"], "ours": out["ours"],
+                      "speedup_per_wrapper": ratio}), flush=True)
+
+
 def reference_triton_leg(cap, dev, our_value, steps=2):
     """The unmodified reference's own Triton path (``baseline/_ref``: its stock ``kbench.runtime``
     over its stock kernels) on the same problem and GPU, after this arm's measurements: median
@@ -890,6 +927,9 @@ def main():
         args.warmup = 3
     if args.traffic_case:
         traffic_case(args)
+        return
+    if args.per_kernel:
+        per_kernel_arm(args, world, rank)
         return
     if args.hvp:
         hvp_arm(args, world, rank, local)
