@@ -21,8 +21,13 @@ Asserted:
   - config 2: every fp32 backward within 3e-4 norm-wise of the exact (fp64 oracle) backward of
     that state -- the fp32 floor of the algorithm (measured: 1.5-1.75e-4 for the reference and
     for ours alike; per-element fp32 rounding amplified by the implicit solve dominates there);
-* end to end against the float64 evaluation (``tests/golden/fp64``): our gradients at least as
-  close as the reference's, norm-wise.
+* end to end against the float64 evaluation (``tests/golden/fp64``): our gradients within
+  E2E_FACTOR of the reference's own distance, norm-wise and elementwise.  Both fp32 pipelines
+  start the backward from a forward state rounded at ~1e-7 relative, and the implicit solve
+  amplifies that rounding (measured distance from fp64: 1.6e-4 norm-wise at config 2, 6-7.5e-3 at
+  config 3, the same for both), so each pipeline draws its own error of that size: measured
+  ours / reference 0.97-0.99 at config 2 and 1.01-1.16 at config 3 norm-wise, 0.6-0.9 in the
+  largest elementwise units.
 
 The report is printed (``pytest -s``) before the assertions.  Skipped without ``baseline/_ref``.
 """
@@ -71,6 +76,7 @@ def _report(config, cuda, exact_on_host):
 
 
 FP32_FLOOR = 3e-4  # norm-wise distance of an fp32 backward from the exact one at config 2
+E2E_FACTOR = 1.5  # bound on our end-to-end distance from fp64 over the reference's
 
 
 def _check(rep):
@@ -91,7 +97,9 @@ def _check(rep):
     e2e = rep["end_to_end_vs_fp64"]
     if e2e is not None:
         for g in parity.GRADS:
-            assert e2e["ours"][g]["norm_rel"] <= max(e2e["ref"][g]["norm_rel"], parity.RTOL), (g, e2e)
+            for key, floor in (("norm_rel", parity.RTOL), ("tol_units", 1.0)):
+                assert e2e["ours"][g][key] <= E2E_FACTOR * max(e2e["ref"][g][key], floor), (g, key, e2e)
+        assert e2e["ours"]["loss_rel"] <= max(E2E_FACTOR * e2e["ref"]["loss_rel"], parity.LOSS_RTOL), e2e
 
 
 @pytest.mark.gpu
