@@ -68,6 +68,8 @@ def parse_args():
                     help="skip timing the reference's own Triton path on this GPU (baseline/_ref) at N=1")
     ap.add_argument("--families", type=int, default=None, help="config 4: families in the whole batch")
     ap.add_argument("--chunk", type=int, default=128, help="config 4: families per chunk on a GPU")
+    ap.add_argument("--host-builder", action="store_true",
+                    help="config 4: build the static layouts and schedules on the host instead of the device")
     ap.add_argument("--directions", type=int, default=32, help="config 5: tangent directions per pass")
     ap.add_argument("--hvp", action="store_true",
                     help="exact-Hessian HVPs/s (newton/hvp_exact.py) on the --hvp-config family")
@@ -626,30 +628,35 @@ def roofline_from_timers(timers, peak, peak_kind, steps):
     }
 
 
-def batch_setup(world, rank, local, n_total, chunk):
-    """This rank's share of the batched workload (config 4): its contiguous block of families,
-    generated by a spawn pool sized to this rank's share of the host's CPUs, loaded as chunks of
-    at most ``chunk`` families."""
+def batch_setup(world, rank, local, n_total, chunk, host_builder=False):
+    """This rank's share of the batched workload (config 4): its contiguous block of families, as
+    chunks of at most ``chunk`` families -- gene topologies sampled by a spawn pool sized to this
+    rank's share of the host's CPUs, the static layouts and the engine's schedules built on the
+    device (``host_builder``: the whole generator on the host pool, the schedules on the host)."""
     import torch
     import torch.distributed as dist
-    from kbench_b200 import batch
+    from kbench_b200 import batch, builder
 
     dev = torch.device("cuda", local if world > 1 else 0)
     f0, f1 = batch.family_block(n_total, world, rank)
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     workers = max(1, len(os.sched_getaffinity(0)) // max(1, local_world))
     t0 = time.perf_counter()
-    chunks = batch.build_chunks(4, f0, f1, chunk, workers=workers)
+    if host_builder:
+        chunks, gen_t = batch.build_chunks(4, f0, f1, chunk, workers=workers), {}
+    else:  # gene topologies sampled on the host, layouts built on the device
+        chunks, gen_t = builder.generate_chunks(4, f0, f1, chunk, device=dev, workers=workers)
     gen_s = time.perf_counter() - t0
     allreduce = (lambda t: dist.all_reduce(t)) if world > 1 else None
     t0 = time.perf_counter()
     fb = batch.FamilyBatch(chunks, n_total, batch.EngineSolver(dev), allreduce=allreduce)
     load_s = time.perf_counter() - t0
-    theta = torch.from_numpy(chunks[0]["inputs"]["theta"]).to(dev)
-    cw = torch.from_numpy(chunks[0]["inputs"]["col_weights"]).to(dev)
+    theta = torch.as_tensor(chunks[0]["inputs"]["theta"]).to(dev)
+    cw = torch.as_tensor(chunks[0]["inputs"]["col_weights"]).to(dev)
     S = int(chunks[0]["meta"]["S"])
-    info = {"f0": f0, "f1": f1, "rows": fb.rows, "n_chunks": len(chunks), "S": S, "generation_s": round(gen_s, 1),
-            "load_s": round(load_s, 1)}
+    info = {"f0": f0, "f1": f1, "rows": fb.rows, "n_chunks": len(chunks), "S": S, "generation_s": round(gen_s, 2),
+            "load_s": round(load_s, 2), "layout_builder": "host" if host_builder else "device",
+            **{k: round(v, 3) for k, v in gen_t.items()}}
     return dev, fb, theta, cw, info
 
 
@@ -688,6 +695,25 @@ def batch_timed(fb, theta, cw, dev, world, warmup, steps, *, on_timed_start=None
     return float(ms_t.item()), launches, clocks, res
 
 
+def static_builder_timing(info, n_fam_local, sample=4):
+    """The static builder's share of the batched setup: topology sampling (host pool) and the
+    device build of this rank's families, against the host generator's layout stage (clade
+    amalgamation + wave assembly of :mod:`kbench_b200.gen`) timed on ``sample`` families and
+    scaled per family (the families are drawn independently from the same process)."""
+    from kbench_b200 import builder
+    species, topo = builder.family_topologies(4, n_families=sample)
+    t0 = time.perf_counter()
+    builder.host_reference(topo, species)
+    host_per_family = (time.perf_counter() - t0) / sample
+    dev_s = info.get("device_build_s")
+    return {"families": n_fam_local, "topology_sampling_s": info.get("sampling_s"),
+            "device_layout_s": dev_s, "device_schedule_s": info["load_s"],
+            "host_layout_s_per_family": round(host_per_family, 4),
+            "host_layout_s_extrapolated": round(host_per_family * n_fam_local, 1),
+            "layout_speedup_vs_host": round(host_per_family * n_fam_local / dev_s, 1) if dev_s else None,
+            "host_sample": f"{sample} families timed on one host core, scaled per family"}
+
+
 def config4_strong(args, world, rank, local, warmup=1, steps=3):
     """The batched workload (config 4: ``--families``, default all 1,024, S = 1,023) strong-scaled
     over the N ranks of this run -- each rank owns a contiguous block of families, one all-reduce
@@ -696,7 +722,7 @@ def config4_strong(args, world, rank, local, warmup=1, steps=3):
     import torch
     from kbench_b200 import gen
     n_total = int(args.families or gen.CONFIGS[4].n_families)
-    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk)
+    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk, args.host_builder)
     ms, launches, _, res = batch_timed(fb, theta, cw, dev, world, warmup, steps)
     out = {"workload": f"config4: {n_total} families (S={info['S']}) in contiguous blocks over {world} rank(s), "
                        f"chunks of <= {args.chunk}; one all-reduce of [loss, 8*S accumulators] per step",
@@ -704,6 +730,8 @@ def config4_strong(args, world, rank, local, warmup=1, steps=3):
            "steps": steps, "warmup": warmup, "scaling": "strong", "rank0_rows": info["rows"],
            "rank0_generation_s": info["generation_s"], "rank0_load_s": info["load_s"],
            "gpu_launches_rank0": int(launches), "loss": float(res.loss)}
+    if not args.host_builder and rank == 0:
+        out["static_builder"] = static_builder_timing(info, n_fam_local=info["f1"] - info["f0"])
     del fb
     torch.cuda.empty_cache()
     return out
@@ -716,7 +744,7 @@ def batch_arm(args, world, rank, local):
     from kbench_b200 import engine, gen
 
     n_total = int(args.families or gen.CONFIGS[4].n_families)
-    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk)
+    dev, fb, theta, cw, info = batch_setup(world, rank, local, n_total, args.chunk, args.host_builder)
     f0, f1, rows, n_chunks, S = info["f0"], info["f1"], info["rows"], info["n_chunks"], info["S"]
     gen_s, load_s = info["generation_s"], info["load_s"]
     timers = [(st, engine.LevelTimer()) for st in fb.statics]
@@ -766,7 +794,8 @@ def batch_arm(args, world, rank, local):
                             f"= {rows} rows in {n_chunks} chunks of <= {args.chunk}",
                 "parallelism": f"dp{world} (family blocks), one all-reduce of [loss, 8*S accumulators] per step",
                 "l2": "state arrays far larger than L2; no flush needed",
-                "generation_s": round(gen_s, 1), "load_s": round(load_s, 1),
+                "generation_s": round(gen_s, 2), "load_s": round(load_s, 2),
+                "layout_builder": info["layout_builder"],
             },
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": round(n_total * 1000.0 / e_ms, 3), "unit": "families/s",

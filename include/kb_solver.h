@@ -499,6 +499,68 @@ int kb_flow_tangent(int C, const long long* row_split_ptr, const long long* sl, 
                     const long long* item_idx, const int* leaf_state, const unsigned* tour_tables,
                     const unsigned* pair_tables, int n_iters, int S, void* stream);
 
+/* ---- static builder: gene-tree topologies -> wave layout ------------------------------------
+ * No reference counterpart: the reference reads this layout from an external capture
+ * (kbench/runtime.py:47-60 make_static consumes it; capture/capture.py:17-18 notes that the
+ * preprocessing is not part of the project).  The layout is the one kbench_b200/gen.py's host
+ * generator writes (family_from_topologies + assemble_static); these entry points produce the
+ * same arrays on the device for a batch of F families.
+ *
+ * Input: T topologies per family over G gene leaves, int32 left/right [F*T, 2G-1] (nodes
+ * 0..G-1 are the gene leaves, G..2G-2 internal), int32 root [F*T], uint64 leaf_hash [F, G]
+ * (random 64-bit gene-leaf hashes; ~0 is reserved), int64 leaf_species [F, G].
+ * Per family, hash tables of 2^clade_cap_log2 clades and 2^split_cap_log2 splits.
+ *
+ * kb_build_workspace: bytes of the workspace (HOST *bytes_out).
+ * kb_build_tables: clade hashes, clade / split tables, amalg_rounds amalgamation rounds,
+ *   log2((count + alpha) / (n_obs + alpha * n_splits)) per split, rows sorted by
+ *   (size, more than one split, family, hash | gene index), waves; synchronises the stream and
+ *   writes HOST sizes_out[5] = {rows C, splits N, waves, status bits, splits added by the
+ *   amalgamation}.  Status bits: 1 clade table full, 2 split table full (retry with a larger
+ *   table), 4 reserved hash value, 8 malformed topology, 16 missing clade, 32 count overflow;
+ *   the outputs are valid only when the status is 0.
+ * kb_build_emit_scratch: bytes of the scratch kb_build_emit needs for N splits.
+ * kb_build_emit: from the same workspace, the layout arrays: leaf_state int32 [C], item_idx /
+ *   row_local (row - its wave's start) int64 [C], root_row_ids int64 [F]; per split in row order
+ *   (each row's splits by the smaller child hash) sl / sr / reduce_idx / split_row (the parent
+ *   row) int64 [N], row_split_ptr int64 [C+1] (each row's splits), log_split_probs f32 [N]; ge2_flat int64 [C + waves] (wave w's ge2_ptr is
+ *   ge2_flat[t[7] .. t[7] + W - n_eq1]); wave_table int64 [waves, 8] rows t = {start, W, n_eq1,
+ *   split begin, split end, ge2_max_fanout, clade size, ge2 slice start}; synchronises and
+ *   writes HOST k_children_out[2] = {distinct child rows summed over waves, status bits}. */
+int kb_build_workspace(int n_families, int n_topologies, int n_genes, int clade_cap_log2, int split_cap_log2,
+                       long long* bytes_out);
+int kb_build_tables(const int* left, const int* right, const int* root, const unsigned long long* leaf_hash,
+                    int n_families, int n_topologies, int n_genes, int amalg_rounds, double alpha,
+                    int clade_cap_log2, int split_cap_log2, void* ws, long long ws_bytes, long long* sizes_out,
+                    void* stream);
+int kb_build_emit_scratch(long long n_splits, long long* bytes_out);
+int kb_build_emit(const void* ws, const unsigned long long* leaf_hash, const long long* leaf_species,
+                  int n_families, int n_topologies, int n_genes, int clade_cap_log2, int split_cap_log2,
+                  long long n_rows, long long n_splits, long long n_waves, int* leaf_state, long long* item_idx,
+                  long long* root_row_ids, long long* row_local, long long* sl, long long* sr,
+                  long long* reduce_idx, long long* split_row, long long* row_split_ptr, float* log_split_probs,
+                  long long* ge2_flat, long long* wave_table, void* scratch, long long scratch_bytes,
+                  long long* k_children_out, void* stream);
+
+/* The fused engine's schedule (kbench_b200/engine.py build_plan) from a row-ordered layout:
+ * split_row / sl / sr int64 [N] and lsp f32 [N] with the splits grouped by parent row in
+ * increasing row order (the layout kb_build_emit writes), row_split_ptr int64 [C+1] (each row's
+ * splits), wave_split_ptr HOST int64 [n_waves+1] (each wave's split range; a row's children lie in
+ * earlier waves).  Outputs (device): rows int32 [C] (rows by dependency level, stable), split_ptr
+ * int64 [C+1], sl_lv / sr_lv / lsp_lv [N] (splits in that order); dataflow arrays over the
+ * distinct (parent, child) pairs P <= 2N: dep0 / dep_b int32 [C] (distinct children / parents),
+ * ready0 / ready_b int32 [<= C] (rows with none), child_ptr / par_ptr int64 [C+1], child_idx /
+ * par_idx int32 [<= 2N]; HOST level_ptr [n_waves+1] and children [n_waves] (distinct child rows
+ * per level).  Synchronises; HOST sizes_out[5] = {levels, pairs P, ready0 count, ready_b count,
+ * status}.  KB_ERR_ARG when a split's rows are out of range or parents are not in row order. */
+int kb_plan_workspace(long long n_rows, long long n_splits, long long* bytes_out);
+int kb_plan_build(long long n_rows, long long n_splits, int n_waves, const long long* wave_split_ptr,
+                  const long long* split_row, const long long* sl, const long long* sr, const float* lsp,
+                  const long long* row_split_ptr, void* ws, long long ws_bytes, int* rows, long long* split_ptr,
+                  long long* sl_lv, long long* sr_lv, float* lsp_lv, int* dep0, int* ready0, long long* par_ptr,
+                  int* par_idx, int* dep_b, int* ready_b, long long* child_ptr, int* child_idx,
+                  long long* level_ptr, long long* children, long long* sizes_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

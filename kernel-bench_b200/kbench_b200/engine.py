@@ -33,7 +33,7 @@ class LevelPlan:
     sl: torch.Tensor           # int64 [N]
     sr: torch.Tensor
     lsp: torch.Tensor          # f32 [N]
-    level_of: np.ndarray       # level of every row (host)
+    level_of: np.ndarray       # level of every row (host; None for a plan built on the device)
     children_per_level: list   # distinct child rows referenced per level (for the traffic model)
     n_splits: int
     # dataflow schedule (one persistent launch): splits in row-id order, dependency counts, parents
@@ -58,10 +58,16 @@ def _sorted_unique(keys: np.ndarray) -> np.ndarray:
 
 
 def build_plan(static) -> LevelPlan:
-    """Dependency levels and the per-row split CSR, from the reference wave layout."""
+    """Dependency levels and the per-row split CSR, from the reference wave layout (on the device
+    by ``kb_plan_build`` when the static carries the flat split arrays of a device-built layout,
+    else on the host)."""
     cached = getattr(static, "_plan", None)
     if cached is not None:
         return cached
+    flat = getattr(static, "flat_layout", None)
+    if flat is not None and flat["sl"].is_cuda:
+        static._plan = build_plan_device(static)
+        return static._plan
     wl = static.wave_layout
     dev = wl["leaf_state_index"].device
     C = int(wl["leaf_state_index"].numel())
@@ -142,6 +148,48 @@ def build_plan(static) -> LevelPlan:
     )
     static._plan = plan
     return plan
+
+
+def build_plan_device(static) -> LevelPlan:
+    """:func:`build_plan` on the device from ``static.flat_layout`` (the row-ordered split arrays a
+    device-built layout carries): the same arrays, computed by ``kb_plan_build``."""
+    fl = static.flat_layout
+    dev = fl["sl"].device
+    C = int(static.wave_layout["leaf_state_index"].numel())
+    N = int(fl["sl"].numel())
+    wsp = np.asarray(fl["wave_split_ptr"], dtype=np.int64)
+    nw = int(wsp.shape[0]) - 1
+    nbytes = np.zeros(1, dtype=np.int64)
+    _lib.call("kb_plan_workspace", C, N, nbytes.ctypes.data)
+    ws = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    i64 = dict(dtype=torch.int64, device=dev)
+    rows, split_ptr = torch.empty(C, **i32), torch.empty(C + 1, **i64)
+    sl_lv, sr_lv = torch.empty(N, **i64), torch.empty(N, **i64)
+    lsp_lv = torch.empty(N, dtype=torch.float32, device=dev)
+    dep0, ready0, dep_b, ready_b = (torch.empty(C, **i32) for _ in range(4))
+    par_ptr, child_ptr = torch.empty(C + 1, **i64), torch.empty(C + 1, **i64)
+    par_idx, child_idx = torch.empty(max(2 * N, 1), **i32), torch.empty(max(2 * N, 1), **i32)
+    level_ptr = np.zeros(nw + 1, dtype=np.int64)
+    children = np.zeros(nw, dtype=np.int64)
+    sizes = np.zeros(5, dtype=np.int64)
+    p = _lib.ptr
+    _lib.call("kb_plan_build", C, N, nw, wsp.ctypes.data, p(fl["split_row"]), p(fl["sl"]), p(fl["sr"]),
+              p(fl["lsp"]), p(fl["row_split_ptr"]), p(ws), int(nbytes[0]), p(rows), p(split_ptr), p(sl_lv), p(sr_lv),
+              p(lsp_lv), p(dep0), p(ready0), p(par_ptr), p(par_idx), p(dep_b), p(ready_b), p(child_ptr),
+              p(child_idx), level_ptr.ctypes.data, children.ctypes.data, sizes.ctypes.data,
+              _lib.stream_handle(dev))
+    n_levels, P, n_r0, n_rb = (int(x) for x in sizes[:4])
+    if int(sizes[4]):
+        raise RuntimeError(f"kb_plan_build: status {int(sizes[4])}")
+    del ws
+    return LevelPlan(
+        n_levels=n_levels, level_ptr=level_ptr[:n_levels + 1].tolist(), rows=rows, split_ptr=split_ptr,
+        sl=sl_lv, sr=sr_lv, lsp=lsp_lv, level_of=None, children_per_level=children[:n_levels].tolist(), n_splits=N,
+        row_split_ptr=fl["row_split_ptr"], sl_r=fl["sl"], sr_r=fl["sr"], lsp_r=fl["lsp"],
+        dep0=dep0, ready0=ready0[:n_r0], par_ptr=par_ptr, par_idx=par_idx[:P], dep_b=dep_b, ready_b=ready_b[:n_rb],
+        child_ptr=child_ptr, child_idx=child_idx[:P],
+    )
 
 
 def supported(static) -> bool:

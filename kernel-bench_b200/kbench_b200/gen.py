@@ -235,25 +235,55 @@ def _clades(left, right, root, weights):
     return out
 
 
-def make_family(cfg: ProblemConfig, species: dict, seed: int, *, alpha: float = 0.5,
-                amalg_rounds: int = 2) -> dict:
-    """One gene family: rows (clades) and their splits, in gene-clade hash space."""
+def sample_topologies(cfg: ProblemConfig, species: dict, seed: int) -> dict:
+    """The gene side of one family: ``T`` topologies over ``G`` gene leaves (one random base
+    topology plus ``T-1`` copies perturbed by ``spr_moves`` nearest-neighbour interchanges), the
+    gene leaves' hashes (random odd 64-bit integers) and their species leaves.
+
+    Returns int32 ``left`` / ``right`` [T, 2G-1] (gene leaves are nodes 0..G-1 with children -1;
+    internal nodes G..2G-2), int32 ``root`` [T], uint64 ``leaf_hash`` [G], int64
+    ``leaf_species`` [G].  This is the input of the static builders (:func:`family_from_topologies`
+    on the host, ``kbench_b200.builder`` on the device)."""
     rng = np.random.Generator(np.random.PCG64(seed))
-    G = cfg.n_genes
+    G, T = cfg.n_genes, cfg.n_topologies
     weights = rng.integers(0, 2 ** 63, size=G, dtype=np.int64).astype(np.uint64) * _U64(2) + _U64(1)
     leaf_species = species["_species_leaves"][rng.integers(0, len(species["_species_leaves"]), size=G)]
     base_l, base_r, base_p, base_root = _random_merge_tree(G, rng)
     base_l, base_r, base_p = base_l.tolist(), base_r.tolist(), base_p.tolist()
-    wlist = [int(w) for w in weights]
-    clade_size = {}
-    clade_count = {}
-    splits = {}        # clade hash -> {split key: observed count}
-    for t in range(cfg.n_topologies):
+    n_nodes = 2 * G - 1
+    lefts = np.empty((T, n_nodes), dtype=np.int32)
+    rights = np.empty((T, n_nodes), dtype=np.int32)
+    roots = np.empty(T, dtype=np.int32)
+    for t in range(T):
         left, right, parent = list(base_l), list(base_r), list(base_p)
         root = base_root
         if t > 0:
             root = _nni(left, right, parent, root, cfg.spr_moves, rng)
-        for hx, sx, ha, hb in _clades(left, right, root, wlist):
+        lefts[t] = left
+        rights[t] = right
+        roots[t] = root
+    return {"left": lefts, "right": rights, "root": roots, "leaf_hash": weights,
+            "leaf_species": leaf_species.astype(np.int64)}
+
+
+def make_family(cfg: ProblemConfig, species: dict, seed: int, *, alpha: float = 0.5,
+                amalg_rounds: int = 2) -> dict:
+    """One gene family: rows (clades) and their splits, in gene-clade hash space."""
+    return family_from_topologies(sample_topologies(cfg, species, seed), alpha=alpha, amalg_rounds=amalg_rounds)
+
+
+def family_from_topologies(topo: dict, *, alpha: float = 0.5, amalg_rounds: int = 2) -> dict:
+    """Clade amalgamation of one family on the host: the union of the topologies' clades (rows)
+    with their observed splits, widened by ``amalg_rounds`` rounds of splits one rearrangement
+    away whose two parts are both clades, and log2 smoothed conditional split frequencies
+    ``log2((count + alpha) / (n_obs + alpha * n_splits))`` per clade."""
+    wlist = [int(w) for w in topo["leaf_hash"]]
+    clade_size = {}
+    clade_count = {}
+    splits = {}        # clade hash -> {split key: observed count}
+    for t in range(topo["left"].shape[0]):
+        left, right = topo["left"][t].tolist(), topo["right"][t].tolist()
+        for hx, sx, ha, hb in _clades(left, right, int(topo["root"][t]), wlist):
             clade_size[hx] = sx
             clade_count[hx] = clade_count.get(hx, 0) + 1
             key = (ha, hb) if ha < hb else (hb, ha)
@@ -304,7 +334,7 @@ def make_family(cfg: ProblemConfig, species: dict, seed: int, *, alpha: float = 
         "clade_size": clade_size,
         "splits": split_logp,
         "leaf_hashes": leaf_hashes,
-        "leaf_species": leaf_species.astype(np.int64),
+        "leaf_species": np.asarray(topo["leaf_species"], dtype=np.int64),
         "root_hash": root_hash,
     }
 

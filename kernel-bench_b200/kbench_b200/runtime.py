@@ -51,6 +51,8 @@ def make_static(captured: dict, device, *, engine: str = "fused") -> SimpleNames
         solver_options=so,
         warm_E=None,
         engine=engine,
+        # flat row-ordered split arrays of a device-built layout (kbench_b200.builder), else None
+        flat_layout=move_to_device(st.get("flat_layout"), device),
     )
     sh = static.state_helpers
     for key in ("S", "max_ancestor_depth"):
