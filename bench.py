@@ -504,8 +504,26 @@ def reference_hvp_arm(args, world):
     }), flush=True)
 
 
+def reference_interpreter_sample(full_rows, n_proc, genes=8):
+    """The reference's own code on the host cores (``baseline/interpreter.py``: its stock runtime
+    and Triton kernels under ``TRITON_INTERPRET=1``): ``n_proc`` processes started together, each
+    one forward + backward of a ``genes``-gene family on the config-3 species tree.  Returns the
+    per-process results and the solve time of a ``full_rows``-row family extrapolated per row."""
+    from baseline import interpreter
+    why = interpreter.unavailable_reason()
+    if why:
+        return None, why
+    runs = interpreter.parallel(("sample", genes, 3000), n_proc)
+    rows = runs[0]["rows"]
+    med = statistics.median(r["solve_s"] for r in runs)
+    return {"runs": n_proc, "sample_rows": rows, "sample_solve_s_median": round(med, 2),
+            "solve_s_extrapolated": med * full_rows / rows / n_proc}, None
+
+
 def reference_arm(args, world, rank):
-    """--impl reference: the oracle port of the reference algorithm on the host cores."""
+    """--impl reference: the reference's own implementation on the host cores (its runtime and
+    Triton kernels under the Triton interpreter, on a bounded sample, extrapolated per row), with
+    the numpy port of the same algorithm as a secondary figure."""
     if rank != 0:
         return
     if args.hvp:
@@ -521,31 +539,55 @@ def reference_arm(args, world, rank):
         full_rows = int(gen.generate(args.config, as_torch=False)["meta"]["C"])
         leaves = gen.CONFIGS[3].n_species
     n_proc = host_threads()
-    rows, walls = parallel_oracle("solve", (48, leaves, 3000), args.warmup + args.steps, n_proc)
-    # n_proc samples of `rows` rows per wall time; one solve is full_rows rows
-    solve_s = statistics.median(walls[args.warmup:]) * full_rows / rows / n_proc
     S = 2 * leaves - 1
+
+    def per_step(solve_s):
+        if batched:
+            return solve_s * n_total, n_total / (solve_s * n_total)
+        return solve_s, 1.0 / solve_s
+
     if batched:
-        step_s = solve_s * n_total
-        value, unit = n_total / step_s, "families/s"
-        metric = "fwd+bwd families/sec (batched config 4: S=1023, ~16k rows per family, shared theta)"
+        unit, metric = "families/s", "fwd+bwd families/sec (batched config 4: S=1023, ~16k rows per family, shared theta)"
         what = f"extrapolated per row to one {full_rows}-row family, x{n_total} families"
     else:
-        step_s = solve_s
-        value, unit, metric = 1.0 / solve_s, "solves/s", METRIC
+        unit, metric = "solves/s", METRIC
         what = f"extrapolated per row to C={full_rows}"
-    sample = (f"numpy oracle forward+backward of a {rows}-row family on the config-{args.config} species "
-              f"tree (S={S}), {n_proc} single-threaded processes at once, {what}")
+    # secondary: the numpy port of the same algorithm, W + K passes
+    rows_p, walls = parallel_oracle("solve", (48, leaves, 3000), args.warmup + args.steps, n_proc)
+    port_step_s, port_value = per_step(statistics.median(walls[args.warmup:]) * full_rows / rows_p / n_proc)
+    port = {"value": port_value, "unit": unit, "cores": n_proc, "kind": "port", "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": port_step_s * 1e3,
+            "sample": f"numpy oracle forward+backward of a {rows_p}-row family on the config-{args.config} species "
+                      f"tree (S={S}), {n_proc} single-threaded processes at once, {what}"}
+    # primary: the reference's own runtime and kernels under the Triton interpreter (one pass; a
+    # pass is ~30 s of CPU per process, so the requested K / W apply to the port only)
+    interp, why = reference_interpreter_sample(full_rows, n_proc)
+    if interp is None:
+        value, step_s, kind, cpu = port_value, port_step_s, "port", port
+        extrap = {"formula": "seconds per solve = median pass wall time x full_rows / sample_rows / processes",
+                  "sample_rows": rows_p, "full_rows": full_rows, "processes": n_proc, "interpreter_unavailable": why}
+        steps, warmup = args.steps, args.warmup
+    else:
+        step_s, value = per_step(interp["solve_s_extrapolated"])
+        kind = "reference"
+        cpu = {"value": value, "unit": unit, "cores": n_proc, "kind": "reference",
+               "sample": f"the reference's kbench.runtime forward+backward over its Triton kernels under "
+                         f"TRITON_INTERPRET=1 (baseline/_ref), a {interp['sample_rows']}-row family on the "
+                         f"config-{args.config} species tree (S={S}), {n_proc} processes at once, {what}"}
+        extrap = {"formula": "seconds per solve = median per-process solve time x full_rows / sample_rows / processes",
+                  "sample_rows": interp["sample_rows"], "full_rows": full_rows, "processes": n_proc,
+                  "sample_solve_s_median": interp["sample_solve_s_median"]}
+        steps, warmup = 1, 0
     line = {
-        "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
         "scaling": "strong" if batched else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)", "impl": "reference",
-        "config": {"workload": f"config{args.config} family, CPU sample", "sample_rows": rows},
-        "extrapolated": {"measured": f"{n_proc} processes x one {rows}-row forward+backward each, per pass",
-                         "formula": "seconds per solve = median pass wall time x full_rows / sample_rows / processes",
-                         "sample_rows": rows, "full_rows": full_rows, "processes": n_proc},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": n_proc, "kind": "port", "sample": sample},
+        "config": {"workload": f"config{args.config} family, CPU sample", "requested_steps": args.steps,
+                   "requested_warmup": args.warmup},
+        "extrapolated": extrap,
+        "cpu_baseline": cpu,
+        "port_secondary": port,
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

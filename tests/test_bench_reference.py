@@ -20,3 +20,21 @@ def test_parallel_oracle_reports_a_failing_sample():
 
 def test_host_threads_is_bounded():
     assert 1 <= bench.host_threads() <= 64
+
+
+def test_reference_interpreter_solves_on_the_cpu():
+    """The reference's own runtime and Triton kernels under TRITON_INTERPRET=1 (the CPU baseline
+    of the reference arm) run in a spawned process and agree with the oracle's loss."""
+    from baseline import interpreter
+    if interpreter.unavailable_reason():
+        pytest.skip(interpreter.unavailable_reason())
+    import numpy as np
+    from kbench_b200 import gen
+    from oracle import kb_oracle
+    (res,) = interpreter.parallel(("tiny", 0, 7), 1)
+    cap = gen.generate(gen.ProblemConfig("tiny", 4, 6, 3, 4, 12), seed=7, as_torch=False)
+    st = dict(cap["static"])
+    st["solver_options"] = cap["meta"]["solver_options"]
+    loss, _ = kb_oracle.forward(st, cap["inputs"]["theta"], cap["inputs"]["col_weights"])
+    assert res["rows"] == int(cap["meta"]["C"]) and res["solve_s"] > 0
+    assert abs(res["loss"] - float(loss)) <= 1e-4 * abs(float(loss)), (res["loss"], float(loss))
