@@ -271,3 +271,36 @@ def host_reference(topo: dict, species: dict, *, alpha: float = 0.5, amalg_round
 
 def cpu_count() -> int:
     return len(os.sched_getaffinity(0))
+
+
+def main():
+    """``python -m kbench_b200.builder --config 4 --families 128``: sample the topologies, build the
+    static layout and the engine's schedule on the GPU once, and print the sizes and timings."""
+    import argparse
+    import json
+    import time
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", type=int, default=4)
+    ap.add_argument("--families", type=int, default=None)
+    ap.add_argument("--workers", type=int, default=cpu_count())
+    a = ap.parse_args()
+    from . import engine, runtime
+    dev = torch.device("cuda:0")
+    species, topo = family_topologies(a.config, n_families=a.families, workers=a.workers)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    static, stats = build_static(topo, species, dev)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    cap = _captured(*_resolve(a.config, None), species, static, stats, int(topo["leaf_hash"].shape[0]), 0, None)
+    st = runtime.make_static(cap, dev)
+    plan = engine.build_plan(st)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    print(json.dumps({"config": a.config, "families": int(topo["leaf_hash"].shape[0]), "rows": stats["C"],
+                      "splits": stats["n_splits"], "waves": stats["n_waves"], "levels": plan.n_levels,
+                      "layout_s": round(t1 - t0, 4), "schedule_s": round(t2 - t1, 4)}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1061,9 +1061,18 @@ __global__ void distinct_flags_kernel(const u64* k, long long n, int* flag) {
   for (long long i = gtid(); i < n; i += gstride()) flag[i] = (i == 0 || k[i] != k[i - 1]) ? 1 : 0;
 }
 
+// cnt[hi] += number of flagged keys with high part hi; the keys are sorted, so the lanes of a warp
+// mostly share hi: one atomic per distinct hi per warp.
 __global__ void count_by_hi_kernel(const u64* k, const int* flag, long long n, long long C, int* cnt) {
-  for (long long i = gtid(); i < n; i += gstride())
-    if (flag[i]) atomicAdd(cnt + (long long)(k[i] / (u64)C), 1);
+  const long long n_pad = (n + 31) / 32 * 32;
+  for (long long i = gtid(); i < n_pad; i += gstride()) {
+    const bool valid = i < n;
+    const long long hi = valid ? (long long)(k[i] / (u64)C) : -1;
+    const int f = valid ? flag[i] : 0;
+    const unsigned peers = __match_any_sync(0xffffffffu, hi);
+    const unsigned hits = __ballot_sync(0xffffffffu, f != 0) & peers;
+    if (valid && (threadIdx.x & 31) == __ffs(peers) - 1 && hits) atomicAdd(cnt + hi, __popc(hits));
+  }
 }
 
 // distinct keys (flag[i] == 1 at position pos[i] of the exclusive scan) -> out
