@@ -31,7 +31,8 @@ _lib = None
 # (kb_abi_version and argument-only failures excluded).  Read by bench.py to report how many
 # of this library's kernels ran inside a timed region.
 LAUNCHES: dict = {}
-_NO_LAUNCH = {"kb_abi_version", "kb_tour_layout", "kb_backward_layout", "kb_backward_ctas"}
+_NO_LAUNCH = {"kb_abi_version", "kb_tour_layout", "kb_backward_layout", "kb_backward_ctas", "kb_build_workspace",
+              "kb_build_emit_scratch", "kb_plan_workspace"}
 
 
 def parse_header(text: str | None = None) -> dict[str, list]:
