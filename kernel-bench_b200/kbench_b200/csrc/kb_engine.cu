@@ -695,35 +695,59 @@ struct BulkStage {
 // Stage rows s0 and s1 (S floats each) into slots B0 / B1 (NTV + 4 floats each), padded with
 // `pad` up to NTV; returns the aligned views.  Called by all threads after the slots' previous
 // readers are done (a barrier); one arrival on `bar` (with the copies' byte count) per call;
-// completion: bulk_wait on the same mbarrier, then a barrier.
+// completion: bulk_wait on the same mbarrier, then bulk_fix_pad on each view, then a barrier.
+// Where the 16-byte aligned cover of a row, [row - lead, row + S rounded up), lies inside
+// [lo, hi) (the buffer the rows belong to), ONE bulk copy brings the cover -- a few floats of
+// the neighbouring rows included, never read -- and no thread loads the row's unaligned ends
+// (they would hold their warp up for a load latency per split); otherwise the aligned middle
+// goes by bulk copy and the ends by loads.
 __device__ __forceinline__ void stage_rows_bulk(float* B0, const float* s0, float* B1, const float* s1, int S,
                                                 int NTV, unsigned long long* bar, const float** v0,
-                                                const float** v1, float pad = neg_inf()) {
+                                                const float** v1, float pad = neg_inf(), const float* lo = nullptr,
+                                                const float* hi = nullptr) {
   const int a0 = (int)(((16u - ((unsigned)(uintptr_t)s0 & 15u)) & 15u) >> 2);
   const int a1 = (int)(((16u - ((unsigned)(uintptr_t)s1 & 15u)) & 15u) >> 2);
-  float* P0 = B0 + ((4 - a0) & 3);
-  float* P1 = B1 + ((4 - a1) & 3);
-  const int nb0 = S > a0 ? (S - a0) >> 2 : 0, nb1 = S > a1 ? (S - a1) >> 2 : 0;
+  const int l0 = (4 - a0) & 3, l1 = (4 - a1) & 3;  // floats of the cover before the row
+  float* P0 = B0 + l0;
+  float* P1 = B1 + l1;
+  const int c0 = (l0 + S + 3) >> 2, c1 = (l1 + S + 3) >> 2;  // 16-byte units of the covers
+  const bool w0 = lo != nullptr && s0 - l0 >= lo && s0 - l0 + 4 * c0 <= hi;
+  const bool w1 = lo != nullptr && s1 - l1 >= lo && s1 - l1 + 4 * c1 <= hi;
+  const int nb0 = w0 ? c0 : (S > a0 ? (S - a0) >> 2 : 0), nb1 = w1 ? c1 : (S > a1 ? (S - a1) >> 2 : 0);
   if (threadIdx.x == 0) {
     // generic-proxy writes -> this thread's bulk copies: the child rows other CTAs wrote (made
     // visible to this thread by the queue's acquire).  The slots' previous readers finished before
     // the caller's barrier, which orders them before any write to the slots.
     asm volatile("fence.proxy.async.global;" ::: "memory");
     mbar_arrive_expect_tx(bar, (unsigned)(16 * (nb0 + nb1)));
-    if (nb0) bulk_copy_g2s(P0 + a0, s0 + a0, (unsigned)(16 * nb0), bar);
-    if (nb1) bulk_copy_g2s(P1 + a1, s1 + a1, (unsigned)(16 * nb1), bar);
+    if (nb0) bulk_copy_g2s(w0 ? B0 : P0 + a0, w0 ? s0 - l0 : s0 + a0, (unsigned)(16 * nb0), bar);
+    if (nb1) bulk_copy_g2s(w1 ? B1 : P1 + a1, w1 ? s1 - l1 : s1 + a1, (unsigned)(16 * nb1), bar);
   }
-  const int h0 = a0 < S ? a0 : S, h1 = a1 < S ? a1 : S;
-  for (int s = threadIdx.x; s < h0; s += blockDim.x) P0[s] = __ldcg(s0 + s);
-  for (int s = threadIdx.x; s < h1; s += blockDim.x) P1[s] = __ldcg(s1 + s);
-  for (int s = h0 + 4 * nb0 + threadIdx.x; s < S; s += blockDim.x) P0[s] = __ldcg(s0 + s);
-  for (int s = h1 + 4 * nb1 + threadIdx.x; s < S; s += blockDim.x) P1[s] = __ldcg(s1 + s);
-  for (int s = S + threadIdx.x; s < NTV; s += blockDim.x) {
+  if (!w0) {
+    const int h0 = a0 < S ? a0 : S;
+    for (int s = threadIdx.x; s < h0; s += blockDim.x) P0[s] = __ldcg(s0 + s);
+    for (int s = h0 + 4 * nb0 + threadIdx.x; s < S; s += blockDim.x) P0[s] = __ldcg(s0 + s);
+  }
+  if (!w1) {
+    const int h1 = a1 < S ? a1 : S;
+    for (int s = threadIdx.x; s < h1; s += blockDim.x) P1[s] = __ldcg(s1 + s);
+    for (int s = h1 + 4 * nb1 + threadIdx.x; s < S; s += blockDim.x) P1[s] = __ldcg(s1 + s);
+  }
+  // the padding the covers' copies may overwrite (at most 3 floats past S) is written by
+  // bulk_fix_pad after the wait; the rest now
+  for (int s = S + 3 + threadIdx.x; s < NTV; s += blockDim.x) {
     P0[s] = pad;
     P1[s] = pad;
   }
   *v0 = P0;
   *v1 = P1;
+}
+
+// The first padding entries of a staged view, after its copies completed (the same threads'
+// bulk_wait) and before the barrier that publishes the slot.
+__device__ __forceinline__ void bulk_fix_pad(const float* P, int S, int NTV, float pad = neg_inf()) {
+  const int s = S + (int)threadIdx.x;
+  if (threadIdx.x < 3 && s < NTV) const_cast<float*>(P)[s] = pad;
 }
 
 __device__ __forceinline__ void bulk_wait(BulkStage& bs, int b) {
@@ -804,7 +828,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
       const long long l = a.sp.sl[i0], r = a.sp.sr[i0];
       if (bulk) {
         stage_rows_bulk(stg, a.Pi_src + (size_t)l * S, stg + RS, a.Pi_src + (size_t)r * S, S, NTV, bs->bar, &cPl,
-                        &cPr);
+                        &cPr, neg_inf(), a.Pi_src, a.Pi_src + (size_t)a.n_rows * S);
       } else {
         cPl = stage_row_cg(stg, a.Pi_src + (size_t)l * S, S, NTV, true);
         cPr = stage_row_cg(stg + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
@@ -821,8 +845,13 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
         bl[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)li * S + s) : 0.f;
         br[k] = s < S ? ld_row<DF>(a.Pibar_src + (size_t)ri * S + s) : 0.f;
       }
-      if (bulk) bulk_wait(*bs, par);
-      else cp_async_wait_all();
+      if (bulk) {
+        bulk_wait(*bs, par);
+        bulk_fix_pad(cPl, S, NTV);
+        bulk_fix_pad(cPr, S, NTV);
+      } else {
+        cp_async_wait_all();
+      }
       __syncthreads();  // split i staged; everyone is done with split i-1's slots
       const float *nPl = nullptr, *nPr = nullptr;
       if (i + 1 < i1) {
@@ -830,7 +859,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
         const long long l = a.sp.sl[i + 1], r = a.sp.sr[i + 1];
         if (bulk) {
           stage_rows_bulk(nb, a.Pi_src + (size_t)l * S, nb + RS, a.Pi_src + (size_t)r * S, S, NTV,
-                          bs->bar + (par ^ 1), &nPl, &nPr);
+                          bs->bar + (par ^ 1), &nPl, &nPr, neg_inf(), a.Pi_src, a.Pi_src + (size_t)a.n_rows * S);
         } else {
           nPl = stage_row_cg(nb, a.Pi_src + (size_t)l * S, S, NTV, true);
           nPr = stage_row_cg(nb + RS, a.Pi_src + (size_t)r * S, S, NTV, true);
@@ -1615,6 +1644,12 @@ __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row
         stage_rows_bulk(b + 2 * RS, dPa + ol, b + 3 * RS, dPa + orr, S, NTV, bs->bar, &vQla, &vQra, 0.f);
         stage_rows_bulk(b + 4 * RS, dPb + ol, b + 5 * RS, dPb + orr, S, NTV, bs->bar, &vQlb, &vQrb, 0.f);
         bulk_wait(*bs, 0);
+        bulk_fix_pad(vPl, S, NTV);
+        bulk_fix_pad(vPr, S, NTV);
+        bulk_fix_pad(vQla, S, NTV, 0.f);
+        bulk_fix_pad(vQra, S, NTV, 0.f);
+        bulk_fix_pad(vQlb, S, NTV, 0.f);
+        bulk_fix_pad(vQrb, S, NTV, 0.f);
       } else {
 #pragma unroll
         for (int k = 0; k < VF; ++k) {
