@@ -113,7 +113,7 @@ class EngineSolver:
     def chunk(self, static, theta, col_weights, prep, acc):
         """Forward + accumulating backward of one chunk; returns its loss (device scalar)."""
         from . import engine, glue, runtime
-        out, extras = engine.forward(static, theta, col_weights, prep=prep)
+        out, extras = engine.forward(static, theta, col_weights, prep=prep, check_errors=False)
         loss = glue.nll_from_root_rows(out[4], out[0])
         saved = dict(zip(runtime.FORWARD_SAVED_NAMES, out))
         saved.update(extras)
@@ -123,13 +123,19 @@ class EngineSolver:
     def reduce_acc(self, acc, S):
         return acc.sum(dim=0)[:, :S]
 
+    def check(self, static):
+        """Raise if a chunk's dataflow launches gave up a wait (one host synchronisation)."""
+        from . import engine
+        engine.check_flow_errors(static)
+
     def finish(self, static, theta, col_weights, prep, acc8, n_fam):
         from . import engine, glue
         S = int(static.state_helpers["S"])
         g = engine.grad_accumulators_from(prep.E, S, acc8.to(torch.float32))
         saved = {"E": prep.E, "E_s1": prep.E_s1, "E_s2": prep.E_s2, "Ebar": prep.Ebar, "log_pS": prep.pS,
                  "log_pD": prep.pD, "log_pL": prep.pL, "max_coupling": prep.mc, "col_log_probs": prep.clp}
-        return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, prep.ucw)
+        # convergence read back by check() at the end of the step
+        return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, prep.ucw, check=False)
 
 
 @dataclass
@@ -170,4 +176,8 @@ class FamilyBatch:
             self.allreduce(packed)
         loss_t, acc8 = unpack(packed, S)
         grad_theta, grad_col = self.solver.finish(s0, theta, col_weights, prep, acc8, self.n_total)
+        check = getattr(self.solver, "check", None)
+        if check is not None:  # after the whole step is enqueued
+            for static in self.statics:
+                check(static)
         return StepResult(loss_t[0], grad_theta, grad_col)

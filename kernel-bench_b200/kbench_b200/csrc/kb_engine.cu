@@ -216,6 +216,7 @@ struct FwdArgs {
   float* residual;  // [C] or null
   int* fallback_count;  // device counter of rows recomputed in log space (may be null)
   int force_log;        // every row takes the log-space iteration (constants below 2^-26)
+  const int* force_log_dev;  // the same decision as a device word (ORed in; may be null)
   int n_rows;
   int pi_iters;
 };
@@ -390,7 +391,7 @@ __global__ void __launch_bounds__(1024, 1) level_forward_kernel(FwdArgs a) {
   // with the dts / leaf terms taken relative to the new scale R + log2(zmax).
   float z[VPT], td[VPT];
   float zmax_l = 0.f, zsum_l = 0.f;
-  bool init_bad = a.force_log != 0;
+  bool init_bad = a.force_log != 0 || (a.force_log_dev != nullptr && *a.force_log_dev != 0);
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int s = threadIdx.x + k * NT;
@@ -907,7 +908,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
   unsigned ce[VF], tr[VF];
   float z[VF], td[VF], kA[VF], kB[VF], kC1[VF], kC2[VF];
   float zmax_l = 0.f, zsum_l = 0.f;
-  bool bad = a.force_log != 0;
+  bool bad = a.force_log != 0 || (a.force_log_dev != nullptr && *a.force_log_dev != 0);
 #pragma unroll
   for (int k = 0; k < VF; ++k) {
     const int s = tid + k * NT;
@@ -2493,6 +2494,7 @@ extern "C" int kb_level_forward(const int* rows, const long long* split_ptr, int
   a.Pi_src = Pi_src; a.Pibar_src = Pibar_src; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = n_rows;
   a.force_log = force_log_space != 0;
+  a.force_log_dev = nullptr;
   a.pi_iters = pi_iters;
   cudaStream_t st = (cudaStream_t)stream;
   int nt4, vf4;
@@ -2693,7 +2695,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
                                const int* node_child1, const int* node_child2, const int* node_subtree_start,
                                const int* node_subtree_end, const int* jumps, int K, const long long* item_idx,
                                const int* leaf_state, const unsigned* tour_tables, const float* tour_consts,
-                               int force_log_space, int pi_iters, int S, void* stream) {
+                               int force_log_space, const int* force_log_flag, int pi_iters, int S, void* stream) {
   if (S <= 0 || C < 0 || K < 0 || pi_iters < 2 || n_ready0 < 0 || n_ready0 > C || max_polls < 1) return KB_ERR_ARG;
   if (tour_tables == nullptr || tour_consts == nullptr || dts_save == nullptr || counters == nullptr) return KB_ERR_ARG;
   int nt, vf;
@@ -2710,6 +2712,7 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
   a.Pi_src = pi; a.Pibar_src = pibar; a.pi = pi; a.pibar = pibar; a.row_max = pibar_row_max;
   a.dts_save = dts_save; a.residual = residual; a.fallback_count = fallback_count; a.n_rows = C;
   a.force_log = force_log_space != 0;
+  a.force_log_dev = force_log_flag;
   a.pi_iters = pi_iters;
   Fwd4Args a4;
   a4.f = a;

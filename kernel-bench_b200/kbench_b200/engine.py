@@ -271,7 +271,13 @@ class Prep:
     k: dict
     lin: torch.Tensor
     k4: torch.Tensor | None   # tour kernel constants [G, NTV, 4] (None where the tour kernel does not apply)
-    force_log: bool = False   # constants outside the linear iteration's exact range: every row in log space
+    # constants outside the linear iteration's exact range (every row in log space), as a device
+    # int32 word: the dataflow forward reads it on the device, without a host round trip
+    force_log_dev: torch.Tensor | None = None
+
+    @property
+    def force_log(self) -> bool:
+        return self.force_log_dev is not None and bool(self.force_log_dev.item())
 
 
 # Smallest log2 of a linear-iteration constant for which the forward kernels' linear-space update is
@@ -280,13 +286,19 @@ class Prep:
 LINEAR_MIN_LOG2 = -26.0
 
 
-def linear_range_ok(k: dict) -> bool:
-    """Whether every finite exponent of the forward's linear constants -- log2(2^dl + 2^ebar) (at
-    least max(dl, ebar)), mc + e, sl1, sl2 -- is at least ``LINEAR_MIN_LOG2``.  Below it (extreme
-    rates) a term could underflow to zero where the reference's log-space update keeps it finite,
-    so the engine then runs every row's iterations in log space."""
+def linear_range_flag(k: dict) -> torch.Tensor:
+    """Device int32 [1]: 1 unless every finite exponent of the forward's linear constants --
+    log2(2^dl + 2^ebar) (at least max(dl, ebar)), mc + e, sl1, sl2 -- is at least
+    ``LINEAR_MIN_LOG2``.  Below it (extreme rates) a term could underflow to zero where the
+    reference's log-space update keeps it finite, so the engine then runs every row's iterations
+    in log space."""
     ex = torch.stack([torch.maximum(k["dl"], k["ebar"]), k["mc"] + k["e"], k["sl1"], k["sl2"]])
-    return not bool(((ex < LINEAR_MIN_LOG2) & torch.isfinite(ex)).any())
+    return ((ex < LINEAR_MIN_LOG2) & torch.isfinite(ex)).any().reshape(1).to(torch.int32)
+
+
+def linear_range_ok(k: dict) -> bool:
+    """Host view of :func:`linear_range_flag` (one synchronisation)."""
+    return not bool(linear_range_flag(k).item())
 
 
 @torch.no_grad()
@@ -310,13 +322,14 @@ def prepare(static, theta, col_weights) -> Prep:
         _lib.call("kb_lin_consts_tour", k["dl"].data_ptr(), k["ebar"].data_ptr(), k["mc"].data_ptr(),
                   k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), G, S, k4.data_ptr(),
                   _lib.stream_handle(dev))
-    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin, k4, not linear_range_ok(k))
+    return Prep(pS, pD, pL, mc, clp, ucw, E, E_s1, E_s2, Ebar, k, lin, k4, linear_range_flag(k))
 
 
-def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | None = None):
+def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | None = None, check_errors=True):
     """theta -> the 13 forward intermediates (same order as ``glue.solve_e_pi``) and the saved
     split reductions ``dts_wave`` [C,S] for the backward.  ``prep`` (from :func:`prepare` on the
-    same theta and species tree) skips the parameter / E-step stage."""
+    same theta and species tree) skips the parameter / E-step stage.  ``check_errors=False`` leaves
+    the dataflow launch's error check (a host synchronisation) to the backward that follows."""
     if not supported(static):
         return glue.solve_e_pi(static, theta, col_weights, pi_residual_out=pi_residual_out), {}
     so = static.solver_options
@@ -327,7 +340,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
     sh, wl = static.state_helpers, static.wave_layout
     S = int(sh["S"])
     if prep is None:
-        if not glue.col_weights_are_uniform(col_weights):
+        if not glue.col_weights_uniform_for(static, col_weights):
             # the level kernels' linear-space update assumes uniform column weights (the layout of
             # every benchmark config); weighted columns take the wrapper-by-wrapper driver
             return glue.solve_e_pi(static, theta, col_weights, pi_residual_out=pi_residual_out), {}
@@ -365,10 +378,11 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                 k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(), k["leaf"].data_ptr(), pDp.data_ptr(),
                 pSp.data_ptr(), prs, crs, tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
                 topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
-                leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), int(prep.force_log),
+                leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), 0, _lib.ptr(prep.force_log_dev),
                 int(so.pi_iters), S, st)
-        if int(fl["counters"][2].item()) != 0:
-            raise RuntimeError("kb_flow_forward: a dataflow wait gave up (dependency counts inconsistent)")
+        note_flow_error(static, fl)
+        if check_errors:
+            check_flow_errors(static)
         roots = pi[wl["root_row_ids"]]
         out = (E, E_s1, E_s2, Ebar, roots, pi, pibar, row_max, pS, pD, pL, mc, clp)
         return out, {"dts_wave": dts}
@@ -395,6 +409,28 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
 # Bound on one dataflow wait (polls of ~0.1-0.2 us each): far above any legitimate wait, so a
 # broken dependency structure ends the launch with an error instead of hanging the GPU.
 FLOW_MAX_POLLS = 1 << 25
+
+
+def note_flow_error(static, fl) -> None:
+    """Fold a dataflow launch's error flag (set when a wait gave up) into the static's device-side
+    error word, without a host synchronisation; check_flow_errors reads it."""
+    err = getattr(static, "_flow_err", None)
+    if err is None or err.device != fl["counters"].device:
+        err = static._flow_err = torch.zeros((1,), device=fl["counters"].device, dtype=torch.int32)
+    err.bitwise_or_(fl["counters"][2:3])
+
+
+def check_flow_errors(static) -> None:
+    """Raise if a dataflow launch on ``static`` gave up a wait, or an E-adjoint solve whose check was
+    deferred did not converge, since the last check (one host synchronisation).  The backward
+    checks at its end; the forward at its end unless its caller defers the check to the backward
+    that follows (``check_errors=False``)."""
+    err = getattr(static, "_flow_err", None)
+    if err is not None and int(err.item()) != 0:
+        err.zero_()
+        static._pending_e_adjoint = []
+        raise RuntimeError("a dataflow wait gave up (dependency counts inconsistent); the results are invalid")
+    glue.check_pending_e_adjoint(static)
 
 
 def _flow_scratch(static, C, dev) -> dict:
@@ -441,13 +477,15 @@ def grad_accumulators_from(E, S, acc8) -> glue.GradAccumulators:
 
 
 @torch.no_grad()
-def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finish=True):
+def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finish=True, check_errors=True):
     """(forward intermediates) -> (grad_theta, grad_col); uses ``saved["dts_wave"]`` when the
     forward was run by this engine, otherwise recomputes the split reductions.
 
     ``slots`` (from :func:`new_grad_slots`) accumulates the column sums into caller-owned fp64
     accumulators, so several chunks of a family batch add into one set; with ``finish=False``
-    the E-adjoint / theta VJP is left to the caller and ``None`` is returned."""
+    the E-adjoint / theta VJP and the dataflow error check (:func:`check_flow_errors`) are left
+    to the caller and ``None`` is returned.  ``check_errors=False`` also leaves the check (one host
+    synchronisation at the end) to the caller, e.g. once after a loop of solves."""
     if not supported(static):
         return glue.implicit_grad(static, theta, col_weights, saved)
     so = static.solver_options
@@ -462,7 +500,7 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
     dev = Pi.device
     st = _lib.stream_handle(dev)
     E = saved["E"]
-    ucw = not glue.col_weights_are_uniform(col_weights)
+    ucw = not glue.col_weights_uniform_for(static, col_weights)
     if ucw:
         if not finish:
             raise ValueError("the fused engine needs uniform column weights")
@@ -502,18 +540,21 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
                 k["ebar"].data_ptr(), k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(),
                 k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
                 item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(), S, st)
-        if int(fl["counters"][2].item()) != 0:
-            raise RuntimeError("kb_flow_backward: a dataflow wait gave up (dependency counts inconsistent)")
+        note_flow_error(static, fl)
     else:
         _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr,
                          so, side_thr, k, pDp, pSp, prs, crs, clp, ucw, item_idx, leaf_state, tt, S, st)
     static._last_acc = acc
-    if not finish:
+    if not finish:  # the caller checks the dataflow error word (check_flow_errors) when it is done
         return None
     out8 = torch.empty((8, S), device=dev, dtype=torch.float32)
     _lib.call("kb_reduce_grad_slots", slots.data_ptr(), n_slots, S, out8.data_ptr(), st)
     g = grad_accumulators_from(E, S, out8)
-    return glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw)
+    grads = glue.e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, int(roots.numel()), ucw,
+                                         check=check_errors)
+    if check_errors:
+        check_flow_errors(static)  # after everything is enqueued: the host never holds the GPU up
+    return grads
 
 
 def _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr, so,

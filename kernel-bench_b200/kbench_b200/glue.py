@@ -35,6 +35,18 @@ def col_weights_are_uniform(col_weights) -> bool:
     return bool(torch.all(flat == flat[0]).item())
 
 
+def col_weights_uniform_for(static, col_weights) -> bool:
+    """col_weights_are_uniform, remembered on ``static`` for the same tensor object at the same
+    version (the check reads the device back -- a host synchronisation -- so a solver loop that
+    passes one col_weights tensor pays it once, not per call)."""
+    c = getattr(static, "_uniform_cols", None)
+    if c is not None and c[0] is col_weights and c[1] == col_weights._version:
+        return c[2]
+    r = col_weights_are_uniform(col_weights)
+    static._uniform_cols = (col_weights, col_weights._version, r)
+    return r
+
+
 def logsumexp2(x, dim, keepdim=False):
     m = x.max(dim=dim, keepdim=True).values
     ms = torch.where(m == NEG_INF, torch.zeros_like(m), m)
@@ -52,7 +64,7 @@ def nll_from_root_rows(root_rows, E):
 def solve_parameters(static, theta, col_weights):
     """(log_pS, log_pD, log_pL, max_coupling, col_log_probs, use_col_weights) as the reference's
     ``solve_e_pi`` derives them (``solver.py:25-44``)."""
-    use_col_weights = not col_weights_are_uniform(col_weights)
+    use_col_weights = not col_weights_uniform_for(static, col_weights)
     S = int(static.state_helpers["S"])
     if use_col_weights:
         pS, pD, pL, mc, clp = extract_parameters_weighted_cols(theta.detach(), col_weights.detach(),
@@ -384,18 +396,28 @@ def implicit_grad(static, theta, col_weights, saved, *, v_out=None, exact_accumu
 DEVICE_E_ADJOINT = True  # one shared E row: the whole solve in one launch (kb_e_adjoint_solve)
 
 
-def _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo):
+def _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo, check=True):
     """:func:`e_adjoint_and_theta_vjp` for one shared E row: the right-hand side, the BiCGSTAB
     solve and the E step's parameter VJP run in ONE kernel (``kb_e_adjoint_solve``); what is left
-    here is the VJP of the parameter extraction, with the same terms as the general path."""
-    from .kernels.e_step import _as_item_state_ad, e_adjoint_solve
+    here is the VJP of the parameter extraction, with the same terms as the general path.  With
+    ``check=False`` the solve's convergence status is kept on ``static._pending_e_adjoint`` for
+    :func:`check_pending_e_adjoint` instead of being read back now."""
+    from .kernels.e_step import _as_item_state_ad, e_adjoint_check, e_adjoint_solve
     so = static.solver_options
     sh = static.state_helpers
     S = int(sh["S"])
-    wE, gp = e_adjoint_solve(saved["E"], saved["log_pS"], saved["log_pD"], saved["log_pL"],
-                             saved["max_coupling"], saved["col_log_probs"], *topo, g.E, g.Ebar, g.E_s1, g.E_s2,
-                             n_fam=n_fam, max_iter=so.bicgstab_max_iter, tol=so.bicgstab_tol,
-                             breakdown_tol=so.bicgstab_breakdown_tol, use_col_weights=use_col_weights)
+    wE, gp, status, rel = e_adjoint_solve(saved["E"], saved["log_pS"], saved["log_pD"], saved["log_pL"],
+                                          saved["max_coupling"], saved["col_log_probs"], *topo, g.E, g.Ebar,
+                                          g.E_s1, g.E_s2, n_fam=n_fam, max_iter=so.bicgstab_max_iter,
+                                          tol=so.bicgstab_tol, breakdown_tol=so.bicgstab_breakdown_tol,
+                                          use_col_weights=use_col_weights, check=False)
+    if check:
+        e_adjoint_check(status, rel)
+    else:
+        pending = getattr(static, "_pending_e_adjoint", None)
+        if pending is None:
+            pending = static._pending_e_adjoint = []
+        pending.append((status, rel))
     static._last_e_adjoint = wE
     theta_req = theta.detach().requires_grad_(True)
     col_req = col_weights.detach().requires_grad_(True)
@@ -412,8 +434,21 @@ def _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_w
     return grad_theta, grad_col
 
 
-def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col_weights):
+def check_pending_e_adjoint(static) -> None:
+    """Read the convergence status of the E-adjoint solves run with ``check=False`` on ``static``
+    (one host synchronisation) and raise the reference's ``RuntimeError`` for one that failed."""
+    from .kernels.e_step import e_adjoint_check
+    pending = getattr(static, "_pending_e_adjoint", None)
+    if not pending:
+        return
+    static._pending_e_adjoint = []
+    for status, rel in pending:
+        e_adjoint_check(status, rel)
+
+
+def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col_weights, check=True):
     """The accumulated cotangents are kept on ``static._last_grad_acc`` for inspection.
+    ``check=False`` defers the one-launch solve's convergence check (:func:`check_pending_e_adjoint`).
 
     Reference ``_implicit_grad.py:373-475``: solve ``(I - J_E^T) w = q`` with BiCGSTAB, one E-step
     VJP kernel per matvec, then the theta / column-weight VJP through the parameter extraction."""
@@ -423,7 +458,7 @@ def e_adjoint_and_theta_vjp(static, theta, col_weights, saved, g, n_fam, use_col
     topo = (sh["node_parent"], sh["node_child1"], sh["node_child2"], int(sh["max_ancestor_depth"]))
     E_star = saved["E"]
     if DEVICE_E_ADJOINT and E_star.shape[0] == 1 and E_star.is_cuda:
-        return _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo)
+        return _e_adjoint_one_launch(static, theta, col_weights, saved, g, n_fam, use_col_weights, topo, check)
     E_req = E_star.detach().requires_grad_(True)
     with torch.enable_grad():
         E_from_E, Es1_from_E, Es2_from_E, Ebar_from_E = e_step_triton_autograd(

@@ -65,17 +65,19 @@ def make_static(captured: dict, device, *, engine: str = "fused") -> SimpleNames
     return static
 
 
-def run_forward(static, theta, col_weights):
+def run_forward(static, theta, col_weights, *, check_errors=True):
     """theta -> (loss, dict of forward intermediates).
 
     The fused engine also returns ``saved["dts_wave"]`` (the per-row split reductions), which its
-    backward reuses instead of recomputing them; every other key is the reference's."""
+    backward reuses instead of recomputing them; every other key is the reference's.
+    ``check_errors=False`` (a caller that runs ``run_backward`` next) leaves the engine's dataflow
+    error check to the end of that backward, so the host does not wait for the forward."""
     from .glue import nll_from_root_rows
     extras = {}
     with torch.no_grad():
         if getattr(static, "engine", "fused") == "fused":
             from . import engine
-            out, extras = engine.forward(static, theta, col_weights)
+            out, extras = engine.forward(static, theta, col_weights, check_errors=check_errors)
         else:
             from . import glue
             out = glue.solve_e_pi(static, theta, col_weights)
@@ -85,10 +87,20 @@ def run_forward(static, theta, col_weights):
     return loss, saved
 
 
-def run_backward(static, theta, col_weights, saved: dict):
-    """(forward intermediates) -> (grad_theta, grad_col)."""
+def run_backward(static, theta, col_weights, saved: dict, *, check_errors=True):
+    """(forward intermediates) -> (grad_theta, grad_col).  ``check_errors=False`` (a solver loop
+    that calls :func:`check_errors` itself, e.g. once after the loop) skips the engine's dataflow
+    error check, the one host synchronisation of a solve."""
     if getattr(static, "engine", "fused") == "fused":
         from . import engine
-        return engine.backward(static, theta, col_weights, saved)
+        return engine.backward(static, theta, col_weights, saved, check_errors=check_errors)
     from . import glue
     return glue.implicit_grad(static, theta, col_weights, saved)
+
+
+def check_errors(static) -> None:
+    """Raise if a dataflow launch of the fused engine on ``static`` gave up a wait since the last
+    check (see ``run_forward`` / ``run_backward``'s ``check_errors``); one host synchronisation."""
+    if getattr(static, "engine", "fused") == "fused":
+        from . import engine
+        engine.check_flow_errors(static)

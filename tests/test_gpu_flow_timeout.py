@@ -1,6 +1,7 @@
 """Failure detection of the dataflow schedule, without a GPU fault: a dependency count that is one
 too high leaves a row that is never released; every wait on it must give up after its poll bound,
-the launch must end with the error flag set (the engine raises), and the device must stay usable
+the launch must end with the error flag set (the engine raises: at the end of the forward, or of
+the backward that follows when the forward's check is deferred), and the device must stay usable
 (a normal forward right after matches the level schedule bitwise)."""
 
 import pytest
@@ -23,6 +24,10 @@ def test_unreleased_row_times_out_and_reports(cuda, monkeypatch):
     monkeypatch.setattr(engine, "FLOW_MAX_POLLS", 2000)
     with pytest.raises(RuntimeError, match="dataflow wait gave up"):
         runtime.run_forward(static, theta, col)
+    # a caller that defers the forward's check to the backward that follows gets it there
+    with pytest.raises(RuntimeError, match="dataflow wait gave up"):
+        _, saved = runtime.run_forward(static, theta, col, check_errors=False)
+        runtime.run_backward(static, theta, col, saved)
     plan.dep0.copy_(good)
     monkeypatch.setattr(engine, "FLOW_MAX_POLLS", 1 << 25)
     loss_f, saved_f = runtime.run_forward(static, theta, col)
