@@ -326,8 +326,10 @@ int kb_level_forward(const int* rows, const long long* split_ptr, int n_rows, co
  * (head, tail, error flag; error != 0 after the launch means a wait gave up after max_polls
  * polls: results are then invalid).  Pi / Pibar child rows are read from pi / pibar (in place).
  * force_log_flag (device int, may be NULL): a nonzero value forces the log-space iteration like
- * force_log_space, decided on the device (no host round trip).  Other arguments as
- * kb_level_forward's tour path. */
+ * force_log_space, decided on the device (no host round trip).  start_order (int32 [C], may be
+ * NULL): a fixed start order of all rows, every row after its child rows; CTAs take rows in that
+ * order, each waiting (bounded) until its children are done, instead of taking rows as they
+ * become ready.  Other arguments as kb_level_forward's tour path. */
 int kb_flow_forward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
                     const float* lsp, const int* dep0, const int* ready0, int n_ready0, const long long* par_ptr,
                     const int* par_idx, int* queue, int* remaining, unsigned* counters, long long max_polls,
@@ -338,8 +340,8 @@ int kb_flow_forward(int C, const long long* row_split_ptr, const long long* sl, 
                     const int* node_parent, const int* node_child1, const int* node_child2,
                     const int* node_subtree_start, const int* node_subtree_end, const int* jumps, int K,
                     const long long* item_idx, const int* leaf_state, const unsigned* tour_tables,
-                    const float* tour_consts, int force_log_space, const int* force_log_flag, int pi_iters, int S,
-                    void* stream);
+                    const float* tour_consts, int force_log_space, const int* force_log_flag, const int* start_order,
+                    int pi_iters, int S, void* stream);
 
 /* The tour kernel's per-column constants, interleaved and zero-padded to NTV = kb_tour_layout(S):
  * out4 [G, NTV, 4] = (2^dl + 2^ebar, 2^(mc+e), 2^sl1, 2^sl2) from the [G,S] constant rows. */

@@ -1095,6 +1095,10 @@ struct Flow {
   int C;
   long long max_polls;
   int n_items;             // C * groups
+  // 1: the queue is pre-filled with every item in a fixed start order (dependencies first); a CTA
+  // takes the next slot and waits until the item's remaining count reaches zero; finishing only
+  // decrements the dependents' counts
+  int static_order;
 };
 
 // Per-CTA state of the dataflow loop (shared memory; the poller sets next = -1 before the loop).
@@ -1128,7 +1132,18 @@ __device__ __forceinline__ int flow_next_row(const Flow& f, FlowSlot* st) {
         __nanosleep(128);
         row = *q;
       }
-      __threadfence();  // the row's children, written before it was queued, are visible
+      if (f.static_order && row >= 0) {  // the slot holds its item from the start: wait until it is ready
+        const volatile int* rem = f.remaining + row;
+        while (*rem > 0) {
+          if (++polls > f.max_polls || *(volatile int*)f.error) {
+            atomicExch(f.error, 1);
+            row = -2;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      __threadfence();  // the row's children, written before it was queued (released), are visible
     }
     st->row = row;
   }
@@ -1149,7 +1164,7 @@ __device__ __forceinline__ void flow_finish_row(const Flow& f, int row, FlowSlot
     const int r = row - grp * f.C;
     for (long long j = f.par_ptr[r] + threadIdx.x; j < f.par_ptr[r + 1]; j += 32) {
       const int p = grp * f.C + f.par_idx[j];
-      if (atomicSub(f.remaining + p, 1) == 1) {
+      if (atomicSub(f.remaining + p, 1) == 1 && !f.static_order) {
         const unsigned slot = atomicAdd(f.tail, 1u);
         atomicExch(f.queue + slot, p);
       }
@@ -2695,7 +2710,8 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
                                const int* node_child1, const int* node_child2, const int* node_subtree_start,
                                const int* node_subtree_end, const int* jumps, int K, const long long* item_idx,
                                const int* leaf_state, const unsigned* tour_tables, const float* tour_consts,
-                               int force_log_space, const int* force_log_flag, int pi_iters, int S, void* stream) {
+                               int force_log_space, const int* force_log_flag, const int* start_order, int pi_iters, int S,
+                               void* stream) {
   if (S <= 0 || C < 0 || K < 0 || pi_iters < 2 || n_ready0 < 0 || n_ready0 > C || max_polls < 1) return KB_ERR_ARG;
   if (tour_tables == nullptr || tour_consts == nullptr || dts_save == nullptr || counters == nullptr) return KB_ERR_ARG;
   int nt, vf;
@@ -2721,7 +2737,11 @@ extern "C" int kb_flow_forward(int C, const long long* row_split_ptr, const long
   a4.k4_rows = const_row_stride == 0 ? 0 : ntv;
   Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), par_ptr, par_idx,
          row_split_ptr, C, max_polls, C};
-  flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
+  f.static_order = start_order != nullptr;
+  if (start_order)  // every row queued in the given order from the start
+    flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, start_order, C);
+  else
+    flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
   const size_t smem = (size_t)(8 * (ntv + 4) + 96) * sizeof(float);
   int dev = 0, n_sm = 0, per_sm = 0;

@@ -192,6 +192,48 @@ def build_plan_device(static) -> LevelPlan:
     )
 
 
+# Relative cost of one split against the rest of a forward row (the split reduction against the
+# pi_iters iterations and the final scans; measured on config 3: ~5.3k and ~80k SM cycles).
+FWD_SPLIT_COST = 0.066
+
+
+def forward_start_order(plan: LevelPlan) -> torch.Tensor:
+    """A fixed start order for the dataflow forward (int32 [C], device): rows by decreasing
+    "bottom level" -- the largest summed cost, a row's own included, of a chain from it to a root
+    through its parents, with a row's cost 1 + FWD_SPLIT_COST x its splits.  A child's bottom
+    level exceeds its parents', so every row comes after its children; and the rows on the longest
+    chains to the end of the pass start first (list scheduling by critical path), which shortens
+    the pass's tail where few rows are ready.  Computed once per plan on the host."""
+    cached = getattr(plan, "_fwd_order", None)
+    if cached is not None:
+        return cached
+    rsp = plan.row_split_ptr.cpu().numpy()
+    C = rsp.shape[0] - 1
+    cost = 1.0 + FWD_SPLIT_COST * np.diff(rsp).astype(np.float64)
+    rows = plan.rows.cpu().numpy().astype(np.int64)
+    lp = np.asarray(plan.level_ptr, dtype=np.int64)
+    level_of = np.empty(C, dtype=np.int64)
+    for L in range(plan.n_levels):
+        level_of[rows[lp[L]:lp[L + 1]]] = L
+    par_ptr = plan.par_ptr.cpu().numpy()
+    par_idx = plan.par_idx.cpu().numpy().astype(np.int64)
+    child_of = np.repeat(np.arange(C, dtype=np.int64), np.diff(par_ptr))
+    by_level = np.argsort(level_of[child_of], kind="stable")
+    pl = level_of[child_of][by_level]
+    bounds = np.searchsorted(pl, np.arange(plan.n_levels + 1))
+    bl = cost.copy()
+    mx = np.zeros(C, dtype=np.float64)
+    for L in range(plan.n_levels - 1, -1, -1):  # parents sit on higher levels: final before their children
+        sel = by_level[bounds[L]:bounds[L + 1]]
+        if sel.shape[0]:
+            np.maximum.at(mx, child_of[sel], bl[par_idx[sel]])
+        r = rows[lp[L]:lp[L + 1]]
+        bl[r] = cost[r] + mx[r]
+    order = np.argsort(-bl, kind="stable").astype(np.int32)
+    plan._fwd_order = torch.from_numpy(order).to(plan.rows.device)
+    return plan._fwd_order
+
+
 def supported(static) -> bool:
     """The fused engine's layouts: one shared item row (statewise, not itemwise) and rows of at
     most 4,095 columns (the tour kernels' 4,096-column padded width); anything else runs on the
@@ -379,6 +421,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                 pSp.data_ptr(), prs, crs, tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
                 topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
                 leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), 0, _lib.ptr(prep.force_log_dev),
+                _lib.ptr(forward_start_order(plan) if getattr(static, "_forward_static_order", True) else None),
                 int(so.pi_iters), S, st)
         note_flow_error(static, fl)
         if check_errors:

@@ -67,3 +67,25 @@ def test_linear_range_decision():
     sl = torch.full((1, S), -3.0)
     sl[0, 2] = float("-inf")
     assert engine.linear_range_ok(dict(base, sl1=sl))
+
+
+def test_forward_start_order_is_topological():
+    """The dataflow forward's fixed start order puts every row after its child rows (the condition
+    under which CTAs taking rows in that order cannot wait on each other forever) and starts the
+    rows of the longest chains first."""
+    from types import SimpleNamespace
+    import numpy as np
+    from kbench_b200 import engine, gen
+    cap = gen.generate(2)
+    plan = engine.build_plan(SimpleNamespace(wave_layout=cap["static"]["wave_layout"]))
+    order = engine.forward_start_order(plan).numpy()
+    C = int(cap["meta"]["C"])
+    assert sorted(order.tolist()) == list(range(C))
+    pos = np.empty(C, dtype=np.int64)
+    pos[order] = np.arange(C)
+    cp, ci = plan.child_ptr.numpy(), plan.child_idx.numpy()
+    child_of = np.repeat(np.arange(C), np.diff(cp))
+    assert (pos[ci] < pos[child_of]).all()
+    # the row started first has no children; the last one is a root row (no parents)
+    assert np.diff(cp)[order[0]] == 0
+    assert np.diff(plan.par_ptr.numpy())[order[-1]] == 0
