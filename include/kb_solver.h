@@ -400,11 +400,26 @@ int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl,
                      const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
                      long long param_row_stride, long long const_row_stride, const float* col_log_probs,
                      int use_col_weights, const long long* item_idx, const int* leaf_state,
-                     const unsigned* packed_padded, int S, void* stream);
+                     const unsigned* packed_padded, const int* start_order, int S, void* stream);
 
 /* Number of backward CTAs that are resident at once on this device for S columns (SMs x CTAs
  * per SM): the slot count to give kb_level_backward / kb_flow_backward (host only). */
 int kb_backward_ctas(int S, int* n_ctas);
+
+/* Host query (no device work): CTAs of kb_flow_forward's persistent grid for rows of S columns
+ * (SMs x resident CTAs per SM of its tour kernel). */
+int kb_forward_ctas(int S, int* n_ctas);
+
+/* Host-only (no device work; all pointers are HOST memory): the start order of a critical-path
+ * list schedule of n rows on n_workers identical workers.  pred_ptr [n+1] / pred_idx: the rows
+ * each row waits for; succ_ptr [n+1] / succ_idx: the rows waiting on each row (the same edges
+ * reversed); cost [n] > 0: a row's modelled duration.  A ready row with the largest level (its cost
+ * plus the largest level of its successors) starts first.  order_out [n]: rows in start order --
+ * every row after its predecessors (the start_order of kb_flow_forward / kb_flow_backward);
+ * makespan_out (may be NULL): the schedule's modelled length.  KB_ERR_ARG on a cycle or edges that
+ * do not match the counts. */
+int kb_list_schedule(int n, const long long* pred_ptr, const int* pred_idx, const long long* succ_ptr,
+                     const int* succ_idx, const double* cost, int n_workers, int* order_out, double* makespan_out);
 
 /* Fixed-order sum of kb_level_backward's fp64 slots -> out8 [8,S] fp32: the cotangents of
  * log_pD, log_pS, max_coupling, E, Ebar, E_s1, E_s2 and col_log_probs (in that order). */

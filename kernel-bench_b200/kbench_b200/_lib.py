@@ -32,7 +32,7 @@ _lib = None
 # of this library's kernels ran inside a timed region.
 LAUNCHES: dict = {}
 _NO_LAUNCH = {"kb_abi_version", "kb_tour_layout", "kb_backward_layout", "kb_backward_ctas", "kb_build_workspace",
-              "kb_build_emit_scratch", "kb_plan_workspace"}
+              "kb_build_emit_scratch", "kb_plan_workspace", "kb_forward_ctas", "kb_list_schedule"}
 
 
 def parse_header(text: str | None = None) -> dict[str, list]:

@@ -21,7 +21,7 @@ REPO = PKG.parent.parent
 CSRC = PKG / "csrc"
 INCLUDE = REPO / "include"
 LIB = PKG / "libkb_solver.so"
-SOURCES = ["kb_misc.cu", "kb_estep.cu", "kb_params.cu", "kb_dts.cu", "kb_wave_fwd.cu", "kb_wave_bwd.cu", "kb_engine.cu", "kb_tangent.cu", "kb_hvp.cu", "kb_builder.cu"]
+SOURCES = ["kb_misc.cu", "kb_estep.cu", "kb_params.cu", "kb_dts.cu", "kb_wave_fwd.cu", "kb_wave_bwd.cu", "kb_engine.cu", "kb_tangent.cu", "kb_hvp.cu", "kb_builder.cu", "kb_sched.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

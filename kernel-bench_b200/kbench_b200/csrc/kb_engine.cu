@@ -2783,7 +2783,8 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
                                 const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
                                 const float* log_pS, long long param_row_stride, long long const_row_stride,
                                 const float* col_log_probs, int use_col_weights, const long long* item_idx,
-                                const int* leaf_state, const unsigned* packed_padded, int S, void* stream) {
+                                const int* leaf_state, const unsigned* packed_padded, const int* start_order, int S,
+                                void* stream) {
   if (S <= 0 || C < 0 || neumann_terms < 0 || n_slots <= 0 || n_ready0 < 0 || n_ready0 > C || max_polls < 1 ||
       counters == nullptr)
     return KB_ERR_ARG;
@@ -2801,7 +2802,11 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   a.n_rows = C;
   Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), child_ptr, child_idx,
          row_split_ptr, C, max_polls, C};
-  flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
+  f.static_order = start_order != nullptr;
+  if (start_order)  // every row queued in the given order from the start
+    flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, start_order, C);
+  else
+    flow_init_kernel<<<(C + 255) / 256, 256, 0, st>>>(f, dep0, ready0, n_ready0);
   if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
   int bd;
   const int vpt = bwd_width(S, bd);
@@ -2891,6 +2896,27 @@ extern "C" int kb_flow_tangent(int C, const long long* row_split_ptr, const long
   }
 #undef KB_FT_CASE
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_forward_ctas(int S, int* n_ctas) {
+  if (S <= 0 || n_ctas == nullptr) return KB_ERR_ARG;
+  int nt, vf;
+  const int ntv = tour_layout(S, nt, vf);
+  if (ntv == 0) return KB_ERR_SIZE;
+  const size_t smem = (size_t)(8 * (ntv + 4) + 96) * sizeof(float);
+  int dev = 0, n_sm = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KB_ERR_LAUNCH;
+  const void* fn = vf == 2 ? (const void*)flow_forward_kernel<2>
+                 : vf == 4 ? (const void*)flow_forward_kernel<4>
+                           : (const void*)flow_forward_kernel<8>;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+    return KB_ERR_LAUNCH;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, nt, smem) != cudaSuccess || per_sm < 1)
+    return KB_ERR_LAUNCH;
+  *n_ctas = n_sm * per_sm;
+  return KB_OK;
 }
 
 extern "C" int kb_backward_ctas(int S, int* n_ctas) {

@@ -192,46 +192,47 @@ def build_plan_device(static) -> LevelPlan:
     )
 
 
-# Relative cost of one split against the rest of a forward row (the split reduction against the
-# pi_iters iterations and the final scans; measured on config 3: ~5.3k and ~80k SM cycles).
+# Relative cost of one split against the rest of a row (measured on config 3: forward ~5.3k of
+# ~80k SM cycles per row besides its splits; backward ~17k of ~100k).
 FWD_SPLIT_COST = 0.066
+BWD_SPLIT_COST = 0.17
 
 
-def forward_start_order(plan: LevelPlan) -> torch.Tensor:
-    """A fixed start order for the dataflow forward (int32 [C], device): rows by decreasing
-    "bottom level" -- the largest summed cost, a row's own included, of a chain from it to a root
-    through its parents, with a row's cost 1 + FWD_SPLIT_COST x its splits.  A child's bottom
-    level exceeds its parents', so every row comes after its children; and the rows on the longest
-    chains to the end of the pass start first (list scheduling by critical path), which shortens
-    the pass's tail where few rows are ready.  Computed once per plan on the host."""
-    cached = getattr(plan, "_fwd_order", None)
+def start_order(plan: LevelPlan, direction: str, n_workers: int) -> torch.Tensor:
+    """A fixed start order for a dataflow pass (int32 [C], device): the order in which rows START
+    in a critical-path list schedule of the pass on ``n_workers`` CTAs (``kb_list_schedule``, host
+    code), with a row's cost 1 + (FWD|BWD)_SPLIT_COST x its splits.  Every row comes after the rows
+    it waits for -- its children in the forward, its parents in the backward -- and the rows of the
+    longest remaining chains start first, which shortens the pass's tail (forward) or ramp
+    (backward) where few rows are ready.  Cached on the plan."""
+    key = f"_order_{direction}_{n_workers}"
+    cached = getattr(plan, key, None)
     if cached is not None:
         return cached
     rsp = plan.row_split_ptr.cpu().numpy()
     C = rsp.shape[0] - 1
-    cost = 1.0 + FWD_SPLIT_COST * np.diff(rsp).astype(np.float64)
-    rows = plan.rows.cpu().numpy().astype(np.int64)
-    lp = np.asarray(plan.level_ptr, dtype=np.int64)
-    level_of = np.empty(C, dtype=np.int64)
-    for L in range(plan.n_levels):
-        level_of[rows[lp[L]:lp[L + 1]]] = L
-    par_ptr = plan.par_ptr.cpu().numpy()
-    par_idx = plan.par_idx.cpu().numpy().astype(np.int64)
-    child_of = np.repeat(np.arange(C, dtype=np.int64), np.diff(par_ptr))
-    by_level = np.argsort(level_of[child_of], kind="stable")
-    pl = level_of[child_of][by_level]
-    bounds = np.searchsorted(pl, np.arange(plan.n_levels + 1))
-    bl = cost.copy()
-    mx = np.zeros(C, dtype=np.float64)
-    for L in range(plan.n_levels - 1, -1, -1):  # parents sit on higher levels: final before their children
-        sel = by_level[bounds[L]:bounds[L + 1]]
-        if sel.shape[0]:
-            np.maximum.at(mx, child_of[sel], bl[par_idx[sel]])
-        r = rows[lp[L]:lp[L + 1]]
-        bl[r] = cost[r] + mx[r]
-    order = np.argsort(-bl, kind="stable").astype(np.int32)
-    plan._fwd_order = torch.from_numpy(order).to(plan.rows.device)
-    return plan._fwd_order
+    w = FWD_SPLIT_COST if direction == "forward" else BWD_SPLIT_COST
+    cost = np.ascontiguousarray(1.0 + w * np.diff(rsp).astype(np.float64))
+    cp, ci = plan.child_ptr.cpu().numpy(), plan.child_idx.cpu().numpy()
+    pp, pi = plan.par_ptr.cpu().numpy(), plan.par_idx.cpu().numpy()
+    (pred_ptr, pred_idx), (succ_ptr, succ_idx) = ((cp, ci), (pp, pi)) if direction == "forward" else ((pp, pi), (cp, ci))
+    arrs = [np.ascontiguousarray(a) for a in (pred_ptr.astype(np.int64), pred_idx.astype(np.int32),
+                                              succ_ptr.astype(np.int64), succ_idx.astype(np.int32))]
+    order = np.empty(C, dtype=np.int32)
+    span = np.zeros(1, dtype=np.float64)
+    _lib.call("kb_list_schedule", C, *(a.ctypes.data for a in arrs), cost.ctypes.data, int(n_workers),
+              order.ctypes.data, span.ctypes.data)
+    out = torch.from_numpy(order).to(plan.rows.device)
+    setattr(plan, key, out)
+    return out
+
+
+def _forward_ctas(S) -> int:
+    """CTAs of the dataflow forward's persistent grid for S columns on the current device."""
+    import ctypes
+    n = ctypes.c_int(0)
+    _lib.call("kb_forward_ctas", S, ctypes.byref(n))
+    return int(n.value)
 
 
 def supported(static) -> bool:
@@ -421,7 +422,8 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                 pSp.data_ptr(), prs, crs, tt.parent.data_ptr(), tt.child1.data_ptr(), tt.child2.data_ptr(),
                 topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
                 leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), 0, _lib.ptr(prep.force_log_dev),
-                _lib.ptr(forward_start_order(plan) if getattr(static, "_forward_static_order", True) else None),
+                _lib.ptr(start_order(plan, "forward", _forward_ctas(S))
+                         if getattr(static, "_forward_static_order", True) else None),
                 int(so.pi_iters), S, st)
         note_flow_error(static, fl)
         if check_errors:
@@ -582,7 +584,9 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
                 int(side_thr > 0.0), int(so.neumann_terms), k["mc"].data_ptr(), k["dl"].data_ptr(),
                 k["ebar"].data_ptr(), k["e"].data_ptr(), k["sl1"].data_ptr(), k["sl2"].data_ptr(),
                 k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
-                item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(), S, st)
+                item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
+                _lib.ptr(start_order(plan, "backward", min(n_slots, C))
+                         if getattr(static, "_backward_static_order", True) else None), S, st)
         note_flow_error(static, fl)
     else:
         _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr,

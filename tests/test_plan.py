@@ -69,23 +69,38 @@ def test_linear_range_decision():
     assert engine.linear_range_ok(dict(base, sl1=sl))
 
 
-def test_forward_start_order_is_topological():
-    """The dataflow forward's fixed start order puts every row after its child rows (the condition
-    under which CTAs taking rows in that order cannot wait on each other forever) and starts the
-    rows of the longest chains first."""
+@pytest.mark.parametrize("direction", ["forward", "backward"])
+def test_start_order_is_topological(direction):
+    """The dataflow passes' fixed start orders (kb_list_schedule, host code in the library) put
+    every row after the rows it waits for -- children in the forward, parents in the backward: the
+    condition under which CTAs taking rows in that order cannot wait on each other forever."""
     from types import SimpleNamespace
     import numpy as np
     from kbench_b200 import engine, gen
     cap = gen.generate(2)
     plan = engine.build_plan(SimpleNamespace(wave_layout=cap["static"]["wave_layout"]))
-    order = engine.forward_start_order(plan).numpy()
+    order = engine.start_order(plan, direction, 148).numpy()
     C = int(cap["meta"]["C"])
     assert sorted(order.tolist()) == list(range(C))
     pos = np.empty(C, dtype=np.int64)
     pos[order] = np.arange(C)
     cp, ci = plan.child_ptr.numpy(), plan.child_idx.numpy()
-    child_of = np.repeat(np.arange(C), np.diff(cp))
-    assert (pos[ci] < pos[child_of]).all()
-    # the row started first has no children; the last one is a root row (no parents)
-    assert np.diff(cp)[order[0]] == 0
-    assert np.diff(plan.par_ptr.numpy())[order[-1]] == 0
+    parent_of_pair = np.repeat(np.arange(C), np.diff(cp))  # pairs (row, child)
+    if direction == "forward":
+        assert (pos[ci] < pos[parent_of_pair]).all()
+        assert np.diff(cp)[order[0]] == 0  # the first row started has no children
+    else:
+        assert (pos[parent_of_pair] < pos[ci]).all()
+        assert np.diff(plan.par_ptr.numpy())[order[0]] == 0  # ... no parents
+
+
+def test_list_schedule_rejects_a_cycle():
+    import numpy as np
+    from kbench_b200 import _lib
+    ptr = np.array([0, 1, 2], dtype=np.int64)
+    idx = np.array([1, 0], dtype=np.int32)  # 0 waits for 1 and 1 for 0
+    cost = np.ones(2)
+    order = np.zeros(2, dtype=np.int32)
+    with pytest.raises(ValueError):
+        _lib.call("kb_list_schedule", 2, ptr.ctypes.data, idx.ctypes.data, ptr.ctypes.data, idx.ctypes.data,
+                  cost.ctypes.data, 4, order.ctypes.data, None)
