@@ -227,6 +227,13 @@ def start_order(plan: LevelPlan, direction: str, n_workers: int) -> torch.Tensor
     return out
 
 
+def _one_family(static) -> bool:
+    """Whether the static holds one family: its chains of dependent rows are what a pass's tail
+    and ramp are made of, and the fixed start order pays; a batch of families keeps the SMs busy
+    with independent chains in any order (and a multi-million-row schedule costs host time)."""
+    return int(static.wave_layout["root_row_ids"].numel()) == 1
+
+
 def _forward_ctas(S) -> int:
     """CTAs of the dataflow forward's persistent grid for S columns on the current device."""
     import ctypes
@@ -423,7 +430,7 @@ def forward(static, theta, col_weights, *, pi_residual_out=None, prep: Prep | No
                 topo.pre.data_ptr(), topo.pre_end.data_ptr(), tt.jumps.data_ptr(), tt.K, item_idx.data_ptr(),
                 leaf_state.data_ptr(), tt.tour.data_ptr(), prep.k4.data_ptr(), 0, _lib.ptr(prep.force_log_dev),
                 _lib.ptr(start_order(plan, "forward", _forward_ctas(S))
-                         if getattr(static, "_forward_static_order", True) else None),
+                         if getattr(static, "_forward_static_order", _one_family(static)) else None),
                 int(so.pi_iters), S, st)
         note_flow_error(static, fl)
         if check_errors:
@@ -586,7 +593,7 @@ def backward(static, theta, col_weights, saved, *, v_out=None, slots=None, finis
                 k["leaf"].data_ptr(), pDp.data_ptr(), pSp.data_ptr(), prs, crs, clp.data_ptr(), int(ucw),
                 item_idx.data_ptr(), leaf_state.data_ptr(), tt.packed_pad.data_ptr(),
                 _lib.ptr(start_order(plan, "backward", min(n_slots, C))
-                         if getattr(static, "_backward_static_order", True) else None), S, st)
+                         if getattr(static, "_backward_static_order", _one_family(static)) else None), S, st)
         note_flow_error(static, fl)
     else:
         _backward_levels(static, plan, rows_ptr, sp_ptr, Pi, Pibar, row_max, dts, acc, v_out, slots, n_slots, thr,
