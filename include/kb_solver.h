@@ -150,6 +150,16 @@ int kb_e_step_backward_so(const float* E, const float* E_new, const float* E_s1,
                           float* d_grad_pD, float* d_grad_pL, float* d_grad_mc, float* d_grad_col, int S, int G,
                           int use_col_weights, void* stream);
 
+/* Column sums of one wave's six parameter buckets in the exact-Hessian HVP (the glue of
+ * newton/hvp_exact.py:264-281 that sums the contraction's and the tangent adjoint's aw buckets):
+ * c_aw [6,W,S] (aw0, aw1, aw2, aw345, aw3, aw4, from kb_wave_backward_so) plus l_aw* [W,S] (the
+ * same buckets from kb_wave_adjoint), added into [S] accumulators: d_pD += aw0, d_pS += aw345,
+ * d_E += aw0 + aw2, d_Ebar += aw1, d_Es1 += aw4, d_Es2 += aw3, d_mc += aw2 (fixed summation order). */
+int kb_hvp_aw_accumulate(const float* c_aw, const float* l_aw0, const float* l_aw1, const float* l_aw2,
+                         const float* l_aw345, const float* l_aw3, const float* l_aw4, int W, int S, float* d_pD,
+                         float* d_pS, float* d_E, float* d_Ebar, float* d_Es1, float* d_Es2, float* d_mc,
+                         void* stream);
+
 /* ---- parameter extraction (kbench/core/parameters/extract_parameters.py) ---------------- */
 
 /* Replaces col_valid_log_normalizer (extract_parameters.py:41-65): norm_out[s] =

@@ -514,3 +514,63 @@ extern "C" int kb_e_step_backward_so(const float* E, const float* E_new, const f
   e_step_so_kernel<<<1, so_block(S), smem, (cudaStream_t)stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }
+
+// Column sums of one wave's six parameter buckets (aw0, aw1, aw2, aw345, aw3, aw4 [W,S] each) from
+// the second-order contraction (c_aw: one [6,W,S] buffer) plus the tangent adjoint's (l.p[0..5]),
+// added into the tangent cotangent accumulators: d_pD += aw0, d_pS += aw345, d_E += aw0 + aw2,
+// d_Ebar += aw1, d_Es1 += aw4, d_Es2 += aw3, d_mc += aw2.  Block (32, 32): 32 columns per block,
+// the rows strided over 32 threads, then summed in a fixed order (deterministic).  The pointers
+// travel by value in the launch (a CUDA graph replays them as they were).
+struct AwBuckets {
+  const float* p[6];
+};
+
+__global__ void __launch_bounds__(1024) aw_accumulate_kernel(const float* __restrict__ c_aw, AwBuckets l, int W,
+                                                             int S, float* d_pD, float* d_pS, float* d_E,
+                                                             float* d_Ebar, float* d_Es1, float* d_Es2,
+                                                             float* d_mc) {
+  __shared__ float part[6][32][33];
+  const int lane = threadIdx.x, ty = threadIdx.y;
+  const int s = blockIdx.x * 32 + lane;
+  float acc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (s < S) {
+    const size_t WS = (size_t)W * S;
+    for (int w = ty; w < W; w += 32) {
+      const size_t o = (size_t)w * S + s;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) acc[k] += c_aw[k * WS + o] + l.p[k][o];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 6; ++k) part[k][ty][lane] = acc[k];
+  __syncthreads();
+  if (ty == 0 && s < S) {
+    float tot[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      float t = 0.f;
+      for (int y = 0; y < 32; ++y) t += part[k][y][lane];
+      tot[k] = t;
+    }
+    d_pD[s] += tot[0];
+    d_pS[s] += tot[3];
+    d_E[s] += tot[0] + tot[2];
+    d_Ebar[s] += tot[1];
+    d_Es1[s] += tot[5];
+    d_Es2[s] += tot[4];
+    d_mc[s] += tot[2];
+  }
+}
+
+extern "C" int kb_hvp_aw_accumulate(const float* c_aw, const float* l_aw0, const float* l_aw1, const float* l_aw2,
+                                    const float* l_aw345, const float* l_aw3, const float* l_aw4, int W, int S,
+                                    float* d_pD, float* d_pS, float* d_E, float* d_Ebar, float* d_Es1, float* d_Es2,
+                                    float* d_mc, void* stream) {
+  if (W < 0 || S <= 0 || !c_aw || !l_aw0 || !l_aw1 || !l_aw2 || !l_aw345 || !l_aw3 || !l_aw4) return KB_ERR_ARG;
+  if (!d_pD || !d_pS || !d_E || !d_Ebar || !d_Es1 || !d_Es2 || !d_mc) return KB_ERR_ARG;
+  if (W == 0) return KB_OK;
+  AwBuckets l{{l_aw0, l_aw1, l_aw2, l_aw345, l_aw3, l_aw4}};
+  aw_accumulate_kernel<<<(S + 31) / 32, dim3(32, 32), 0, (cudaStream_t)stream>>>(c_aw, l, W, S, d_pD, d_pS, d_E,
+                                                                               d_Ebar, d_Es1, d_Es2, d_mc);
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}

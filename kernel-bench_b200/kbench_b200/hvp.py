@@ -148,9 +148,10 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
         q = _safe_exp2_ratio(root_Pi, logsumexp2(root_Pi, dim=-1, keepdim=True))
         d_rhs = torch.zeros((C, S), device=theta.device, dtype=torch.float32)
         d_rhs.index_copy_(0, root_ids, (-LN2 * q * (t_root - (q * t_root).sum(dim=-1, keepdim=True))).float())
-        d_gpD, d_gpS = torch.zeros_like(acc.pD), torch.zeros_like(acc.pS)
-        d_gE, d_gEbar, d_gEs1, d_gEs2 = (torch.zeros_like(E_star) for _ in range(4))
-        d_gmc = torch.zeros_like(acc.mt)
+        zf = dict(device=theta.device, dtype=torch.float32)  # contiguous: kb_hvp_aw_accumulate adds into row 0
+        d_gpD, d_gpS = torch.zeros(acc.pD.shape, **zf), torch.zeros(acc.pS.shape, **zf)
+        d_gE, d_gEbar, d_gEs1, d_gEs2 = (torch.zeros(E_star.shape, **zf) for _ in range(4))
+        d_gmc = torch.zeros(acc.mt.shape, **zf)
         d_gcol = torch.zeros((S,), device=theta.device, dtype=torch.float32)
         for wave in cache["waves"]:  # reverse wave order
             ws, W, meta = wave["ws"], wave["W"], wave["meta"]
@@ -178,15 +179,11 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
                 node_parent=parent, max_ancestor_depth=mad, pibar_row_max=prm, item_idx=item_idx,
                 item_indexed_consts=True, **lv, grad_col_log_probs=d_gcol, use_col_weights=False,
                 self_loop_solver=so.self_loop_solver)
-            # column sums of aw0, aw1, aw2, aw345, aw3, aw4 (contraction + solve parts) in one pass
-            aw = (torch.stack(c_aw) + torch.stack(l_aw)).sum(dim=1)
-            d_gpD[0] += aw[0]
-            d_gpS[0] += aw[3]
-            d_gE[0] += aw[0] + aw[2]
-            d_gEbar[0] += aw[1]
-            d_gEs1[0] += aw[5]
-            d_gEs2[0] += aw[4]
-            d_gmc[0] += aw[2]
+            # column sums of aw0, aw1, aw2, aw345, aw3, aw4 (contraction + solve parts) into the
+            # accumulators (hvp_exact.py:264-281), one launch: c_aw are views of one [6,W,S] buffer
+            _lib.call("kb_hvp_aw_accumulate", c_aw[0].data_ptr(), *(t.data_ptr() for t in l_aw), W, S,
+                      d_gpD.data_ptr(), d_gpS.data_ptr(), d_gE.data_ptr(), d_gEbar.data_ptr(), d_gEs1.data_ptr(),
+                      d_gEs2.data_ptr(), d_gmc.data_ptr(), _lib.stream_handle(theta.device))
             if dts_r is not None:
                 gl, gr, side, _, _ = dts_cross_backward_accum_fused(
                     sv["pi_wave"], sv["pibar_wave"], dv, ws, meta["sl"], meta["sr"], meta["reduce_idx"],
