@@ -28,7 +28,8 @@ from .kernels.wave_backward import (dts_cross_backward_accum_fused, uniform_cros
                                     wave_backward_uniform_fused)
 from .kernels.wave_so import wave_backward_so
 from .params import as_item_param, as_item_state, extract_parameters_weighted_cols
-from .tangent import jvp_root_scores, tangent_wave_cache
+from . import engine, tree
+from .tangent import jvp_batch, jvp_root_scores, tangent_wave_cache
 
 LN2 = math.log(2.0)
 
@@ -133,12 +134,32 @@ def make_exact_hvp(static, theta, col_weights, sv, *, cache=None, debug_out=None
                     + (mt_hi * cot_mc).sum() + (col_h * cot_col).sum())
             (g1,) = torch.autograd.grad(phi1, theta_req, create_graph=True)
 
+    # the tangent forward by the fused engine's level launches (one launch per dependency level
+    # instead of two per wave; no host read-back, so it stays inside the CUDA graph) where the
+    # primal state came from the fused forward (its saved split reductions); else wave by wave
+    engine_tangent = ("dts_wave" in sv and G == 1 and tree.tour_layout(S) is not None
+                      and engine.supported(static) and getattr(static, "_hvp_engine_tangent", True))
+
+    def tangent_forward(u):
+        if not engine_tangent:
+            return jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters,
+                                   wave_cache=tcache)
+        roots, f = jvp_batch(static, theta, u.reshape(1, S, 3), sv, self_iters=tangent_self_iters,
+                             return_full=True)
+        st = lambda t: as_item_state(t, S, 1)  # noqa: E731
+        dpS, dpD, dE = f["dlog_pS"], f["dlog_pD"], f["dE"]
+        dc = {"dDL": st(dpD) + st(dE), "dEbar": st(f["dEbar"]), "dE": st(dE), "dSL1": st(dpS) + st(f["dE_s2"]),
+              "dSL2": st(dpS) + st(f["dE_s1"]), "dMC": st(f["dmax_coupling"]), "dleaf": st(dpS),
+              "dpd_param": as_item_param(dpD, 1, S), "dps_param": as_item_param(dpS, 1, S)}
+        return roots[0], {"dPi": f["dPi"][0], "dPibar": f["dPibar"][0], "dcst": dc, "dE": dE,
+                          "dEbar": f["dEbar"], "dE_s1": f["dE_s1"], "dE_s2": f["dE_s2"], "dlog_pS": dpS,
+                          "dlog_pD": dpD, "dlog_pL": f["dlog_pL"], "dmax_coupling": f["dmax_coupling"]}
+
     @torch.no_grad()
     def body(u_vec):
         """One HVP without host synchronisation: returns (H u, E-solve status, residual)."""
         u = u_vec.reshape(S, 3).to(torch.float32)
-        t_root, full = jvp_root_scores(static, theta, u, sv, return_full=True, self_iters=tangent_self_iters,
-                                       wave_cache=tcache)
+        t_root, full = tangent_forward(u)
         dc = full["dcst"]
         dPi, dPibar = full["dPi"], full["dPibar"]
         dE, dEbar_e, dE_s1, dE_s2 = full["dE"], full["dEbar"], full["dE_s1"], full["dE_s2"]

@@ -161,3 +161,24 @@ def test_hvp_cuda_graph_replays_match(name, cuda):
         u = torch.from_numpy(hv[f"u{k}"]).to(cuda)
         close_vec(f"graph Hu[{k}]", graphed(u).cpu().numpy(), eager(u).cpu().numpy())
         close_vec(f"graph Hu[{k}] vs reference", graphed(u).cpu().numpy(), hv[f"hu{k}"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_hvp_engine_tangent_matches_wave_tangent(name, cuda):
+    """On a primal state from the fused forward (which carries its split reductions), the HVP's
+    tangent forward runs on the engine's level launches; it must give the HVP of the wave-by-wave
+    tangent sweep on the same state."""
+    from kbench_b200.hvp import make_exact_hvp
+    cap, _ = load_golden(name)
+    hv = dict(np.load(GOLDEN / "hvp" / f"{name}.npz"))
+    capt = gen.to_torch(cap)
+    static = runtime.make_static(capt, cuda)
+    theta = capt["inputs"]["theta"].to(cuda)
+    cw = capt["inputs"]["col_weights"].to(cuda)
+    _, sv = runtime.run_forward(static, theta, cw)
+    u = torch.from_numpy(hv["u0"]).to(cuda)
+    out = {}
+    for engine_tangent in (True, False):
+        static._hvp_engine_tangent = engine_tangent
+        out[engine_tangent] = make_exact_hvp(static, theta, cw, sv)(u).cpu().numpy()
+    close_vec("Hu engine vs wave tangent", out[True], out[False])
