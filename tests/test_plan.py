@@ -104,3 +104,35 @@ def test_list_schedule_rejects_a_cycle():
     with pytest.raises(ValueError):
         _lib.call("kb_list_schedule", 2, ptr.ctypes.data, idx.ctypes.data, ptr.ctypes.data, idx.ctypes.data,
                   cost.ctypes.data, 4, order.ctypes.data, None)
+
+
+def test_list_schedule_bounds():
+    """The host list scheduler's modelled makespan: the summed cost on one worker, the critical
+    path with a worker per row, and in between the classic list-scheduling bounds."""
+    from types import SimpleNamespace
+    import numpy as np
+    from kbench_b200 import _lib, engine, gen
+    cap = gen.generate(1)
+    plan = engine.build_plan(SimpleNamespace(wave_layout=cap["static"]["wave_layout"]))
+    C = int(cap["meta"]["C"])
+    cp, ci = plan.child_ptr.numpy().astype(np.int64), plan.child_idx.numpy().astype(np.int32)
+    pp, pi = plan.par_ptr.numpy().astype(np.int64), plan.par_idx.numpy().astype(np.int32)
+    cost = 1.0 + 0.1 * np.diff(plan.row_split_ptr.numpy()).astype(np.float64)
+    # critical path (forward: a row after its children)
+    fin = np.zeros(C)
+    for r in range(C):  # children have smaller row ids
+        fin[r] = cost[r] + (fin[ci[cp[r]:cp[r + 1]]].max() if cp[r + 1] > cp[r] else 0.0)
+    crit = fin.max()
+
+    def span(workers):
+        order = np.empty(C, dtype=np.int32)
+        out = np.zeros(1)
+        _lib.call("kb_list_schedule", C, cp.ctypes.data, ci.ctypes.data, pp.ctypes.data, pi.ctypes.data,
+                  cost.ctypes.data, workers, order.ctypes.data, out.ctypes.data)
+        return float(out[0])
+
+    assert abs(span(1) - cost.sum()) < 1e-6 * cost.sum()
+    assert abs(span(C) - crit) < 1e-9 * crit
+    for w in (2, 8, 32):
+        s = span(w)
+        assert max(cost.sum() / w, crit) - 1e-9 <= s <= cost.sum() / w + crit + 1e-9
