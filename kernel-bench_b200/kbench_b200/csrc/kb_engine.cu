@@ -628,6 +628,74 @@ __device__ __forceinline__ void tour_scan_sw(float* T, float* red, float& mx, fl
   __syncthreads();
 }
 
+// The same scan with one barrier: T (the swizzled tour, NT * 2VF floats) is only read, and the
+// WITHIN-WARP exclusive prefix of every slot goes to X (same layout) before the barrier that
+// publishes the warp totals.  Lane w of every warp returns in wx the exclusive prefix of warp w's
+// total, so the prefix of the slot at byte offset off is
+//     lds_at(X, off) + __shfl_sync(full, wx, off / (4 * 64 * VF))
+// (64 VF floats per warp), readable after the return without another barrier.  Block max of mx
+// and block sum of sm as tour_scan_sw.  The caller syncs before (T complete); X's previous readers
+// must be past a barrier that precedes this call.
+template <int VF>
+__device__ __forceinline__ void tour_scan_sw_wx(const float* T, float* X, float* red, float& mx, float& sm,
+                                                float& wx) {
+  constexpr int Q = VF / 2;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int sw = Q == 1 ? 0 : ((t / (8 / Q)) & (Q - 1));
+  const float4* base = reinterpret_cast<const float4*>(T) + t * Q;
+  float4* xb = reinterpret_cast<float4*>(X) + t * Q;
+  float4 v[Q];
+  float gs[Q];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    v[q] = base[q ^ sw];
+    gs[q] = (v[q].x + v[q].y) + (v[q].z + v[q].w);
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) local += gs[q];
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  float run = incl - local;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    float4 o;
+    o.x = run;
+    o.y = run + v[q].x;
+    o.z = o.y + v[q].y;
+    o.w = o.z + v[q].z;
+    xb[q ^ sw] = o;
+    run += gs[q];
+  }
+  mx = warp_max(mx);
+  sm = warp_sum(sm);
+  if (lane == 31) red[wid] = incl;
+  if (lane == 0) { red[32 + wid] = mx; red[64 + wid] = sm; }
+  __syncthreads();
+  float tt = lane < nw ? red[lane] : 0.f;
+  const float bm = lane < nw ? red[32 + lane] : 0.f;
+  const float bs = lane < nw ? red[64 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, tt, o);
+    if (lane >= o) tt += y;
+  }
+  mx = warp_max(bm);
+  sm = warp_sum(bs);
+  const float prev = __shfl_up_sync(0xffffffffu, tt, 1);
+  wx = lane == 0 ? 0.f : prev;
+}
+
+// The slot prefix of tour_scan_sw_wx at byte offset off.
+template <int VF>
+__device__ __forceinline__ float tour_prefix_wx(const char* X, unsigned off, float wx) {
+  return lds_at(X, off) + __shfl_sync(0xffffffffu, wx, (int)(off / (4u * 64u * VF)));
+}
+
 struct Fwd4Args {
   FwdArgs f;
   const unsigned* tb;   // [3, NTV] tour tables
@@ -788,6 +856,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
   float* red = sm + 8 * (NTV + 4);  // after the split staging slots (the tour buffers alias them)
   char* T0 = reinterpret_cast<char*>(sm);
   char* T1 = reinterpret_cast<char*>(sm + TB);
+  char* TX = reinterpret_cast<char*>(sm + 2 * TB);  // the iterations' scanned prefixes (6 NTV <= 8 (NTV + 4))
   const int tid = threadIdx.x;
   const long long item = c.item_idx[row];
   const size_t cb = (size_t)(item * c.crs);
@@ -940,8 +1009,10 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
 #pragma unroll
     for (int k = 0; k < VF; ++k)
       part[k] = fmaf(lds_at(Tc, ce[k] & 0xFFFFu), kC1[k], lds_at(Tc, ce[k] >> 16) * kC2[k]);
-    float zmax = zmax_l, zsum = zsum_l;
-    tour_scan_sw<VF>(reinterpret_cast<float*>(Tc), red, zmax, zsum);
+    // Tc stays as it is (the speciation gathers above read it); the prefixes go to TX, whose
+    // readers of the previous iteration are past the barrier at the top of this one
+    float zmax = zmax_l, zsum = zsum_l, wx;
+    tour_scan_sw_wx<VF>(reinterpret_cast<const float*>(Tc), reinterpret_cast<float*>(TX), red, zmax, zsum, wx);
     const float inv = zmax > 0.f ? 1.0f / zmax : 0.f;
     const float Rn = zmax > 0.f ? R + lg2(zmax) : R;
     const float fd = ex2(Rd - Rn);
@@ -951,7 +1022,7 @@ __device__ __forceinline__ void forward_tour_row(const Fwd4Args& args, long long
     const bool resid = (it == last) && (a.residual != nullptr);
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
-      const float path = lds_at(Tc, tr[k] & 0xFFFFu) + z[k];
+      const float path = tour_prefix_wx<VF>(TX, tr[k] & 0xFFFFu, wx) + z[k];
       const float D = fmaxf(zsum - path, 0.f);
       const float lin = fmaf(D, kB[k], fmaf(z[k], kA[k], part[k]));
       const float zn = fmaf(lin, inv, td[k] * fd);
@@ -1526,6 +1597,78 @@ __device__ __forceinline__ float2& pair_at(float2* base, unsigned off) {
   return *reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + off);
 }
 
+// tour_scan_pair with one barrier, as tour_scan_sw_wx: T is only read, the within-warp exclusive
+// prefixes of both sums go to X (same layout) before the barrier, and lane w returns in wa / wb the
+// exclusive prefixes of warp w's totals; the slot at byte offset off then holds
+//     pair_at(X, off) + (__shfl_sync(full, wa, off / (512 VF)), __shfl_sync(full, wb, ...))
+// (2 VF float2 entries = 16 VF bytes per thread).  Block sums of sa and sb as tour_scan_pair.
+template <int VF>
+__device__ __forceinline__ void tour_scan_pair_wx(const float2* T, float2* X, float* red, float& sa, float& sb,
+                                                  float& wa, float& wb) {
+  constexpr int Q = VF;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int sw = Q == 1 ? 0 : ((t / (8 / Q)) & (Q - 1));
+  const float4* base = reinterpret_cast<const float4*>(T) + t * Q;
+  float4* xb = reinterpret_cast<float4*>(X) + t * Q;
+  float la = 0.f, lb = 0.f;  // the group sums are formed again below (no registers held across the scan)
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    la += v.x + v.z;
+    lb += v.y + v.w;
+  }
+  float ia = la, ib = lb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, ia, o);
+    const float yb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ya;
+      ib += yb;
+    }
+  }
+  float ra = ia - la, rb = ib - lb;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 v = base[q ^ sw];
+    xb[q ^ sw] = make_float4(ra, rb, ra + v.x, rb + v.y);
+    ra += v.x + v.z;
+    rb += v.y + v.w;
+  }
+  sa = warp_sum(sa);
+  sb = warp_sum(sb);
+  if (lane == 31) { red[wid] = ia; red[32 + wid] = ib; }
+  if (lane == 0) { red[64 + wid] = sa; red[96 + wid] = sb; }
+  __syncthreads();
+  float ta = lane < nw ? red[lane] : 0.f;
+  float tb2 = lane < nw ? red[32 + lane] : 0.f;
+  const float bsa = lane < nw ? red[64 + lane] : 0.f;
+  const float bsb = lane < nw ? red[96 + lane] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, ta, o);
+    const float yb = __shfl_up_sync(0xffffffffu, tb2, o);
+    if (lane >= o) {
+      ta += ya;
+      tb2 += yb;
+    }
+  }
+  sa = warp_sum(bsa);
+  sb = warp_sum(bsb);
+  const float pa = __shfl_up_sync(0xffffffffu, ta, 1);
+  const float pb = __shfl_up_sync(0xffffffffu, tb2, 1);
+  wa = lane == 0 ? 0.f : pa;
+  wb = lane == 0 ? 0.f : pb;
+}
+
+// The slot prefix pair of tour_scan_pair_wx at byte offset off.
+template <int VF>
+__device__ __forceinline__ float2 tour_prefix_pair_wx(float2* X, unsigned off, float wa, float wb) {
+  const int w = (int)(off / (512u * VF));
+  const float2 p = pair_at(X, off);
+  return make_float2(p.x + __shfl_sync(0xffffffffu, wa, w), p.y + __shfl_sync(0xffffffffu, wb, w));
+}
+
 // Tangent of one level for a PAIR of directions per CTA (blockIdx.y = pair index): the primal
 // weights, the Euler-tour addressing and the split weights are shared by the two directions,
 // which travel together as float2 through the tour scan and the gathers.  Same arithmetic as
@@ -1741,10 +1884,16 @@ __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row
       }
     }
   }
+  // Two barriers per step: the tour (T0) and the tangent row (DP0) are written, published, then
+  // gathered and scanned, the scan leaving its prefixes in T1; the next step's stores come after
+  // this step's scan barrier, which every reader of T0 and DP0 passed, and the prefixes' readers
+  // pass the next step's publishing barrier before the next scan writes T1.  The barrier before
+  // the first step ends the setup's and the splits' use of these buffers (DP0 held the parked
+  // coefficients, read back by other threads' columns).
+  __syncthreads();
   for (int it = 1; it <= last; ++it) {
-    float2* Tc = (it & 1) ? T0 : T1;
-    float2* Dc = (it & 1) ? DP0 : DP1;
-    __syncthreads();  // the previous step's (or the setup's) readers of Tc / Dc are done
+    float2* Tc = T0;
+    float2* Dc = DP0;
     float sa = 0.f, sbv = 0.f;
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
@@ -1763,10 +1912,11 @@ __device__ __forceinline__ void tangent_pair_row(const TanArgs& a, long long row
       pa[k] = fmaf(c3[k], g1.x, c4[k] * g2.x);
       pbv[k] = fmaf(c3[k], g1.y, c4[k] * g2.y);
     }
-    tour_scan_pair<VF>(Tc, red, sa, sbv);
+    float wa, wb;
+    tour_scan_pair_wx<VF>(Tc, T1, red, sa, sbv, wa, wb);
 #pragma unroll
     for (int k = 0; k < VF; ++k) {
-      const float2 p = pair_at(Tc, tr[k] & 0xFFFFu);
+      const float2 p = tour_prefix_pair_wx<VF>(T1, tr[k] & 0xFFFFu, wa, wb);
       const float Da = sa - (p.x + r[k] * dpa[k]);
       const float Db = sbv - (p.y + r[k] * dpb[k]);
       dpa[k] = cA[k] * dpa[k] + c2[k] * Da + pa[k] + ca_[k];
