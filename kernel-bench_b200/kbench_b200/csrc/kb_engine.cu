@@ -1235,7 +1235,9 @@ __device__ __forceinline__ void flow_finish_row(const Flow& f, int row, FlowSlot
     const int r = row - grp * f.C;
     for (long long j = f.par_ptr[r] + threadIdx.x; j < f.par_ptr[r + 1]; j += 32) {
       const int p = grp * f.C + f.par_idx[j];
-      if (atomicSub(f.remaining + p, 1) == 1 && !f.static_order) {
+      if (f.static_order) {
+        atomicSub(f.remaining + p, 1);  // value unused: a reduction, no round trip before the next row
+      } else if (atomicSub(f.remaining + p, 1) == 1) {
         const unsigned slot = atomicAdd(f.tail, 1u);
         atomicExch(f.queue + slot, p);
       }
@@ -2063,6 +2065,32 @@ enum { G_PD = 0, G_PS, G_MT, G_E, G_EBAR, G_ES1, G_ES2, G_COL, G_N };
 static_assert(G_PD == 0 && G_PS == 1 && G_MT == 2, "shared column-sum rows");
 
 #define KB_FLOW_FLUSH_ROWS 8
+// Splits whose child rows are requested into L2 ahead of their turn (see bwd_prefetch_split).
+#define KB_BWD_PREFETCH_SPLITS 4
+
+// A hint (one thread): bring the row of n floats at p into L2 with one bulk prefetch.  The range
+// is the row's 16-byte aligned cover rounded INWARD at the end (the start rounds down to at most
+// 12 bytes before p, still inside the array, whose base is 16-byte aligned), so it never leaves
+// the array; a prefetch changes no data, so the few floats it misses or adds do not matter.
+__device__ __forceinline__ void l2_prefetch_row(const float* p, int n) {
+  const unsigned long long a = (unsigned long long)(uintptr_t)p & ~15ull;
+  const unsigned long long e = (unsigned long long)(uintptr_t)(p + n) & ~15ull;
+  if (e > a)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((unsigned)(e - a)) : "memory");
+}
+
+// The child rows split i of the backward reads: the children's Pi rows (staged), Pibar rows (read
+// at the own columns) and adjoint rows (the targets of the split's atomic adds).  A backward row's
+// split phase otherwise meets each split's rows at the latency of HBM.
+__device__ __forceinline__ void bwd_prefetch_split(const BwdArgs& a, long long i, int S) {
+  const size_t l = (size_t)a.sp.sl[i] * S, r = (size_t)a.sp.sr[i] * S;
+  l2_prefetch_row(a.Pi + l, S);
+  l2_prefetch_row(a.Pi + r, S);
+  l2_prefetch_row(a.Pibar + l, S);
+  l2_prefetch_row(a.Pibar + r, S);
+  l2_prefetch_row(a.acc + l, S);
+  l2_prefetch_row(a.acc + r, S);
+}
 
 // DF = the dataflow schedule (one persistent launch; f.par_ptr / par_idx then list each row's
 // distinct CHILD rows, released when the row is done; a row is ready once all its parents ran).
@@ -2152,6 +2180,11 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     if (!active) {
       if (DF) flow_finish_row(f, (int)row, &fs);
       continue;
+    }
+    // the first splits' child rows travel to L2 while the row's precompute and Neumann terms run
+    if (has_splits && threadIdx.x == 0) {
+      const long long pe = i1 < i0 + KB_BWD_PREFETCH_SPLITS ? i1 : i0 + KB_BWD_PREFETCH_SPLITS;
+      for (long long i = i0; i < pe; ++i) bwd_prefetch_split(a, i, S);
     }
 
     // ---- dts row (log) ----
@@ -2436,6 +2469,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
           cSR = stage_row_cg(SRb, a.Pi + (size_t)a.sp.sr[i + 1] * S, S, NTV, true);
           cp_async_commit();
         }
+        if (threadIdx.x == 0 && i + KB_BWD_PREFETCH_SPLITS < i1) bwd_prefetch_split(a, i + KB_BWD_PREFETCH_SPLITS, S);
         float sabs_l = 0.f, sabs_r = 0.f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {  // the scatter wrote each column's pair at pre(s)
@@ -2469,6 +2503,18 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     }
     if (DF) {
       flow_finish_row(f, (int)row, &fs);
+      // In a fixed start order the slot the poller just took names the CTA's next row: its own
+      // rows travel to L2 while the CTA waits for it or flushes
+      if (f.static_order && threadIdx.x == flow_poller() && fs.next >= 0 && fs.next < f.n_items) {
+        const int nr = f.queue[fs.next];
+        if (nr >= 0 && nr < f.C) {
+          const size_t o = (size_t)nr * S;
+          l2_prefetch_row(a.acc + o, S);
+          l2_prefetch_row(a.Pi + o, S);
+          l2_prefetch_row(a.Pibar + o, S);
+          if (a.dts_saved) l2_prefetch_row(a.dts_saved + o, S);
+        }
+      }
       // A persistent CTA runs hundreds of rows: keep the fp32 partial sums short (as a level launch
       // does) by moving them into the fp64 slot every few rows.  Own columns only: no barrier.
       if (++since_flush == KB_FLOW_FLUSH_ROWS) {
