@@ -233,7 +233,11 @@ int kb_active_mask(const float* rhs, long long row_stride, int W, int S, float t
  * const_mode: 0 shared [S] constants, 1 row-expanded [W,S], 2 item rows [G,S] via item_idx.
  * leaf_mode: 0 [S], 1 [G], 2 [G,S], 3 scalar. grad_col (may be NULL) is accumulated.
  * last_relres (may be NULL; [W]): |last Neumann term| / max(|v|, FLT_MIN) per row, 0 on inactive
- * rows -- the return_last_increment output (wave_backward.py:1596-1613). */
+ * rows -- the return_last_increment output (wave_backward.py:1596-1613).
+ * initial_v (may be NULL; [W,S] rows at initial_v_row_stride): the warm-started solve of the
+ * initial_v option (wave_backward.py:1493-1534): v = initial_v, then neumann_terms fixed-point
+ * updates v <- rhs + J^T v per active row; inactive rows' v_k rows are set to initial_v; last_relres
+ * must then be NULL (the reference returns no last increment for it, :1596-1600). */
 int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
                     const float* rhs, long long rhs_row_stride, const unsigned char* active, const float* dl,
                     const float* ebar, const float* e, const float* sl1, const float* sl2, int const_mode,
@@ -241,9 +245,24 @@ int kb_wave_adjoint(const float* Pi, const float* Pibar, const float* pibar_row_
                     const int* node_child2, const int* node_parent, const int* jumps, int K,
                     const long long* lv_ptr, int n_levels, const int* lv_par, const int* lv_c1, const int* lv_c2,
                     int use_leaf_index, const int* leaf_state, const float* leaf_logp, int leaf_mode,
-                    const float* leaf_term, const long long* item_idx, int neumann_terms, float* grad_col,
-                    float* v_k, float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4,
-                    float* last_relres, int ws, int W, int S, void* stream);
+                    const float* leaf_term, const long long* item_idx, int neumann_terms,
+                    const float* initial_v, long long initial_v_row_stride, float* grad_col, float* v_k,
+                    float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4, float* last_relres,
+                    int ws, int W, int S, void* stream);
+
+/* The self_loop_grad_targets option of wave_backward_uniform_fused (wave_backward.py:1615-1640 and
+ * the ACCUM_GRADS branch of its parameter store, :1208-1262): the column sums over the wave's rows
+ * of the buckets kb_wave_adjoint wrote ([W,S] each, zero on inactive rows) are ADDED into the
+ * caller's fp32 targets: grad_log_pD += aw0 and grad_log_pS += aw345 ([S] each with
+ * param_grad_vector, else one scalar each: the sums over all columns), grad_E += aw0 + aw2,
+ * grad_Ebar += aw1, grad_E_s1 += aw4, grad_E_s2 += aw3, grad_mt += aw2 ([S] each).  Sums in fp64
+ * in a fixed order (the reference adds row by row with atomics).  col_tot: [2,S] fp64 scratch,
+ * required without param_grad_vector (may be NULL with it). */
+int kb_wave_adjoint_accum_targets(const float* aw0, const float* aw1, const float* aw2, const float* aw345,
+                                  const float* aw3, const float* aw4, int W, int S, float* grad_log_pD,
+                                  float* grad_log_pS, int param_grad_vector, float* grad_E, float* grad_Ebar,
+                                  float* grad_E_s1, float* grad_E_s2, float* grad_mt, double* col_tot,
+                                  void* stream);
 
 /* The operator of the self-loop solve, A x = x - J_self^T x, per active row (one application of
  * the single-term kernel with OUTPUT_A, wave_backward.py:485-638, as the GMRES self-loop solver

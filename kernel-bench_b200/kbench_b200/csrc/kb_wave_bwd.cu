@@ -66,6 +66,8 @@ struct AdjArgs {
   const float* leaf_term;    // [W,S] materialised leaf term, or null
   const long long* item_idx; // [C] or null
   int neumann_terms;
+  const float* init_v;       // [W,S] rows at stride init_rs, or null: with it the solve is the
+  long long init_rs;         //   warm-started fixed point v <- rhs + J^T v (neumann_terms updates)
   float* grad_col;           // [S] or null (accumulated)
   float* v_k;
   float* aw0;
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
       } else {
         a.aw0[ob + s] = 0.f; a.aw1[ob + s] = 0.f; a.aw2[ob + s] = 0.f;
         a.aw345[ob + s] = 0.f; a.aw3[ob + s] = 0.f; a.aw4[ob + s] = 0.f;
+        if (a.init_v) a.v_k[ob + s] = a.init_v[(size_t)w * a.init_rs + s];  // inactive rows keep it
       }
     }
     if (a.last_relres && threadIdx.x == 0) a.last_relres[w] = 0.f;
@@ -203,7 +206,8 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
       const int x = a.c1[s], y = a.c2[s];
       if (x >= 0 && x < S) EDGE[x] = s1w;
       if (y >= 0 && y < S) EDGE[y] = s2w;
-      v[k] = a.apply_out ? a.apply_in[(size_t)w * a.apply_rs + s] : a.rhs[(size_t)w * a.rhs_rs + s];
+      v[k] = a.apply_out ? a.apply_in[(size_t)w * a.apply_rs + s]
+                         : (a.init_v ? a.init_v[(size_t)w * a.init_rs + s] : a.rhs[(size_t)w * a.rhs_rs + s]);
     }
   }
   __syncthreads();
@@ -243,7 +247,12 @@ __global__ void __launch_bounds__(512) wave_adjoint_kernel(AdjArgs a) {
         const float base = T[s] * diag[k] + pp[k] * (A - U[s]);
         const float pt = (par >= 0 && par < S) ? T[par] : 0.f;
         nv[k] = base + pt * edge[k];
-        v[k] += nv[k];
+        if (a.init_v) {  // fixed-point update: the next iterate is rhs + J^T v, and is also the next T
+          nv[k] = a.rhs[(size_t)w * a.rhs_rs + s] + nv[k];
+          v[k] = nv[k];
+        } else {
+          v[k] += nv[k];
+        }
       }
     }
     __syncthreads();
@@ -621,6 +630,78 @@ extern "C" int kb_active_mask(const float* rhs, long long row_stride, int W, int
 
 namespace {
 
+// Column sums of one wave's six parameter buckets (aw0, aw1, aw2, aw345, aw3, aw4; [W,S], zero on
+// inactive rows) added into the caller's gradient targets: the self_loop_grad_targets form of the
+// parameter store (ACCUM_GRADS).  32 columns per CTA, ACC_ROWS row strides; every sum in fp64 and in a
+// fixed order (the reference adds row by row with atomics).  pd_vector == 0: grad_pD / grad_pS are
+// one scalar each; the per-column sums of aw0 / aw345 go to col_tot [2,S] and targets_scalar_kernel
+// adds their totals.
+struct AccumTargets {
+  const float* aw[6];
+  float* pD;
+  float* pS;
+  float* E;
+  float* Ebar;
+  float* Es1;
+  float* Es2;
+  float* mt;
+  double* col_tot;  // [2,S] when !pd_vector
+  int pd_vector;
+};
+
+constexpr int ACC_ROWS = 16;
+
+__global__ void __launch_bounds__(32 * ACC_ROWS) accum_targets_kernel(AccumTargets t, int W, int S) {
+  __shared__ double part[6][ACC_ROWS][33];
+  const int lane = threadIdx.x, ty = threadIdx.y;
+  const int s = blockIdx.x * 32 + lane;
+  double acc[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+  if (s < S) {
+    for (int w = ty; w < W; w += ACC_ROWS) {
+      const size_t o = (size_t)w * S + s;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) acc[k] += (double)t.aw[k][o];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 6; ++k) part[k][ty][lane] = acc[k];
+  __syncthreads();
+  if (ty == 0 && s < S) {
+    double tot[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      double v = 0.0;
+      for (int y = 0; y < ACC_ROWS; ++y) v += part[k][y][lane];
+      tot[k] = v;
+    }
+    if (t.pd_vector) {
+      t.pD[s] = (float)((double)t.pD[s] + tot[0]);
+      t.pS[s] = (float)((double)t.pS[s] + tot[3]);
+    } else {
+      t.col_tot[s] = tot[0];
+      t.col_tot[S + s] = tot[3];
+    }
+    t.E[s] = (float)((double)t.E[s] + (tot[0] + tot[2]));
+    t.Ebar[s] = (float)((double)t.Ebar[s] + tot[1]);
+    t.Es1[s] = (float)((double)t.Es1[s] + tot[5]);
+    t.Es2[s] = (float)((double)t.Es2[s] + tot[4]);
+    t.mt[s] = (float)((double)t.mt[s] + tot[2]);
+  }
+}
+
+// Scalar pD / pS targets: the totals of col_tot's two rows, in column order, by one warp each.
+__global__ void targets_scalar_kernel(const double* __restrict__ col_tot, int S, float* pD, float* pS) {
+  const int lane = threadIdx.x & 31, which = threadIdx.x >> 5;
+  const double* row = col_tot + (size_t)which * S;
+  double v = 0.0;
+  for (int s = lane; s < S; s += 32) v += row[s];
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  if (lane == 0) {
+    float* dst = which == 0 ? pD : pS;
+    dst[0] = (float)((double)dst[0] + v);
+  }
+}
+
 AdjArgs adjoint_args(const float* Pi, const float* Pibar, const float* pibar_row_max, const float* dts,
                      const unsigned char* active, const float* dl, const float* ebar, const float* e,
                      const float* sl1, const float* sl2, int const_mode, const float* col_log_probs,
@@ -670,9 +751,11 @@ extern "C" int kb_wave_adjoint(const float* Pi, const float* Pibar, const float*
                                const int* lv_par, const int* lv_c1, const int* lv_c2, int use_leaf_index,
                                const int* leaf_state, const float* leaf_logp, int leaf_mode,
                                const float* leaf_term, const long long* item_idx, int neumann_terms,
-                               float* grad_col, float* v_k, float* aw0, float* aw1, float* aw2, float* aw345,
-                               float* aw3, float* aw4, float* last_relres, int ws, int W, int S, void* stream) {
+                               const float* initial_v, long long initial_v_row_stride, float* grad_col,
+                               float* v_k, float* aw0, float* aw1, float* aw2, float* aw345, float* aw3, float* aw4,
+                               float* last_relres, int ws, int W, int S, void* stream) {
   if (S <= 0 || W < 0 || K < 0 || neumann_terms < 0 || n_levels < 0) return KB_ERR_ARG;
+  if (initial_v && last_relres) return KB_ERR_ARG;  // no last increment for a warm-started solve
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (W == 0) return KB_OK;
   AdjArgs a = adjoint_args(Pi, Pibar, pibar_row_max, dts, active, dl, ebar, e, sl1, sl2, const_mode, col_log_probs,
@@ -681,6 +764,7 @@ extern "C" int kb_wave_adjoint(const float* Pi, const float* Pibar, const float*
                            item_idx, ws, W, S);
   a.rhs = rhs; a.rhs_rs = rhs_row_stride;
   a.neumann_terms = neumann_terms; a.grad_col = grad_col; a.v_k = v_k;
+  a.init_v = initial_v; a.init_rs = initial_v_row_stride;
   a.aw0 = aw0; a.aw1 = aw1; a.aw2 = aw2; a.aw345 = aw345; a.aw3 = aw3; a.aw4 = aw4;
   a.last_relres = last_relres;
   return launch_adjoint(a, stream);
@@ -784,5 +868,26 @@ extern "C" int kb_pibar_vjp_tree(const float* Pi, const float* col_log_probs, in
   const size_t smem = (size_t)S * sizeof(float);
   if (smem_attr((const void*)pibar_tree_kernel, smem)) return KB_ERR_LAUNCH;
   pibar_tree_kernel<<<2 * N, bd, smem, (cudaStream_t)stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
+}
+
+extern "C" int kb_wave_adjoint_accum_targets(const float* aw0, const float* aw1, const float* aw2,
+                                             const float* aw345, const float* aw3, const float* aw4, int W, int S,
+                                             float* grad_log_pD, float* grad_log_pS, int param_grad_vector,
+                                             float* grad_E, float* grad_Ebar, float* grad_E_s1, float* grad_E_s2,
+                                             float* grad_mt, double* col_tot, void* stream) {
+  if (W < 0 || S <= 0 || !aw0 || !aw1 || !aw2 || !aw345 || !aw3 || !aw4) return KB_ERR_ARG;
+  if (!grad_log_pD || !grad_log_pS || !grad_E || !grad_Ebar || !grad_E_s1 || !grad_E_s2 || !grad_mt)
+    return KB_ERR_ARG;
+  if (!param_grad_vector && !col_tot) return KB_ERR_ARG;
+  if (W == 0) return KB_OK;
+  AccumTargets t;
+  t.aw[0] = aw0; t.aw[1] = aw1; t.aw[2] = aw2; t.aw[3] = aw345; t.aw[4] = aw3; t.aw[5] = aw4;
+  t.pD = grad_log_pD; t.pS = grad_log_pS; t.E = grad_E; t.Ebar = grad_Ebar; t.Es1 = grad_E_s1;
+  t.Es2 = grad_E_s2; t.mt = grad_mt; t.col_tot = col_tot; t.pd_vector = param_grad_vector;
+  cudaStream_t st = (cudaStream_t)stream;
+  accum_targets_kernel<<<(S + 31) / 32, dim3(32, ACC_ROWS), 0, st>>>(t, W, S);
+  if (cudaGetLastError() != cudaSuccess) return KB_ERR_LAUNCH;
+  if (!param_grad_vector) targets_scalar_kernel<<<1, 64, 0, st>>>(col_tot, S, grad_log_pD, grad_log_pS);
   return cudaGetLastError() == cudaSuccess ? KB_OK : KB_ERR_LAUNCH;
 }

@@ -110,21 +110,28 @@ def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_sq
                                 grad_col_log_probs=None, use_col_weights=True, self_loop_grad_targets=None,
                                 initial_v=None, self_loop_solver="neumann", return_last_increment=False):
     """Reference ``wave_backward.py:1737-1867``: per active row, the adjoint ``v`` of the self-loop
-    -- ``self_loop_solver="neumann"``: the series ``v = sum_{n=0..N} (J_self^T)^n rhs``;
-    ``"gmres"``: ``N`` GMRES steps on ``(I - J_self^T) v = rhs`` over the whole wave -- and the
-    per-element parameter cotangents.
+    -- ``self_loop_solver="neumann"``: the series ``v = sum_{n=0..N} (J_self^T)^n rhs``, or, given
+    ``initial_v`` ([W,S]), ``v = initial_v`` followed by ``N`` fixed-point updates
+    ``v <- rhs + J_self^T v`` (``:1493-1534``; inactive rows keep ``initial_v``); ``"gmres"``: ``N``
+    GMRES steps on ``(I - J_self^T) v = rhs`` over the whole wave -- and the per-element parameter
+    cotangents.
 
     Returns ``(v_k, aw0, aw1, aw2, aw345, aw3, aw4)`` (new [W,S] tensors; aw* zero and v_k
     unspecified on inactive rows in the Neumann solve, zero in the GMRES solve), plus, with
     ``return_last_increment``, the per-row ``|last Neumann term| / |v|`` ([W], zero on inactive
-    rows; None for the GMRES solve or N = 0, as the reference); accumulates ``grad_col_log_probs``
-    in place."""
+    rows; None for the GMRES solve, a warm-started solve or N = 0, as the reference); accumulates
+    ``grad_col_log_probs`` in place.  With ``self_loop_grad_targets`` = (grad_log_pD, grad_log_pS,
+    grad_E, grad_Ebar, grad_E_s1, grad_E_s2, grad_mt, param_grad_vector) (``:1615-1640``, ``:1208-1262``)
+    the buckets' column sums over the wave are added into those fp32 tensors instead (pD += aw0,
+    pS += aw345 -- per column with ``param_grad_vector``, else one scalar each --, E += aw0 + aw2,
+    Ebar += aw1, E_s1 += aw4, E_s2 += aw3, mt += aw2) and the six buckets are returned as None."""
     require_cuda_f32("GPUREC self-loop 2D fast path", Pi_star, Pibar_star, rhs)
     solver = str(self_loop_solver).strip().lower()
     if solver not in ("neumann", "gmres"):
         raise ValueError(f"unsupported self-loop solver {self_loop_solver!r}")
-    if initial_v is not None or self_loop_grad_targets is not None:
-        raise NotImplementedError("initial_v / self_loop_grad_targets are not supported")
+    if solver == "gmres" and initial_v is not None:
+        raise ValueError("GMRES self-loop solve does not support initial_v")
+    targets = _grad_targets(self_loop_grad_targets, int(S), Pi_star.device)
     requested_has_leaf_term = bool(has_leaf_term)
     use_leaf_index = requested_has_leaf_term and leaf_state_idx is not None and leaf_logp is not None
     const_mode = _const_mode(DL_const, item_idx, bool(item_indexed_consts))
@@ -150,10 +157,17 @@ def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_sq
                      compact_level_child1=compact_level_child1, compact_level_child2=compact_level_child2)
     shape = (W, S)
     v_k, aw0, aw1, aw2, aw345, aw3, aw4 = (torch.empty(shape, device=dev, dtype=torch.float32) for _ in range(7))
-    want_rel = bool(return_last_increment) and solver == "neumann" and int(neumann_terms) > 0
+    if initial_v is not None:
+        if tuple(initial_v.shape) != shape:
+            raise ValueError(f"initial_v shape {tuple(initial_v.shape)} does not match wave scratch shape {shape}")
+        initial_v = initial_v.to(device=dev, dtype=torch.float32).contiguous()
+    want_rel = (bool(return_last_increment) and solver == "neumann" and initial_v is None
+                and int(neumann_terms) > 0)
     last_rel = torch.empty((W,), device=dev, dtype=torch.float32) if want_rel else None
-    out = (v_k, aw0, aw1, aw2, aw345, aw3, aw4)
+    out = (v_k, aw0, aw1, aw2, aw345, aw3, aw4) if targets is None else (v_k, None, None, None, None, None, None)
     if W == 0:
+        if initial_v is not None:
+            v_k.copy_(initial_v)
         return (*out, last_rel) if return_last_increment else out
     has_materialized = leaf_term_wt is not None
     leaf_term = None
@@ -188,9 +202,37 @@ def wave_backward_uniform_fused(Pi_star, Pibar_star, ws, W, S, dts_r, rhs, mt_sq
         v_k.copy_(v)
         rhs_c, n_terms = v, 0  # the buckets and the column gradient of the solved rows
     _lib.call("kb_wave_adjoint", *head, rhs_c.data_ptr(), int(rhs_c.stride(0)), *tail, n_terms,
-              _lib.ptr(grad_col_log_probs), v_k.data_ptr(), aw0.data_ptr(), aw1.data_ptr(), aw2.data_ptr(),
-              aw345.data_ptr(), aw3.data_ptr(), aw4.data_ptr(), _lib.ptr(last_rel), ws, W, S, st)
+              _lib.ptr(initial_v), S, _lib.ptr(grad_col_log_probs), v_k.data_ptr(), aw0.data_ptr(),
+              aw1.data_ptr(), aw2.data_ptr(), aw345.data_ptr(), aw3.data_ptr(), aw4.data_ptr(), _lib.ptr(last_rel),
+              ws, W, S, st)
+    if targets is not None:
+        vals, vector = targets
+        col_tot = None if vector else torch.empty((2, S), device=dev, dtype=torch.float64)
+        _lib.call("kb_wave_adjoint_accum_targets", aw0.data_ptr(), aw1.data_ptr(), aw2.data_ptr(),
+                  aw345.data_ptr(), aw3.data_ptr(), aw4.data_ptr(), W, S, vals[0].data_ptr(), vals[1].data_ptr(),
+                  int(vector), vals[2].data_ptr(), vals[3].data_ptr(), vals[4].data_ptr(), vals[5].data_ptr(),
+                  vals[6].data_ptr(), _lib.ptr(col_tot), st)
     return (*out, last_rel) if return_last_increment else out
+
+
+def _grad_targets(targets, S: int, device):
+    """Validate ``self_loop_grad_targets`` (reference ``wave_backward.py:1615-1625``): seven fp32
+    tensors updated in place and the ``param_grad_vector`` flag.  Returns ``(tensors, vector)`` or
+    None.  grad_log_pD / grad_log_pS hold ``S`` values with the flag and one without; the other five
+    hold ``S``."""
+    if targets is None:
+        return None
+    if len(targets) != 8:
+        raise ValueError("self_loop_grad_targets must be (grad_log_pD, grad_log_pS, grad_E, grad_Ebar, "
+                         "grad_E_s1, grad_E_s2, grad_mt, param_grad_vector)")
+    vals, vector = list(targets[:7]), bool(targets[7])
+    for i, t in enumerate(vals):
+        need = S if (i >= 2 or vector) else 1
+        if not torch.is_tensor(t) or t.device != device or t.dtype != torch.float32 or not t.is_contiguous() \
+                or t.numel() < need:
+            raise ValueError(f"self_loop_grad_targets[{i}] must be a contiguous fp32 tensor on {device} "
+                             f"with at least {need} elements")
+    return vals, vector
 
 
 def _param_ref(param, *, S, item_indexed, device):
