@@ -82,6 +82,9 @@ def parse_args():
     ap.add_argument("--per-kernel", action="store_true",
                     help="per-wrapper times of one forward + backward pass driven by the reference's own glue, "
                          "over the reference's stock Triton kernels and over this project's (--config, default 2)")
+    ap.add_argument("--atomic-backward", action="store_true",
+                    help="run the headline backward with atomic child adds instead of its deterministic form "
+                         "(child adjoints gathered from edge rows in a fixed order; engine._edge_scratch)")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
@@ -178,19 +181,24 @@ def algorithmic_bytes(plan, S):
 # Counters of ONE launch of each dataflow kernel on the benchmark's own config-3 family (seed 3000,
 # C = 128,282 rows), from single-pass ncu captures of the full-size launches
 # (``bench.py --traffic-case config3``): DRAM bytes read and written, and warp instructions
-# executed.  Empty until captured for the current build; the bench then reports null.
+# executed; the backward's per form (its child adjoints gathered from edge rows, the default, or
+# added with atomics).  A form not captured for the current build reports null.
 CONFIG3_ROWS = 128282
 CONFIG3_COUNTERS: dict = {
     "kb_flow_forward": {"dram_read": 18417902080, "dram_write": 6217162240, "warp_inst": 23781305587},
-    "kb_flow_backward": {"dram_read": 45366837504, "dram_write": 16917131776, "warp_inst": 40822535893},
+    ("kb_flow_backward", "atomic"): {"dram_read": 45366837504, "dram_write": 16917131776,
+                                     "warp_inst": 40822535893},
+    ("kb_flow_backward", "deterministic"): {"dram_read": 85957630464, "dram_write": 42019007232,
+                                            "warp_inst": 43715164395},
 }
 
 
-def launch_counters(name, C, S):
-    """The captured counters of one launch of ``name`` on the config-3 family, else None."""
+def launch_counters(name, C, S, form=None):
+    """The captured counters of one launch of ``name`` (the backward: in ``form``) on the config-3
+    family, else None."""
     if S != 4095 or C != CONFIG3_ROWS:
         return None
-    return CONFIG3_COUNTERS.get(name)
+    return CONFIG3_COUNTERS.get(name if form is None else (name, form))
 
 
 def issue_roofline(warp_inst, ms, sm_mhz):
@@ -1021,6 +1029,7 @@ def main():
     S = int(cap["meta"]["S"])
     C = int(cap["meta"]["C"])
     static = runtime.make_static(cap, dev)
+    static._deterministic_backward = not args.atomic_backward
     theta = cap["inputs"]["theta"].to(dev)
     cw = cap["inputs"]["col_weights"].to(dev)
     plan = engine.build_plan(static)
@@ -1151,7 +1160,9 @@ def main():
             kb = sum((fwd_b if "forward" in name else bwd_b).values())
             entry = {"ms": round(kms, 3), "hbm_gbs": round(kb / (kms * 1e-3) / 1e9, 1),
                      "hbm_frac": round(kb / (kms * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes": kb}
-            cnt = launch_counters(name, C, S)
+            cnt = launch_counters(name, C, S, None if name != "kb_flow_backward" else
+                                  ("deterministic" if getattr(static, "_edge_scratch", None) is not None
+                                   else "atomic"))
             if cnt is not None:
                 entry["dram_bytes"] = cnt["dram_read"] + cnt["dram_write"]
                 entry["dram_over_algorithmic"] = round(entry["dram_bytes"] / kb, 3)
@@ -1189,6 +1200,8 @@ def main():
                             "gradients all-reduced",
                 "parallelism": f"dp{world} (families)",
                 "l2": "state arrays (C*S*4 bytes each) far larger than L2; no flush needed",
+                "backward": ("deterministic (edge rows)" if getattr(static, "_edge_scratch", None) is not None
+                             else "atomic child adds"),
             },
             "ms_per_solve": round(ms_max, 3), "fwd_ms": round(fwd_ms, 3), "bwd_ms": round(bwd_ms, 3),
             "roofline": roofline,

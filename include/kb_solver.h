@@ -418,7 +418,13 @@ int kb_level_backward(const int* rows, const long long* split_ptr, int n_rows, c
  * without parents (the roots); child_ptr [C+1] / child_idx: the distinct child rows of each row.
  * Scratch queue [C], remaining [C], counters [3] (head, tail, error: nonzero after the launch =
  * a wait gave up after max_polls polls, results invalid).  grad_slots [n_slots, 8, NTV]: one per
- * persistent CTA (n_slots CTAs run).  Other arguments as kb_level_backward. */
+ * persistent CTA (n_slots CTAs run).  edge_rows (may be NULL: each split then adds its children's
+ * cotangents into accumulated_rhs with fp32 atomics, whose order varies run to run): [2N,S]
+ * scratch, row 2i / 2i+1 = split i's contribution to its left / right child (zeros when the row
+ * is inactive); a row's adjoint is then accumulated_rhs[row] (its seed) plus its incoming rows
+ * in_edge[in_ptr[row] .. in_ptr[row+1]) (edge ids 2i + side, ascending), added left to right, and
+ * the column sums move to the fp64 slots after every row: the adjoint rows are bitwise the same
+ * every run.  Other arguments as kb_level_backward. */
 int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl, const long long* sr,
                      const float* lsp, const int* dep0, const int* ready0, int n_ready0, const long long* child_ptr,
                      const int* child_idx, int* queue, int* remaining, unsigned* counters, long long max_polls,
@@ -429,7 +435,8 @@ int kb_flow_backward(int C, const long long* row_split_ptr, const long long* sl,
                      const float* sl2, const float* leaf_logp, const float* log_pD, const float* log_pS,
                      long long param_row_stride, long long const_row_stride, const float* col_log_probs,
                      int use_col_weights, const long long* item_idx, const int* leaf_state,
-                     const unsigned* packed_padded, const int* start_order, int S, void* stream);
+                     const unsigned* packed_padded, const int* start_order, float* edge_rows,
+                     const long long* in_ptr, const int* in_edge, int S, void* stream);
 
 /* Number of backward CTAs that are resident at once on this device for S columns (SMs x CTAs
  * per SM): the slot count to give kb_level_backward / kb_flow_backward (host only). */

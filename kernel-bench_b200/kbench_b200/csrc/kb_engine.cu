@@ -2057,6 +2057,14 @@ struct BwdArgs {
   int side_thr_enabled;
   int neumann_terms;
   int n_rows;
+  // Deterministic child adjoints (dataflow schedule; edge == null: atomic adds into acc).  Split i
+  // (row-order index) writes its two children's contributions to edge rows 2i and 2i+1 (zeros when
+  // its row is inactive); a row's adjoint is its seed acc[row] plus its incoming edge rows
+  // in_edge[in_ptr[row] .. in_ptr[row+1]) (ascending edge ids), added left to right -- the same sum
+  // in the same order whatever order the parents ran in.
+  float* edge;                  // [2N, S]
+  const long long* in_ptr;      // [C+1]
+  const int* in_edge;           // [2N]
 };
 
 // accumulator rows of the per-CTA column sums
@@ -2080,17 +2088,22 @@ __device__ __forceinline__ void l2_prefetch_row(const float* p, int n) {
 }
 
 // The child rows split i of the backward reads: the children's Pi rows (staged), Pibar rows (read
-// at the own columns) and adjoint rows (the targets of the split's atomic adds).  A backward row's
-// split phase otherwise meets each split's rows at the latency of HBM.
+// at the own columns) and adjoint rows (the targets of the split's atomic adds, when there are no
+// edge rows).  A backward row's split phase otherwise meets each split's rows at the latency of HBM.
 __device__ __forceinline__ void bwd_prefetch_split(const BwdArgs& a, long long i, int S) {
   const size_t l = (size_t)a.sp.sl[i] * S, r = (size_t)a.sp.sr[i] * S;
   l2_prefetch_row(a.Pi + l, S);
   l2_prefetch_row(a.Pi + r, S);
   l2_prefetch_row(a.Pibar + l, S);
   l2_prefetch_row(a.Pibar + r, S);
-  l2_prefetch_row(a.acc + l, S);
-  l2_prefetch_row(a.acc + r, S);
+  if (a.edge == nullptr) {
+    l2_prefetch_row(a.acc + l, S);
+    l2_prefetch_row(a.acc + r, S);
+  }
 }
+
+// A row's incoming edge rows travel to L2 ahead of its start (at most this many).
+#define KB_BWD_PREFETCH_EDGES 16
 
 // DF = the dataflow schedule (one persistent launch; f.par_ptr / par_idx then list each row's
 // distinct CHILD rows, released when the row is done; a row is ready once all its parents ran).
@@ -2172,12 +2185,57 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
       v[k] = s < S ? (DF ? __ldcg(rrow + s) : rrow[s]) : 0.f;  // DF: parents add with atomics (L2)
-      amax = fmaxf(amax, fabsf(v[k]));
     }
+    if (DF && a.edge) {  // the seed plus the incoming edge rows, left to right in edge order
+      const int lane = threadIdx.x & 31;
+      for (long long jb = a.in_ptr[row], je = a.in_ptr[row + 1]; jb < je; jb += 32) {
+        const int nb = je - jb < 32 ? (int)(je - jb) : 32;
+        const int mine = lane < nb ? __ldg(a.in_edge + jb + lane) : 0;  // a warp reads 32 ids at once
+        int jj = 0;
+        for (; jj + 4 <= nb; jj += 4) {  // four rows' loads in flight together
+          float x[4][VPT];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float* er = a.edge + (size_t)__shfl_sync(0xffffffffu, mine, jj + u) * S;
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+              const int s = threadIdx.x + k * NT;
+              x[u][k] = s < S ? __ldcg(er + s) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) v[k] += x[u][k];
+        }
+        for (; jj < nb; ++jj) {
+          const float* er = a.edge + (size_t)__shfl_sync(0xffffffffu, mine, jj) * S;
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            const int s = threadIdx.x + k * NT;
+            if (s < S) v[k] += __ldcg(er + s);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) amax = fmaxf(amax, fabsf(v[k]));
     // the block max compares above the threshold iff some thread's own max does: one barrier
     const bool active =
         __syncthreads_or(a.strict_gt ? (amax > a.threshold) : (amax >= a.threshold)) != 0;
     if (!active) {
+      if (DF && a.edge) {  // the children add this row's edge rows whatever it did: zeros
+        for (long long i = i0; i < i1; ++i) {
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            const int s = threadIdx.x + k * NT;
+            if (s < S) {
+              __stcg(a.edge + (size_t)(2 * i) * S + s, 0.f);
+              __stcg(a.edge + (size_t)(2 * i + 1) * S + s, 0.f);
+            }
+          }
+        }
+      }
       if (DF) flow_finish_row(f, (int)row, &fs);
       continue;
     }
@@ -2495,8 +2553,13 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
             const float tl = side_l ? wl[k] * (Al - (ue.x - ub.x)) : 0.f;
             const float trr = side_r ? wr[k] * (Ar - (ue.y - ub.y)) : 0.f;
             ACC[3 * NTV + x] += tl + trr;
-            atomicAdd(rl + x, cl[k] + stl + tl);
-            atomicAdd(rr + x, cr[k] + str + trr);
+            if (DF && a.edge) {
+              __stcg(a.edge + (size_t)(2 * i) * S + x, cl[k] + stl + tl);
+              __stcg(a.edge + (size_t)(2 * i + 1) * S + x, cr[k] + str + trr);
+            } else {
+              atomicAdd(rl + x, cl[k] + stl + tl);
+              atomicAdd(rr + x, cr[k] + str + trr);
+            }
           }
         }
       }
@@ -2513,11 +2576,20 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
           l2_prefetch_row(a.Pi + o, S);
           l2_prefetch_row(a.Pibar + o, S);
           if (a.dts_saved) l2_prefetch_row(a.dts_saved + o, S);
+          if (a.edge) {
+            const long long j0 = a.in_ptr[nr], j1 = a.in_ptr[nr + 1];
+            const long long je = j1 < j0 + KB_BWD_PREFETCH_EDGES ? j1 : j0 + KB_BWD_PREFETCH_EDGES;
+            for (long long j = j0; j < je; ++j) l2_prefetch_row(a.edge + (size_t)a.in_edge[j] * S, S);
+          }
         }
       }
       // A persistent CTA runs hundreds of rows: keep the fp32 partial sums short (as a level launch
-      // does) by moving them into the fp64 slot every few rows.  Own columns only: no barrier.
-      if (++since_flush == KB_FLOW_FLUSH_ROWS) {
+      // does) by moving them into the fp64 slot every few rows.  Own columns only: no barrier.  With
+      // the edge rows, after every row: which rows share a CTA varies run to run, so only a row's own
+      // fp32 sums (formed in a fixed order) may be grouped before the fp64 slot.
+      // The moves are fp64 reductions whose result nobody waits for (each address is this thread's
+      // own column: program order, deterministic per CTA), not load-add-store round trips.
+      if (++since_flush == (a.edge ? 1 : KB_FLOW_FLUSH_ROWS)) {
         since_flush = 0;
         double* slot = a.slots + (size_t)blockIdx.x * G_N * NTV;
 #pragma unroll
@@ -2525,7 +2597,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
           const int s = threadIdx.x + k * NT;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            slot[(size_t)(j == 3 ? G_COL : j) * NTV + s] += (double)ACC[j * NTV + s];
+            atomicAdd(slot + (size_t)(j == 3 ? G_COL : j) * NTV + s, (double)ACC[j * NTV + s]);
             ACC[j * NTV + s] = 0.f;
           }
         }
@@ -2765,7 +2837,7 @@ extern "C" int kb_level_backward(const int* rows, const long long* split_ptr, in
   if (S <= 0 || n_rows < 0 || neumann_terms < 0 || n_slots <= 0) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (n_rows == 0) return KB_OK;
-  BwdArgs a;
+  BwdArgs a{};  // value-initialised: the edge fields stay null unless set
   a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, nullptr, nullptr, nullptr, nullptr, log_pD, log_pS,
                 param_row_stride, const_row_stride, col_log_probs, use_col_weights, nullptr, nullptr, nullptr,
                 nullptr, nullptr, nullptr, nullptr, nullptr, 0, item_idx, leaf_state, packed_padded, S);
@@ -2979,15 +3051,17 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
                                 const float* sl1, const float* sl2, const float* leaf_logp, const float* log_pD,
                                 const float* log_pS, long long param_row_stride, long long const_row_stride,
                                 const float* col_log_probs, int use_col_weights, const long long* item_idx,
-                                const int* leaf_state, const unsigned* packed_padded, const int* start_order, int S,
+                                const int* leaf_state, const unsigned* packed_padded, const int* start_order,
+                                float* edge_rows, const long long* in_ptr, const int* in_edge, int S,
                                 void* stream) {
   if (S <= 0 || C < 0 || neumann_terms < 0 || n_slots <= 0 || n_ready0 < 0 || n_ready0 > C || max_polls < 1 ||
       counters == nullptr)
     return KB_ERR_ARG;
+  if (edge_rows && (!in_ptr || !in_edge)) return KB_ERR_ARG;
   if (S > KB_MAX_S) return KB_ERR_SIZE;
   if (C == 0) return KB_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  BwdArgs a;
+  BwdArgs a{};  // value-initialised: the edge fields stay null unless set
   a.c = make_lc(mc, dl, ebar, e, sl1, sl2, leaf_logp, nullptr, nullptr, nullptr, nullptr, log_pD, log_pS,
                 param_row_stride, const_row_stride, col_log_probs, use_col_weights, nullptr, nullptr, nullptr,
                 nullptr, nullptr, nullptr, nullptr, nullptr, 0, item_idx, leaf_state, packed_padded, S);
@@ -2996,6 +3070,7 @@ extern "C" int kb_flow_backward(int C, const long long* row_split_ptr, const lon
   a.v_out = v_out; a.slots = grad_slots; a.threshold = threshold; a.strict_gt = strict_gt;
   a.side_thr = side_threshold; a.side_thr_enabled = side_threshold_enabled; a.neumann_terms = neumann_terms;
   a.n_rows = C;
+  a.edge = edge_rows; a.in_ptr = in_ptr; a.in_edge = in_edge;
   Flow f{queue, remaining, counters, counters + 1, reinterpret_cast<int*>(counters + 2), child_ptr, child_idx,
          row_split_ptr, C, max_polls, C};
   f.static_order = start_order != nullptr;

@@ -24,7 +24,7 @@ __global__ void build_jumps_kernel(const int* __restrict__ parent, int S, int K,
 
 }  // namespace
 
-extern "C" int kb_abi_version(void) { return 3; }
+extern "C" int kb_abi_version(void) { return 4; }
 
 extern "C" int kb_build_jumps(const int* node_parent, int S, int K, int* jumps, void* stream) {
   if (S <= 0 || K < 0) return KB_ERR_ARG;

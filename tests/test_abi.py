@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     for name in _lib.parse_header():
         assert hasattr(handle, name), name
     lib = _lib.lib()
-    assert lib.kb_abi_version() == 3
+    assert lib.kb_abi_version() == 4
 
 
 def test_invalid_sizes_are_rejected_without_a_device():
