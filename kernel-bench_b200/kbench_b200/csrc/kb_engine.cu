@@ -2184,7 +2184,7 @@ __global__ void __launch_bounds__(1024 / (VPT >= 8 ? 2 : 1), 1) level_backward_k
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int s = threadIdx.x + k * NT;
-      v[k] = s < S ? (DF ? __ldcg(rrow + s) : rrow[s]) : 0.f;  // DF: parents add with atomics (L2)
+      v[k] = s < S ? (DF ? __ldcg(rrow + s) : rrow[s]) : 0.f;  // DF: L2 (the atomic form's parents add there)
     }
     if (DF && a.edge) {  // the seed plus the incoming edge rows, left to right in edge order
       const int lane = threadIdx.x & 31;

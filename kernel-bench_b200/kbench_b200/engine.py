@@ -507,19 +507,24 @@ def _edge_scratch(static, plan, C, S, dev):
     adds, 73.0 ms against 77.8 ms for the config-3 backward), or when the edge rows would exceed
     ``EDGE_ROWS_MAX_BYTES``.  Returns the edge rows ``[2N, S]`` (row 2i / 2i+1: split i's
     contribution to its left / right child) and the CSR of each row's incoming edges
-    (``in_ptr [C+1]``, ``in_edge [2N]`` ascending)."""
+    (``in_ptr [C+1]``, ``in_edge [2N]`` ascending).  If the edge rows cannot be allocated (a GPU
+    shared with other work), the static switches to the atomic form."""
     N = int(plan.n_splits)
     if not getattr(static, "_deterministic_backward", True) or N == 0 or 2 * N * S * 4 > EDGE_ROWS_MAX_BYTES:
         return None
     ed = getattr(static, "_edge_scratch", None)
     if ed is not None and ed["rows"].device == dev and tuple(ed["rows"].shape) == (2 * N, S):
         return ed
+    try:
+        rows = torch.empty((2 * N, S), device=dev, dtype=torch.float32)
+    except torch.cuda.OutOfMemoryError:  # a GPU shared with other work: keep the atomic form
+        static._deterministic_backward = False
+        return None
     child = torch.stack([plan.sl_r.to(dev), plan.sr_r.to(dev)], dim=1).reshape(-1)  # edge 2i + side
     order = torch.sort(child, stable=True).indices  # by child row, ascending edge id within a row
     in_ptr = torch.zeros((C + 1,), device=dev, dtype=torch.int64)
     in_ptr[1:] = torch.cumsum(torch.bincount(child, minlength=C), dim=0)
-    ed = {"rows": torch.empty((2 * N, S), device=dev, dtype=torch.float32), "in_ptr": in_ptr,
-          "in_edge": order.to(torch.int32)}
+    ed = {"rows": rows, "in_ptr": in_ptr, "in_edge": order.to(torch.int32)}
     static._edge_scratch = ed
     return ed
 

@@ -136,3 +136,29 @@ def test_list_schedule_bounds():
     for w in (2, 8, 32):
         s = span(w)
         assert max(cost.sum() / w, crit) - 1e-9 <= s <= cost.sum() / w + crit + 1e-9
+
+
+@pytest.mark.parametrize("config,seed", [(1, 1000), (2, 2000)])
+def test_backward_edge_csr_lists_every_split_side_once_in_order(config, seed):
+    """The deterministic backward's gather table: each row's incoming edges (edge 2i + side of split
+    i, in row-order split numbering) are exactly the split sides that name it as a child, in
+    ascending order, and the backward dependency counts (distinct parents) follow from them."""
+    import torch
+    cap = gen.generate(config, seed=seed)
+    static = runtime.make_static(cap, "cpu")
+    plan = engine.build_plan(static)
+    C, S = int(cap["meta"]["C"]), int(cap["meta"]["S"])
+    ed = engine._edge_scratch(static, plan, C, S, torch.device("cpu"))
+    assert ed is not None and tuple(ed["rows"].shape) == (2 * plan.n_splits, S)
+    ptr, edges = ed["in_ptr"].numpy(), ed["in_edge"].numpy().astype(np.int64)
+    assert ptr[0] == 0 and ptr[-1] == 2 * plan.n_splits and (np.diff(ptr) >= 0).all()
+    child = np.stack([plan.sl_r.numpy(), plan.sr_r.numpy()], axis=1).reshape(-1)
+    rsp = plan.row_split_ptr.numpy()
+    parent = np.repeat(np.arange(C), np.diff(rsp))
+    for r in range(C):
+        e = edges[ptr[r]:ptr[r + 1]]
+        assert (np.diff(e) > 0).all() and (child[e] == r).all()
+        assert len(set(parent[e // 2].tolist())) == int(plan.dep_b.numpy()[r])
+    assert np.array_equal(np.sort(edges), np.arange(2 * plan.n_splits))
+    static._deterministic_backward = False
+    assert engine._edge_scratch(static, plan, C, S, torch.device("cpu")) is None
