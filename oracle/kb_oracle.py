@@ -604,7 +604,8 @@ def gmres_fixed(apply_a, b, max_iter):
 
 def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, tree: Tree,
                   *, neumann_terms, leaf_state=None, leaf_logp=None, active=None,
-                  grad_col=None, use_col_weights=False, self_loop_solver="neumann", last_out=None):
+                  grad_col=None, use_col_weights=False, self_loop_solver="neumann", last_out=None,
+                  initial_v=None, grad_targets=None):
     """``wave_backward_uniform_fused`` (``experiments/pristine_kernels/wave_backward.py:
     1270-1736`` retained 2D path): precompute (``:203-417``), the self-loop adjoint -- Neumann
     ``v = sum_n (J^T)^n rhs`` (``:419-570``) or GMRES on ``(I - J^T) v = rhs`` over the wave's
@@ -612,15 +613,25 @@ def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, t
     (``:747-966``).  Returns (v_k, aw0, aw1, aw2, aw345, aw3, aw4); v_k rows of inactive rows are
     NaN in the Neumann solve (uninitialised in the reference), zero in the GMRES solve.
     ``last_out`` ([W], Neumann with at least one term) receives ``|last term| / |v|`` per row
-    (zero on inactive rows; ``:1275-1292``)."""
+    (zero on inactive rows; ``:1275-1292``).
+
+    ``initial_v`` ([W,S], Neumann only; ``:1190-1230``): ``v = initial_v``, then ``neumann_terms``
+    fixed-point updates ``v <- rhs + J^T v`` on the active rows (the JT kernel with
+    FIXED_POINT_UPDATE, ``:420-655``); inactive rows keep ``initial_v``; no last increment
+    (``:1275-1280``).  ``grad_targets`` = (grad_log_pD, grad_log_pS, grad_E, grad_Ebar, grad_E_s1,
+    grad_E_s2, grad_mt, param_grad_vector) (``:1294-1314`` and the ACCUM_GRADS branch of the
+    parameter store, ``:907-959``): the active rows' buckets are summed over rows and ADDED into
+    those arrays (pD += aw0 and pS += aw345 per column, or -- without param_grad_vector -- each row's
+    sum over columns; E += aw0 + aw2, Ebar += aw1, E_s1 += aw4, E_s2 += aw3, mt += aw2); the six
+    buckets are then returned as None."""
     S = tree.S
     act = np.ones(W, dtype=bool) if active is None else np.asarray(active, dtype=bool)
     rows_l = np.nonzero(act)[0]
     rows = ws + rows_l
-    v_k = np.full((W, S), np.nan, dtype=F32)
+    v_k = np.full((W, S), np.nan, dtype=F32) if initial_v is None else _f(initial_v).copy()
     aw = [np.zeros((W, S), dtype=F32) for _ in range(7)]
     if rows_l.size == 0:
-        return (v_k, aw[0], aw[1], aw[2], aw[3], aw[4], aw[5])
+        return (v_k, *((None,) * 6 if grad_targets is not None else (aw[0], aw[1], aw[2], aw[3], aw[4], aw[5])))
     ls = None if leaf_state is None else leaf_state[rows_l]
     dts_rows = None if dts_r is None else dts_r[rows_l]
     e, inv_sum, w_L = _self_loop_terms(Pi, Pibar, rows, consts, tree, ls, leaf_logp, dts_rows)
@@ -654,8 +665,14 @@ def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, t
         return (base + np.where(par_ok, term[:, par_safe], F32(0.0)) * edge).astype(F32)
 
     if str(self_loop_solver).strip().lower() == "gmres":
+        if initial_v is not None:
+            raise ValueError("GMRES self-loop solve does not support initial_v")
         v = gmres_fixed(lambda x: (x - jt(x)).astype(F32), rhs_a, int(neumann_terms))
         v_k[:] = F32(0.0)
+    elif initial_v is not None:
+        v = _f(initial_v)[rows_l].copy()
+        for _ in range(int(neumann_terms)):
+            v = (rhs_a + jt(v)).astype(F32)
     else:
         v = rhs_a.copy()
         term = rhs_a
@@ -683,6 +700,21 @@ def wave_backward(Pi, Pibar, row_max_all, ws, W, dts_r, rhs, consts, col_logp, t
     aw[3][rows_l] = (a[3] + a[4] + a[5]).astype(F32)
     aw[4][rows_l] = a[3]
     aw[5][rows_l] = a[4]
+    if grad_targets is not None:
+        g_pD, g_pS, g_E, g_Ebar, g_Es1, g_Es2, g_mt, vector = grad_targets
+        col = [x.sum(axis=0, dtype=F32) for x in aw[:6]]  # active rows only: the others are zero
+        if vector:
+            g_pD += col[0]
+            g_pS += col[3]
+        else:
+            g_pD += aw[0].sum(axis=1, dtype=F32).sum(dtype=F32)
+            g_pS += aw[3].sum(axis=1, dtype=F32).sum(dtype=F32)
+        g_E += (col[0] + col[2]).astype(F32)
+        g_Ebar += col[1]
+        g_Es1 += col[5]
+        g_Es2 += col[4]
+        g_mt += col[2]
+        return (v_k, None, None, None, None, None, None)
     return (v_k, aw[0], aw[1], aw[2], aw[3], aw[4], aw[5])
 
 

@@ -103,3 +103,48 @@ def test_wave_backward_option_errors(cuda):
                                                                    True)
     with pytest.raises(ValueError, match="self_loop_grad_targets"):
         wave_backward_uniform_fused(*args, **{**kw, "self_loop_grad_targets": bad})
+
+
+def test_oracle_options_match_reference_golden():
+    """The CPU oracle's warm start and gradient targets (``oracle/kb_oracle.py`` ``wave_backward``)
+    against the same pristine-kernel outputs, on the CPU."""
+    from oracle import kb_oracle as O
+    g = _golden()
+    a, kw = g["args"], g["kwargs"]
+    W, S, ws = g["W"], g["S"], int(a[2])
+    n = lambda t: t.detach().numpy()  # noqa: E731
+    tree = O.Tree({"S": S, "node_parent": n(kw["node_parent"]), "node_child1": n(a[14]), "node_child2": n(a[15]),
+                   "node_subtree_start": np.zeros(S), "node_subtree_end": np.zeros(S),
+                   "max_ancestor_depth": kw["max_ancestor_depth"], "unnorm_row_max": np.zeros(1),
+                   "compact_level_ptr": n(kw["compact_level_ptr"]),
+                   "compact_level_parents": n(kw["compact_level_parents"]),
+                   "compact_level_child1": n(kw["compact_level_child1"]),
+                   "compact_level_child2": n(kw["compact_level_child2"])})
+    assert a[5] is None and int(kw["item_idx"].abs().max()) == 0  # the leaf wave of one family
+    consts = {k: n(a[i]).reshape(S) for k, i in (("dl", 8), ("ebar", 9), ("e", 10), ("sl1", 11), ("sl2", 12))}
+    mask = n(kw["active_mask"]).astype(bool)
+    for case, rec in g["cases"].items():
+        ex = rec["extra"]
+        gc = n(g["kwargs"]["grad_col_log_probs"]).copy()
+        targets = None
+        if "self_loop_grad_targets" in ex:
+            vals, vec = ex["self_loop_grad_targets"]
+            targets = (*[n(v).copy() for v in vals], bool(vec))
+        out = O.wave_backward(n(a[0]), n(a[1]), n(kw["pibar_row_max"]), ws, W, None, n(a[6]), consts,
+                              n(a[13]), tree, neumann_terms=int(ex.get("neumann_terms", kw["neumann_terms"])),
+                              leaf_state=n(kw["leaf_state_idx"])[ws:ws + W].astype(np.int64),
+                              leaf_logp=n(kw["leaf_logp"]).reshape(S), active=mask, grad_col=gc,
+                              initial_v=None if "initial_v" not in ex else n(ex["initial_v"]),
+                              grad_targets=targets)
+        assert_close(f"{case} v_k", out[0][mask], n(rec["v_k"])[mask])
+        if "initial_v" in ex:
+            assert np.array_equal(out[0][~mask], n(ex["initial_v"])[~mask])
+        if rec["aw"] is None:
+            assert all(t is None for t in out[1:])
+        else:
+            for i, (got, want) in enumerate(zip(out[1:], rec["aw"])):
+                assert_close(f"{case} aw[{i}]", got, n(want))
+        assert_close_vec(f"{case} grad_col", gc, n(rec["grad_col_post"]))
+        if targets is not None:
+            for i, want in enumerate(rec["targets_post"]):
+                assert_close_vec(f"{case} target {i}", targets[i], n(want))
