@@ -59,13 +59,16 @@ def rows_of(t, G: int, S: int):
 def state_rows(t, S: int):
     """Parameter -> (contiguous [rows,S] tensor, row stride): one shared row -> stride 0.
 
-    Mirrors the addressing of ``dts_fused.py:11-16`` (``_load_rate``): [*, S] tensors are
-    state-indexed rows; [G], [G,1] and scalars are one value per item row, broadcast over S."""
-    if t.ndim == 2 and int(t.shape[1]) == S and int(t.shape[1]) != 1:
+    Mirrors the addressing of the forward split-reduction wrappers (``dts_fused.py:11-16``
+    ``_load_rate`` with ``:193-194``; ``dts_tangent.py:112-113``): a 2-D tensor whose second
+    dimension is not 1 ([1,S] or [G,S]) holds state-indexed rows; anything else -- [G], [G,1], a
+    scalar, and also a 1-D [S] tensor -- is one value per item row (the value at the item's index),
+    broadcast over S."""
+    if t.ndim == 2 and int(t.shape[1]) != 1:
+        if int(t.shape[1]) != S:
+            raise ValueError(f"state-indexed DTS parameters must have S = {S} columns, got {tuple(t.shape)}")
         t = f32(t)
         return t, (0 if int(t.shape[0]) == 1 else S)
-    if t.ndim == 1 and int(t.shape[0]) == S and S != 1:
-        return f32(t.reshape(1, S)), 0
     vals = f32(t.reshape(-1))
     g = int(vals.numel())
     full = vals.reshape(g, 1).expand(g, S).contiguous()

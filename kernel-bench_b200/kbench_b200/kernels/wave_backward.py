@@ -235,23 +235,42 @@ def _grad_targets(targets, S: int, device):
     return vals, vector
 
 
+def _dts_backward_layout(shape, S: int, item_indexed: bool):
+    """(row_stride, elem_stride) of a DTS backward parameter or gradient of ``shape``: the value of
+    item ``g`` at column ``s`` is at ``g * row_stride + s * elem_stride``; None for a layout the
+    reference rejects.  The precedence is the reference's layout contract
+    (``kbench/core/kernels/_dts_layout_contract.py:158-200``): one element is a shared scalar; with
+    item indexing any 1-D tensor is one value per item (before ``[S]`` is considered); ``[S]`` is
+    a shared state row; with item indexing ``[G, 1]`` is one value per item and ``[G, S]`` one row
+    per item (one shared row when G = 1)."""
+    shape = tuple(int(d) for d in shape)
+    n = 1
+    for d in shape:
+        n *= d
+    if n == 1:
+        return 0, 0
+    if item_indexed and len(shape) == 1:
+        return 1, 0
+    if len(shape) == 1 and shape[0] == S:
+        return 0, 1
+    if item_indexed and len(shape) == 2 and shape[1] == 1:
+        return 1, 0
+    if item_indexed and len(shape) == 2 and shape[1] == S:
+        return (0 if shape[0] == 1 else S), 1
+    return None
+
+
 def _param_ref(param, *, S, item_indexed, device):
     """(tensor, row_stride, elem_stride) for the DTS backward parameter layouts
-    (reference ``wave_backward.py:36-86``: scalar, [S], [G]/[G,1], [G,S])."""
+    (reference ``wave_backward.py:103-163``: scalar, [S], [G]/[G,1], [G,S], classified by
+    :func:`_dts_backward_layout`)."""
     if not torch.is_tensor(param):
         return torch.tensor([float(param)], device=device, dtype=torch.float32), 0, 0
-    p = f32(param.to(device))
-    if p.numel() == 1:
-        return p.reshape(1), 0, 0
-    if p.ndim == 2 and int(p.shape[1]) == S and S != 1:
-        return p, (0 if int(p.shape[0]) == 1 else S), 1
-    if p.ndim == 1 and item_indexed:
-        return p, 1, 0  # item scalar rows
-    if p.ndim == 1 and int(p.shape[0]) == S:
-        return p, 0, 1
-    if p.ndim == 2 and int(p.shape[1]) == 1:
-        return p.reshape(-1), 1, 0
-    raise ValueError("DTS parameters must be scalar, [S], [G], [G, 1], or [G, S] for the fused DTS backward path")
+    lay = _dts_backward_layout(param.shape, S, item_indexed)
+    if lay is None:
+        raise ValueError("DTS parameters must be scalar, [S], [G], [G, 1], or [G, S] for the fused DTS backward path")
+    p = f32(param.to(device)).reshape(-1)
+    return p, lay[0], lay[1]
 
 
 def dts_cross_backward_accum_fused(Pi_star, Pibar_star, v_k, ws, sl, sr, reduce_idx, wlsp, log_pD, log_pS,
@@ -294,19 +313,15 @@ def dts_cross_backward_accum_fused(Pi_star, Pibar_star, v_k, ws, sl, sr, reduce_
     thr_enabled = bool(output_pibar_side_active and (torch.is_tensor(pibar_side_threshold) or thr > 0.0))
     # gradient addressing
     if accum_param_reductions:
+        lays = []
         for g in (grad_log_pD, grad_log_pS):
-            if g.dtype != dt or not g.is_contiguous():
+            lay = _dts_backward_layout(g.shape, S, item_indexed)
+            if g.dtype != dt or not g.is_contiguous() or lay is None:
                 raise ValueError("unsupported DTS gradient layout")
-        if grad_log_pD.numel() == 1:
-            gp_rs, gp_es = 0, 0
-        elif grad_log_pD.ndim == 2 and int(grad_log_pD.shape[1]) == S and S != 1:
-            gp_rs, gp_es = (0 if int(grad_log_pD.shape[0]) == 1 else S), 1
-        elif grad_log_pD.ndim == 1 and item_indexed:
-            gp_rs, gp_es = 1, 0
-        elif grad_log_pD.ndim == 1 and int(grad_log_pD.shape[0]) == S:
-            gp_rs, gp_es = 0, 1
-        else:
-            gp_rs, gp_es = 1, 0
+            lays.append(lay)
+        if lays[0] != lays[1]:
+            raise ValueError("unsupported DTS gradient layout")
+        gp_rs, gp_es = lays[0]
     else:
         gp_rs, gp_es = 0, 0
     if accum_mt_reduction:
