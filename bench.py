@@ -15,10 +15,14 @@ one NCCL all-reduce per step -- the family-sharded data-parallel step; per-GPU w
 ``e2e`` is the same step through the public API with theta/col_weights copied from pinned host
 memory and the loss + gradients copied back every step.
 
-``--impl reference`` times the reference algorithm's CPU restatement (the numpy oracle under
-``oracle/``) on a bounded sample of the same workload (a family with the same species tree and
-fewer rows), extrapolated per row, on every host thread (one single-threaded process per thread,
-all passes started together); on N>1 only rank 0 runs it.
+``--impl reference`` times the reference's own implementation on the host cores: its runtime and
+kernels under the Triton interpreter, on a bounded sample of the same workload (a family with the
+same species tree and fewer rows), extrapolated per row (the line states the formula), one
+single-threaded process per host thread, all started together; the numpy port of the same
+algorithm (``oracle/``) is reported beside it.  On N>1 only rank 0 runs it.
+
+``--atomic-backward`` runs the headline backward with atomic child adds instead of its default
+deterministic form (child adjoints gathered from edge rows in a fixed order).
 
 ``--config 4`` measures the batched workload instead: 1024 families (S=1023, ~16k rows each)
 sharing one theta, split into contiguous blocks per rank, each block processed in chunks of
