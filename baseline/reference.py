@@ -14,8 +14,8 @@ Two uses:
   stock Triton kernels -- for timing the reference's Triton path on the same GPU and comparing
   results with it (``bench.py``, ``tests/test_gpu_reference_triton.py``);
 * :func:`checkout_copy` lays out a scratch copy of the reference checkout (package + ``bench/``)
-  whose kernel modules re-export this project's wrappers -- the drop-in recipe of INTEGRATION.md,
-  applied to a copy -- so the reference's unchanged glue, runtime and ``bench/check.py`` run on the
+  whose kernel modules re-export this project's wrappers -- the drop-in recipe, applied to a
+  copy -- so the reference's unchanged glue, runtime and ``bench/check.py`` run on the
   sm_100a kernels (``tests/test_gpu_reference_gate.py``).
 """
 
@@ -31,7 +31,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent.parent
 REF = ROOT / "baseline" / "_ref"
 
-# kbench/core/kernels/<module>.py -> the re-export that replaces it (INTEGRATION.md's table)
+# kbench/core/kernels/<module>.py -> the re-export that replaces it (the drop-in recipe)
 SHIMS = {
     "wave_step": "from kbench_b200.kernels.wave_step import compute_wave_step, compute_leaf_initial_wave_step",
     "dts_fused": "from kbench_b200.kernels.dts_fused import compute_dts_forward",

@@ -1,7 +1,7 @@
 """The reference's own correctness gate, unchanged, on this project's kernels.
 
 A scratch copy of the reference checkout is laid out whose ``kbench/core/kernels/*.py`` re-export
-this project's wrappers (the drop-in recipe of INTEGRATION.md), with golden captures made by the
+this project's wrappers (the drop-in recipe: each kernel module re-exports ours), with golden captures made by the
 reference's own ``capture/capture.py`` from its pristine kernels (``tests/golden/make_capture.py``:
 a config-1 problem with 19 per-wrapper snapshots, the adjoint-options problem and a
 weighted-column problem).  Then the reference's ``bench/check.py`` runs as shipped:
